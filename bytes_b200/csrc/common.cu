@@ -1,0 +1,112 @@
+// Host-side helpers shared by every entry point: error reporting and descriptor checks.
+#include "common.cuh"
+
+#include <mutex>
+
+namespace bd {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int status, const std::string& msg) {
+  g_last_error = std::string(bd_status_name(status)) + ": " + msg;
+  return status;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return BD_OK;
+  return fail(BD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int num_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (sms[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = v > 0 ? v : 148;
+  }
+  return sms[dev];
+}
+
+const char* dtype_name(int dt) {
+  switch (dt) {
+    case BD_F32: return "f32";
+    case BD_F16: return "f16";
+    case BD_BF16: return "bf16";
+    case BD_F8E4M3: return "f8e4m3";
+    case BD_U8: return "u8";
+    case BD_I8: return "i8";
+    case BD_I32: return "i32";
+    case BD_I64: return "i64";
+  }
+  return "?";
+}
+
+std::string shape_str(const bd_tensor* t) {
+  std::string s = "[";
+  for (int i = 0; i < t->ndim; ++i) {
+    s += std::to_string(t->shape[i]);
+    if (i + 1 < t->ndim) s += ",";
+  }
+  return s + "]";
+}
+
+int check_tensor(const bd_tensor* t, const char* name, int ndim, int dtype) {
+  if (!t) return fail(BD_ERR_NULL, std::string(name) + " descriptor is NULL");
+  if (t->ndim != ndim)
+    return fail(BD_ERR_SHAPE, std::string(name) + " must have " + std::to_string(ndim) +
+                                  " dims, got " + std::to_string(t->ndim));
+  if (dtype >= 0 && t->dtype != dtype)
+    return fail(BD_ERR_DTYPE, std::string(name) + " must be " + dtype_name(dtype) + ", got " +
+                                  dtype_name(t->dtype));
+  int64_t numel = 1;
+  for (int i = 0; i < ndim; ++i) {
+    if (t->shape[i] < 0) return fail(BD_ERR_SHAPE, std::string(name) + " has a negative dim");
+    numel *= t->shape[i];
+  }
+  if (numel > 0 && !t->data) return fail(BD_ERR_NULL, std::string(name) + " data pointer is NULL");
+  return BD_OK;
+}
+
+int check_rows_aligned(const bd_tensor* t, const char* name, size_t align) {
+  const size_t es = dtype_size(t->dtype);
+  if (t->ndim > 0 && t->shape[t->ndim - 1] > 1 && t->stride[t->ndim - 1] != 1)
+    return fail(BD_ERR_STRIDE, std::string(name) + " innermost dim must be contiguous");
+  if (reinterpret_cast<uintptr_t>(t->data) % align)
+    return fail(BD_ERR_ALIGN, std::string(name) + " base pointer not " + std::to_string(align) + "-byte aligned");
+  for (int i = 0; i + 1 < t->ndim; ++i)
+    if (t->shape[i] > 1 && (size_t(t->stride[i]) * es) % align)
+      return fail(BD_ERR_ALIGN, std::string(name) + " stride of dim " + std::to_string(i) +
+                                    " is not a multiple of " + std::to_string(align) + " bytes");
+  return BD_OK;
+}
+
+}  // namespace bd
+
+extern "C" {
+
+int bd_abi_version(void) { return 1; }
+
+const char* bd_status_name(int s) {
+  switch (s) {
+    case BD_OK: return "BD_OK";
+    case BD_ERR_NULL: return "BD_ERR_NULL";
+    case BD_ERR_DTYPE: return "BD_ERR_DTYPE";
+    case BD_ERR_SHAPE: return "BD_ERR_SHAPE";
+    case BD_ERR_STRIDE: return "BD_ERR_STRIDE";
+    case BD_ERR_ALIGN: return "BD_ERR_ALIGN";
+    case BD_ERR_WORKSPACE: return "BD_ERR_WORKSPACE";
+    case BD_ERR_UNSUPPORTED: return "BD_ERR_UNSUPPORTED";
+    case BD_ERR_CUDA: return "BD_ERR_CUDA";
+    case BD_ERR_VALUE: return "BD_ERR_VALUE";
+  }
+  return "BD_ERR_UNKNOWN";
+}
+
+const char* bd_last_error(void) { return bd::g_last_error.c_str(); }
+
+}  // extern "C"

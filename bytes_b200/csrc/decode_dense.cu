@@ -1,0 +1,668 @@
+// Dense GQA decode attention over a bf16 or fp8-e4m3 KV cache (split-KV flash-decoding).
+//
+// Follows decode_attn_bf16 / decode_attn_fp8 (src/attention_kernels.py:8-182 of the
+// reference): per query head, softmax(scaling * q.k) . v with fp32 accumulation.
+//
+// Design (one CTA = one (batch, KV head, query-head chunk, key split)):
+//  * 4 consumer warps; a 64-token tile is split into 16-token row blocks, one per warp.
+//  * K/V tiles stream HBM -> shared memory through a 3-stage cp.async pipeline; the rows
+//    land with a 16-byte pad so ldmatrix reads are bank-conflict free.
+//  * The GQA group makes QK^T a dense contraction: S^T[16 tokens x 8 heads] =
+//    K[16 x D] . Q^T[D x 8] on the tensor cores (mma.sync m16n8k16, bf16 or f16 in,
+//    fp32 accumulate). Every K/V byte is read from HBM once per KV head, not G times.
+//  * Online softmax in exp2 space on the accumulator fragments; P is transposed in
+//    registers (movmatrix) into the B operand of O^T[D x 8] += V^T[D x 16] . P^T[16 x 8].
+//  * Warps merge through shared memory; splits merge in a log-sum-exp combine kernel.
+// fp8 keys/values are widened to f16 (exact) in registers; the query is fed as f16,
+// pre-scaled by a power of two when its magnitude would exceed the f16 range.
+#include "common.cuh"
+#include "decode_shared.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace bd {
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kRows = 16 * kWarps;  // tokens per tile
+constexpr int kStages = 3;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct DenseParams {
+  const void* q; int64_t q_sb, q_sh; int q_dtype;
+  const uint8_t* k; int64_t k_sb, k_sh, k_ss;  // strides in elements
+  const uint8_t* v; int64_t v_sb, v_sh, v_ss;
+  int B, Hq, Hk, G, S;
+  int head_chunks, heads_per_chunk;
+  int tiles_per_split, n_splits;
+  int split_offset, split_stride;  // partial index = (b*Hq+hq)*split_stride + split_offset + split
+  float scale_log2;
+  // split partials: index ((b*Hq + hq) * n_splits + split)
+  float* part_m; float* part_l; float* part_o;
+  // direct output when n_splits == 1 and final
+  void* out; int out_dtype; int64_t o_sb, o_sh;
+  int direct;
+};
+
+template <typename T>
+__device__ __forceinline__ float ldq(const void* base, int64_t off) {
+  return to_f32<T>(reinterpret_cast<const T*>(base)[off]);
+}
+
+__device__ __forceinline__ float load_q(const DenseParams& p, int64_t off) {
+  switch (p.q_dtype) {
+    case BD_BF16: return ldq<__nv_bfloat16>(p.q, off);
+    case BD_F16: return ldq<__half>(p.q, off);
+    default: return ldq<float>(p.q, off);
+  }
+}
+
+__device__ __forceinline__ void store_out(void* base, int dt, int64_t off, float x) {
+  switch (dt) {
+    case BD_BF16: reinterpret_cast<__nv_bfloat16*>(base)[off] = __float2bfloat16_rn(x); break;
+    case BD_F16: reinterpret_cast<__half*>(base)[off] = __float2half_rn(x); break;
+    default: reinterpret_cast<float*>(base)[off] = x; break;
+  }
+}
+
+template <int D, int NT, bool FP8>
+__global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const DenseParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int ELT = FP8 ? 1 : 2;
+  constexpr int ROWB = D * ELT;
+  constexpr int PITCH = ROWB + 16;
+  constexpr int TILEB = kRows * PITCH;
+  constexpr int CHUNKS = ROWB / 16;
+  constexpr int KSTEPS = D / 16;
+  constexpr int NH = 8 * NT;  // heads per CTA (padded)
+
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y / p.head_chunks;
+  const int chunk = blockIdx.y % p.head_chunks;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+
+  const int t_begin = split * p.tiles_per_split * kRows;
+  const int t_end = min(p.S, t_begin + p.tiles_per_split * kRows);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + kRows - 1) / kRows : 0;
+  const int h0 = chunk * p.heads_per_chunk;  // first local head of this chunk
+  const int nheads = min(p.heads_per_chunk, p.G - h0);
+
+  const uint8_t* kbase = p.k + (int64_t(b) * p.k_sb + int64_t(hk) * p.k_sh) * ELT;
+  const uint8_t* vbase = p.v + (int64_t(b) * p.v_sb + int64_t(hk) * p.v_sh) * ELT;
+
+  // ---- query fragments (B operand of QK^T), kept in registers for the whole split
+  uint32_t qb[KSTEPS][NT][2];
+  float score_mul = p.scale_log2;
+  {
+    float qv[KSTEPS][NT][4];
+    float amax = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int hl = nt * 8 + g;
+        const bool ok = hl < nheads;
+        const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? hl : 0)) * p.q_sh;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // bf16 path: natural channel order (2tq, 2tq+1, 2tq+8, 2tq+9);
+          // fp8 path: the ldmatrix byte layout gives channels 4tq..4tq+3 per k-step.
+          const int c = FP8 ? kk * 16 + 4 * tq + e : kk * 16 + 2 * tq + (e & 1) + (e >> 1) * 8;
+          qv[kk][nt][e] = ok ? load_q(p, qoff + c) : 0.f;
+          amax = fmaxf(amax, fabsf(qv[kk][nt][e]));
+        }
+      }
+    float qscale = 1.f;
+    if (FP8) {
+      amax = warp_max(amax);
+      // keep |q| below 2^15 in f16; power-of-two scaling is exact
+      int ex = 0;
+      frexpf(amax, &ex);
+      const int shift = ex > 15 ? ex - 15 : 0;
+      qscale = ldexpf(1.f, -shift);
+      score_mul = ldexpf(p.scale_log2, shift);
+    }
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (FP8) {
+          qb[kk][nt][0] = pack_f16x2(qv[kk][nt][0] * qscale, qv[kk][nt][1] * qscale);
+          qb[kk][nt][1] = pack_f16x2(qv[kk][nt][2] * qscale, qv[kk][nt][3] * qscale);
+        } else {
+          qb[kk][nt][0] = pack_bf16x2(qv[kk][nt][0], qv[kk][nt][1]);
+          qb[kk][nt][1] = pack_bf16x2(qv[kk][nt][2], qv[kk][nt][3]);
+        }
+      }
+  }
+
+  auto load_tile = [&](int tile, int stage) {
+    const int t0 = t_begin + tile * kRows;
+    const uint32_t ks = smem_u32(smem + stage * 2 * TILEB);
+    const uint32_t vs = ks + TILEB;
+    for (int c = threadIdx.x; c < kRows * CHUNKS; c += kWarps * 32) {
+      const int r = c / CHUNKS, cc = c % CHUNKS;
+      const int t = t0 + r;
+      const bool ok = t < t_end;
+      const int tt = ok ? t : t_begin;
+      cp_async16(ks + r * PITCH + cc * 16, kbase + int64_t(tt) * p.k_ss * ELT + cc * 16, ok ? 16 : 0);
+      cp_async16(vs + r * PITCH + cc * 16, vbase + int64_t(tt) * p.v_ss * ELT + cc * 16, ok ? 16 : 0);
+    }
+  };
+
+  float o[KSTEPS][NT][4];
+  float mrow[NT][2], lrow[NT][2];
+#pragma unroll
+  for (int mt = 0; mt < KSTEPS; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    mrow[nt][0] = mrow[nt][1] = -INFINITY;
+    lrow[nt][0] = lrow[nt][1] = 0.f;
+  }
+
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < ntiles) load_tile(s, s);
+    cp_async_commit();
+  }
+
+  const int r0 = warp * 16;
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();
+    {
+      const int nxt = it + kStages - 1;
+      if (nxt < ntiles) load_tile(nxt, nxt % kStages);
+      cp_async_commit();
+    }
+    const int stage = it % kStages;
+    const uint32_t ks = smem_u32(smem + stage * 2 * TILEB);
+    const uint32_t vs = ks + TILEB;
+    const int t0 = t_begin + it * kRows + r0;
+    if (t0 >= t_end) continue;  // this warp's rows are past the end (uniform per warp)
+
+    // ---- S^T = K . Q^T
+    float s[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    const int arow = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    if (!FP8) {
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(a0, a1, a2, a3, ks + arow * PITCH + (kk * 16 + (lane >> 4) * 8) * 2);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16(s[nt], a0, a1, a2, a3, qb[kk][nt][0], qb[kk][nt][1]);
+      }
+    } else {
+#pragma unroll
+      for (int k2 = 0; k2 < KSTEPS / 2; ++k2) {
+        uint32_t r0_, r1_, r2_, r3_;
+        ldmatrix_x4(r0_, r1_, r2_, r3_, ks + arow * PITCH + k2 * 32 + (lane >> 4) * 16);
+        const uint32_t x0 = e4m3x2_to_f16x2(r0_), x1 = e4m3x2_to_f16x2(r1_);
+        const uint32_t x2 = e4m3x2_to_f16x2(r0_ >> 16), x3 = e4m3x2_to_f16x2(r1_ >> 16);
+        const uint32_t y0 = e4m3x2_to_f16x2(r2_), y1 = e4m3x2_to_f16x2(r3_);
+        const uint32_t y2 = e4m3x2_to_f16x2(r2_ >> 16), y3 = e4m3x2_to_f16x2(r3_ >> 16);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_f16(s[nt], x0, x1, x2, x3, qb[2 * k2][nt][0], qb[2 * k2][nt][1]);
+          mma_f16(s[nt], y0, y1, y2, y3, qb[2 * k2 + 1][nt][0], qb[2 * k2 + 1][nt][1]);
+        }
+      }
+    }
+
+    // ---- mask, online softmax (exp2 domain), P fragments
+    const bool v0 = t0 + g < t_end, v1 = t0 + g + 8 < t_end;
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float pv[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float a = v0 ? s[nt][j] * score_mul : -INFINITY;
+        const float c = v1 ? s[nt][2 + j] * score_mul : -INFINITY;
+        float mx = fmaxf(a, c);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mnew = fmaxf(mrow[nt][j], mx);
+        const float muse = mnew == -INFINITY ? 0.f : mnew;
+        const float alpha = exp2f(mrow[nt][j] - muse);
+        pv[j] = exp2f(a - muse);
+        pv[2 + j] = exp2f(c - muse);
+        lrow[nt][j] = lrow[nt][j] * alpha + pv[j] + pv[2 + j];
+        mrow[nt][j] = mnew;
+#pragma unroll
+        for (int mt = 0; mt < KSTEPS; ++mt) {
+          o[mt][nt][j] *= alpha;
+          o[mt][nt][2 + j] *= alpha;
+        }
+      }
+      if (FP8) {
+        pb[nt][0] = movmatrix_trans(pack_f16x2(pv[0], pv[1]));
+        pb[nt][1] = movmatrix_trans(pack_f16x2(pv[2], pv[3]));
+      } else {
+        pb[nt][0] = movmatrix_trans(pack_bf16x2(pv[0], pv[1]));
+        pb[nt][1] = movmatrix_trans(pack_bf16x2(pv[2], pv[3]));
+      }
+    }
+
+    // ---- O^T += V^T . P^T
+    if (!FP8) {
+      const int vrow = r0 + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+      for (int mt = 0; mt < KSTEPS; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(a0, a1, a2, a3, vs + vrow * PITCH + (mt * 16 + ((lane >> 3) & 1) * 8) * 2);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+      }
+    } else {
+      const int vrow = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int m2 = 0; m2 < KSTEPS / 2; ++m2) {
+        uint32_t r0_, r1_, r2_, r3_;
+        ldmatrix_x4_trans(r0_, r1_, r2_, r3_, vs + vrow * PITCH + m2 * 32 + (lane >> 4) * 16);
+        // r0: tokens 0-7, r1: tokens 8-15 of channel block [32*m2, +16); r2/r3: block +16.
+        // Each holds (tok 2tq: ch 2g,2g+1 | tok 2tq+1: ch 2g,2g+1) as bytes 0..3.
+        const uint32_t a0 = e4m3x2_to_f16x2(prmt(r0_, 0, 0x0020)), a1 = e4m3x2_to_f16x2(prmt(r0_, 0, 0x0031));
+        const uint32_t a2 = e4m3x2_to_f16x2(prmt(r1_, 0, 0x0020)), a3 = e4m3x2_to_f16x2(prmt(r1_, 0, 0x0031));
+        const uint32_t c0 = e4m3x2_to_f16x2(prmt(r2_, 0, 0x0020)), c1 = e4m3x2_to_f16x2(prmt(r2_, 0, 0x0031));
+        const uint32_t c2 = e4m3x2_to_f16x2(prmt(r3_, 0, 0x0020)), c3 = e4m3x2_to_f16x2(prmt(r3_, 0, 0x0031));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_f16(o[2 * m2][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          mma_f16(o[2 * m2 + 1][nt], c0, c1, c2, c3, pb[nt][0], pb[nt][1]);
+        }
+      }
+    }
+  }
+
+  // ---- merge the warps: sum l over rows, then rescale to the CTA-wide max
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float l = lrow[nt][j];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      lrow[nt][j] = l;
+    }
+  cp_async_wait<0>();
+  __syncthreads();
+  float* red_m = reinterpret_cast<float*>(smem);   // [warps][NH]
+  float* red_l = red_m + kWarps * NH;              // [warps][NH]
+  float* red_o = red_l + kWarps * NH;              // [warps][NH][D]
+  if (g == 0) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        red_m[warp * NH + nt * 8 + 2 * tq + j] = mrow[nt][j];
+        red_l[warp * NH + nt * 8 + 2 * tq + j] = lrow[nt][j];
+      }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int h = nt * 8 + 2 * tq + j;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, red_m[w * NH + h]);
+      const float f = (M == -INFINITY) ? 0.f : exp2f(mrow[nt][j] - M);
+#pragma unroll
+      for (int mt = 0; mt < KSTEPS; ++mt) {
+        const int ca = FP8 ? mt * 16 + 2 * g : mt * 16 + g;
+        const int cb = FP8 ? ca + 1 : ca + 8;
+        red_o[(warp * NH + h) * D + ca] = o[mt][nt][j] * f;
+        red_o[(warp * NH + h) * D + cb] = o[mt][nt][2 + j] * f;
+      }
+    }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nheads * D; idx += kWarps * 32) {
+    const int h = idx / D, c = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, red_m[w * NH + h]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = (M == -INFINITY) ? 0.f : exp2f(red_m[w * NH + h] - M);
+      L += red_l[w * NH + h] * f;
+      O += red_o[(w * NH + h) * D + c];
+    }
+    const int hq = hk * p.G + h0 + h;
+    if (p.direct) {
+      store_out(p.out, p.out_dtype, int64_t(b) * p.o_sb + int64_t(hq) * p.o_sh + c, O / L);
+    } else {
+      const int64_t pi = (int64_t(b) * p.Hq + hq) * p.split_stride + p.split_offset + split;
+      p.part_o[pi * D + c] = O;
+      if (c == 0) {
+        p.part_m[pi] = M * kLn2;  // natural-log units of scaling*q.k
+        p.part_l[pi] = L;
+      }
+    }
+  }
+}
+
+// Merge per-split partials. mode 0: final output O/L; mode 1: export (m, l, O) per (b,hq).
+struct CombineParams {
+  const float* m; const float* l; const float* o;  // [rows][n] and [rows][n][D]
+  int rows, n, D, Hq;
+  int64_t m_s0, o_s0;   // stride between the n partial sets (elements); contiguous rows inside
+  void* out; int out_dtype; int64_t o_sb, o_sh;
+  float* em; float* el; float* eo;  // export targets [rows], [rows], [rows][D]
+  int mode;
+  int ms_rows;          // 1: partials laid out [rows][n]; 0: [n][rows]
+};
+
+__global__ void lse_combine_kernel(const CombineParams p) {
+  extern __shared__ float wsm[];  // [n] weights
+  const int row = blockIdx.x;
+  __shared__ float sM, sL;
+  auto midx = [&](int i) -> int64_t { return p.ms_rows ? int64_t(row) * p.n + i : int64_t(i) * p.m_s0 + row; };
+  if (threadIdx.x < 32) {
+    float M = -INFINITY;
+    for (int i = threadIdx.x; i < p.n; i += 32) M = fmaxf(M, p.m[midx(i)]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int i = threadIdx.x; i < p.n; i += 32) {
+      const float w = (M == -INFINITY) ? 0.f : __expf(p.m[midx(i)] - M);
+      wsm[i] = w;
+      L += p.l[midx(i)] * w;
+    }
+    L = warp_sum(L);
+    if (threadIdx.x == 0) { sM = M; sL = L; }
+  }
+  __syncthreads();
+  const int b = row / p.Hq, h = row % p.Hq;
+  for (int c = threadIdx.x; c < p.D; c += blockDim.x) {
+    float O = 0.f;
+    for (int i = 0; i < p.n; ++i) {
+      const int64_t oi = p.ms_rows ? (int64_t(row) * p.n + i) * p.D + c : int64_t(i) * p.o_s0 + int64_t(row) * p.D + c;
+      O += p.o[oi] * wsm[i];
+    }
+    if (p.mode == 0) {
+      store_out(p.out, p.out_dtype, int64_t(b) * p.o_sb + int64_t(h) * p.o_sh + c, O / sL);
+    } else {
+      p.eo[int64_t(row) * p.D + c] = O;
+      if (c == 0) { p.em[row] = sM; p.el[row] = sL; }
+    }
+  }
+}
+
+struct Plan {
+  int D, NT, head_chunks, heads_per_chunk, n_splits, tiles_per_split;
+  bool fp8;
+};
+
+int make_plan(const bd_tensor* q, const bd_tensor* k, Plan* pl, int target_ctas = 0) {
+  const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
+  const int64_t Hk = k->shape[1], S = k->shape[2];
+  if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
+  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128, got " + std::to_string(D));
+  const int G = int(Hq / Hk);
+  pl->D = int(D);
+  pl->fp8 = k->dtype == BD_F8E4M3;
+  pl->NT = G <= 8 ? 1 : 2;
+  pl->heads_per_chunk = 8 * pl->NT;
+  pl->head_chunks = (G + pl->heads_per_chunk - 1) / pl->heads_per_chunk;
+  const int64_t ntiles = (S + kRows - 1) / kRows;
+  const int64_t pairs = B * Hk * pl->head_chunks;
+  const int64_t slots = target_ctas > 0 ? target_ctas : 2LL * num_sms();
+  int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
+  int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;
+  splits = ntiles > 0 ? (ntiles + tps - 1) / tps : 1;
+  pl->n_splits = int(splits);
+  pl->tiles_per_split = int(tps);
+  return BD_OK;
+}
+
+size_t ws_bytes(const bd_tensor* q, const Plan& pl) {
+  const size_t rows = size_t(q->shape[0]) * size_t(q->shape[1]);
+  return rows * size_t(pl.n_splits) * (size_t(pl.D) + 2) * sizeof(float) + 256;
+}
+
+template <int D, int NT, bool FP8>
+int launch_dense(const DenseParams& p, const Plan& pl, cudaStream_t st) {
+  constexpr int ELT = FP8 ? 1 : 2;
+  constexpr int PITCH = D * ELT + 16;
+  size_t smem = size_t(kStages) * 2 * kRows * PITCH;
+  const size_t red = (2 * kWarps * 8 * NT + size_t(kWarps) * 8 * NT * D) * sizeof(float);
+  smem = std::max(smem, red);
+  auto kern = dense_decode_kernel<D, NT, FP8>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                        "cudaFuncSetAttribute");
+    if (rc) return rc;
+    attr_set[dev & 63] = true;
+  }
+  dim3 grid(pl.n_splits, p.Hk * pl.head_chunks, p.B);
+  kern<<<grid, kWarps * 32, smem, st>>>(p);
+  return cuda_check(cudaGetLastError(), "dense_decode_kernel launch");
+}
+
+int dispatch_dense(const DenseParams& p, const Plan& pl, cudaStream_t st) {
+  if (pl.D == 128) {
+    if (pl.fp8) return pl.NT == 1 ? launch_dense<128, 1, true>(p, pl, st) : launch_dense<128, 2, true>(p, pl, st);
+    return pl.NT == 1 ? launch_dense<128, 1, false>(p, pl, st) : launch_dense<128, 2, false>(p, pl, st);
+  }
+  if (pl.fp8) return pl.NT == 1 ? launch_dense<64, 1, true>(p, pl, st) : launch_dense<64, 2, true>(p, pl, st);
+  return pl.NT == 1 ? launch_dense<64, 1, false>(p, pl, st) : launch_dense<64, 2, false>(p, pl, st);
+}
+
+int validate(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v) {
+  int rc;
+  if ((rc = check_tensor(q, "q", 3))) return rc;
+  if ((rc = check_tensor(k, "k", 4))) return rc;
+  if ((rc = check_tensor(v, "v", 4))) return rc;
+  if (q->dtype != BD_BF16 && q->dtype != BD_F16 && q->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "q must be bf16, f16 or f32");
+  if (k->dtype != v->dtype || (k->dtype != BD_BF16 && k->dtype != BD_F8E4M3))
+    return fail(BD_ERR_DTYPE, "k and v must both be bf16 or both fp8 e4m3");
+  if (k->dtype == BD_BF16 && q->dtype != BD_BF16)
+    return fail(BD_ERR_DTYPE, "a bf16 KV cache needs a bf16 query");
+  for (int i = 0; i < 4; ++i)
+    if (k->shape[i] != v->shape[i]) return fail(BD_ERR_SHAPE, "k and v shapes differ");
+  if (k->shape[0] != q->shape[0] || k->shape[3] != q->shape[2])
+    return fail(BD_ERR_SHAPE, "q " + shape_str(q) + " does not match k " + shape_str(k));
+  if (q->shape[2] > 1 && q->stride[2] != 1) return fail(BD_ERR_STRIDE, "q innermost dim must be contiguous");
+  if ((rc = check_rows_aligned(k, "k"))) return rc;
+  if ((rc = check_rows_aligned(v, "v"))) return rc;
+  return BD_OK;
+}
+
+void fill_common(DenseParams& p, const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const Plan& pl,
+                 float scaling) {
+  p.q = q->data; p.q_sb = q->stride[0]; p.q_sh = q->stride[1]; p.q_dtype = q->dtype;
+  p.k = static_cast<const uint8_t*>(k->data); p.k_sb = k->stride[0]; p.k_sh = k->stride[1]; p.k_ss = k->stride[2];
+  p.v = static_cast<const uint8_t*>(v->data); p.v_sb = v->stride[0]; p.v_sh = v->stride[1]; p.v_ss = v->stride[2];
+  p.B = int(q->shape[0]); p.Hq = int(q->shape[1]); p.Hk = int(k->shape[1]); p.G = p.Hq / p.Hk; p.S = int(k->shape[2]);
+  p.head_chunks = pl.head_chunks; p.heads_per_chunk = pl.heads_per_chunk;
+  p.tiles_per_split = pl.tiles_per_split; p.n_splits = pl.n_splits;
+  p.split_offset = 0; p.split_stride = pl.n_splits;
+  p.scale_log2 = scaling * kLog2e;
+}
+
+}  // namespace
+
+int dense_split_count(int64_t B, int64_t Hq, int64_t Hk, int64_t S, int64_t D, int target_ctas) {
+  bd_tensor q{}, k{};
+  q.ndim = 3; q.shape[0] = B; q.shape[1] = Hq; q.shape[2] = D;
+  k.ndim = 4; k.shape[0] = B; k.shape[1] = Hk; k.shape[2] = S; k.shape[3] = D; k.dtype = BD_BF16;
+  Plan pl;
+  if (make_plan(&q, &k, &pl, target_ctas)) return -1;
+  return pl.n_splits;
+}
+
+int launch_dense_partials(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
+                          const Partials& part, int split_offset, int nsplit_here, cudaStream_t st) {
+  int rc;
+  if ((rc = validate(q, k, v))) return rc;
+  Plan pl;
+  if ((rc = make_plan(q, k, &pl))) return rc;
+  // force the caller's split count
+  const int64_t S = k->shape[2];
+  const int64_t ntiles = (S + kRows - 1) / kRows;
+  const int64_t tps = ntiles > 0 ? (ntiles + nsplit_here - 1) / nsplit_here : 1;
+  pl.tiles_per_split = int(tps);
+  pl.n_splits = nsplit_here;
+  DenseParams p{};
+  fill_common(p, q, k, v, pl, scaling);
+  p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
+  p.split_offset = split_offset; p.split_stride = part.nsplit;
+  p.direct = 0;
+  return dispatch_dense(p, pl, st);
+}
+
+int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st) {
+  CombineParams c{};
+  c.m = part.m; c.l = part.l; c.o = part.o;
+  c.rows = B * Hq; c.n = part.nsplit; c.D = D; c.Hq = Hq; c.ms_rows = 1;
+  c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
+  c.mode = 0;
+  if (c.rows == 0) return BD_OK;
+  lse_combine_kernel<<<c.rows, 128, size_t(c.n) * sizeof(float), st>>>(c);
+  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+}
+
+}  // namespace bd
+
+extern "C" {
+
+size_t bd_decode_attn_workspace(const bd_tensor* q, const bd_tensor* k) {
+  if (bd::check_tensor(q, "q", 3) || bd::check_tensor(k, "k", 4)) return 0;
+  bd::Plan pl;
+  if (bd::make_plan(q, k, &pl)) return 0;
+  return bd::ws_bytes(q, pl);
+}
+
+int bd_decode_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* out, float scaling,
+                   void* workspace, size_t workspace_bytes, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = validate(q, k, v))) return rc;
+  if ((rc = check_tensor(out, "out", 3))) return rc;
+  if (out->dtype != BD_BF16 && out->dtype != BD_F16 && out->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "out must be bf16, f16 or f32");
+  for (int i = 0; i < 3; ++i)
+    if (out->shape[i] != q->shape[i]) return fail(BD_ERR_SHAPE, "out shape must equal q shape");
+  if (out->stride[2] != 1) return fail(BD_ERR_STRIDE, "out innermost dim must be contiguous");
+  Plan pl;
+  if ((rc = make_plan(q, k, &pl))) return rc;
+  if (q->shape[0] == 0 || q->shape[1] == 0) return BD_OK;
+  DenseParams p{};
+  fill_common(p, q, k, v, pl, scaling);
+  p.out = out->data; p.out_dtype = out->dtype; p.o_sb = out->stride[0]; p.o_sh = out->stride[1];
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pl.n_splits == 1) {
+    p.direct = 1;
+    return dispatch_dense(p, pl, st);
+  }
+  const size_t need = ws_bytes(q, pl);
+  if (!workspace || workspace_bytes < need)
+    return fail(BD_ERR_WORKSPACE, "need " + std::to_string(need) + " workspace bytes");
+  const size_t rows = size_t(p.B) * p.Hq;
+  float* base = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  p.part_m = base;
+  p.part_l = base + rows * pl.n_splits;
+  p.part_o = base + 2 * rows * pl.n_splits;
+  p.direct = 0;
+  if ((rc = dispatch_dense(p, pl, st))) return rc;
+  CombineParams c{};
+  c.m = p.part_m; c.l = p.part_l; c.o = p.part_o;
+  c.rows = int(rows); c.n = pl.n_splits; c.D = pl.D; c.Hq = p.Hq; c.ms_rows = 1;
+  c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
+  c.mode = 0;
+  lse_combine_kernel<<<int(rows), pl.D, pl.n_splits * sizeof(float), st>>>(c);
+  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+}
+
+int bd_decode_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
+                           const bd_tensor* m, const bd_tensor* l, const bd_tensor* o, void* workspace,
+                           size_t workspace_bytes, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = validate(q, k, v))) return rc;
+  if ((rc = check_tensor(m, "m", 2, BD_F32)) || (rc = check_tensor(l, "l", 2, BD_F32)) ||
+      (rc = check_tensor(o, "o", 3, BD_F32)))
+    return rc;
+  const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
+  if (m->shape[0] != B || m->shape[1] != Hq || l->shape[0] != B || l->shape[1] != Hq || o->shape[0] != B ||
+      o->shape[1] != Hq || o->shape[2] != D)
+    return fail(BD_ERR_SHAPE, "m,l must be [B,Hq] and o [B,Hq,D]");
+  if (m->stride[1] != 1 || m->stride[0] != Hq || l->stride[1] != 1 || l->stride[0] != Hq || o->stride[2] != 1 ||
+      o->stride[1] != D || o->stride[0] != Hq * D)
+    return fail(BD_ERR_STRIDE, "m, l, o must be contiguous");
+  Plan pl;
+  if ((rc = make_plan(q, k, &pl))) return rc;
+  if (B == 0 || Hq == 0) return BD_OK;
+  const size_t need = ws_bytes(q, pl);
+  if (!workspace || workspace_bytes < need)
+    return fail(BD_ERR_WORKSPACE, "need " + std::to_string(need) + " workspace bytes");
+  DenseParams p{};
+  fill_common(p, q, k, v, pl, scaling);
+  const size_t rows = size_t(B) * Hq;
+  float* base = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  p.part_m = base;
+  p.part_l = base + rows * pl.n_splits;
+  p.part_o = base + 2 * rows * pl.n_splits;
+  p.direct = 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if ((rc = dispatch_dense(p, pl, st))) return rc;
+  CombineParams c{};
+  c.m = p.part_m; c.l = p.part_l; c.o = p.part_o;
+  c.rows = int(rows); c.n = pl.n_splits; c.D = int(D); c.Hq = int(Hq); c.ms_rows = 1;
+  c.mode = 1;
+  c.em = static_cast<float*>(m->data); c.el = static_cast<float*>(l->data); c.eo = static_cast<float*>(o->data);
+  lse_combine_kernel<<<int(rows), int(D), pl.n_splits * sizeof(float), st>>>(c);
+  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+}
+
+int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o, const bd_tensor* out,
+                   bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_tensor(m, "m", 3, BD_F32)) || (rc = check_tensor(l, "l", 3, BD_F32)) ||
+      (rc = check_tensor(o, "o", 4, BD_F32)) || (rc = check_tensor(out, "out", 3)))
+    return rc;
+  const int64_t n = m->shape[0], B = m->shape[1], Hq = m->shape[2], D = o->shape[3];
+  if (l->shape[0] != n || l->shape[1] != B || l->shape[2] != Hq || o->shape[0] != n || o->shape[1] != B ||
+      o->shape[2] != Hq || out->shape[0] != B || out->shape[1] != Hq || out->shape[2] != D)
+    return fail(BD_ERR_SHAPE, "shapes must be m,l [n,B,Hq], o [n,B,Hq,D], out [B,Hq,D]");
+  if (m->stride[2] != 1 || m->stride[1] != Hq || l->stride[2] != 1 || l->stride[1] != Hq ||
+      m->stride[0] != l->stride[0] || o->stride[3] != 1 || o->stride[2] != D || o->stride[1] != Hq * D ||
+      out->stride[2] != 1)
+    return fail(BD_ERR_STRIDE, "m, l, o must be contiguous within each shard");
+  if (out->dtype != BD_BF16 && out->dtype != BD_F16 && out->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "out must be bf16, f16 or f32");
+  if (n <= 0 || n > 4096) return fail(BD_ERR_VALUE, "shard count must be in [1, 4096]");
+  if (B * Hq == 0) return BD_OK;
+  CombineParams c{};
+  c.m = static_cast<const float*>(m->data); c.l = static_cast<const float*>(l->data);
+  c.o = static_cast<const float*>(o->data);
+  c.rows = int(B * Hq); c.n = int(n); c.D = int(D); c.Hq = int(Hq);
+  c.m_s0 = m->stride[0]; c.o_s0 = o->stride[0]; c.ms_rows = 0;
+  c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
+  c.mode = 0;
+  lse_combine_kernel<<<c.rows, 128, size_t(n) * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(c);
+  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,757 @@
+// KIVI-style 2/4-bit KV-cache decode attention, the KIVI pack step and the KIVI GEMV.
+//
+// Reference contract (saifmb0/bytes, benchmarks/kivi_latency.py:26-90):
+//   Kq  int32 [B,Hk,D,Sq/fpi]  keys quantised per channel over groups of 32 tokens,
+//                              token e of a channel row at word e/fpi, bits (e%fpi)*bits
+//   Ks,Km f16 [B,Hk,D,Sq/32]   per (channel, token-group) scale and minimum
+//   Vq  int32 [B,Hk,Sq,D/fpi]  values quantised per token over groups of 32 channels
+//   Vs,Vm f16 [B,Hk,Sq,D/32]
+//   K_res,V_res bf16 [B,Hk,R,D] the most recent R tokens at full precision
+//   out = softmax(Q.[K;K_res]^T / sqrt(D)) . [V;V_res]          (fpi = 32/bits)
+//
+// Fused decode design (one CTA = (batch, KV head, head chunk of 8, token split)):
+//  * A 128-token tile of codes, scales and minima streams into shared memory through a
+//    cp.async pipeline; each of the 4 warps owns 32 tokens = one key group.
+//  * Keys: score = sum_c q_c (code*s_c + m_c) = sum_c (q_c s_c) code + sum_c q_c m_c.
+//    The scale folds into Q' = q*s (f16, per warp per group) and the minimum into a
+//    per-(head, group) bias, so the contraction runs on the tensor cores over raw
+//    codes: S^T[16 tok x 8 heads] += codes[16 x 16] . Q'^T[16 x 8] (mma.sync f16).
+//  * Codes become MMA operands in registers without any shared-memory staging: the
+//    f16 bit pattern 0x6400|c is the value 1024+c, so one shift and one LOP3 per
+//    word yield two f16 operands; the 1024*sum(Q') offset is subtracted once per
+//    group. Register pairs along the contraction dim come from PRMT of two words.
+//  * Values: O^T[16 ch x 8 heads] += codes^T[16 x 16 tok] . P'^T[16 tok x 8], with the
+//    per-token scale folded into P' = P*s_v (one version per 32-channel group) and
+//    the minimum + 1024 offset folded into a per-(head, group) correction.
+//  * Row/token permutations are chosen so every shared-memory read is conflict-free
+//    and the movmatrix transpose of P lands directly in the PV operand layout.
+//  * The bf16 residual window runs through the dense split kernel into the same
+//    partial buffer; a log-sum-exp combine produces the output.
+#include "common.cuh"
+#include "decode_shared.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace bd {
+namespace {
+
+constexpr int kWarpsK = 4;
+constexpr int kTile = 128;  // tokens per tile
+constexpr int kStagesK = 3;
+constexpr float kLog2eK = 1.4426950408889634f;
+constexpr float kLn2K = 0.6931471805599453f;
+constexpr uint32_t kMagic = 0x64006400u;  // two f16 1024.0
+
+template <int BITS>
+struct KL {
+  static constexpr int FPI = 32 / BITS;
+  static constexpr int KQ_WORDS = kTile / FPI;          // words per channel per tile
+  static constexpr int KQ_PITCH = BITS == 2 ? 32 : 80;  // smem bytes per channel row
+  static constexpr int VQ_WORDS = 128 / FPI;            // words per token (D = 128)
+  static constexpr int VQ_PITCH = BITS == 2 ? 32 : 80;
+  static constexpr int KQ_BYTES = 128 * KQ_PITCH;
+  static constexpr int KS_BYTES = 128 * 8;  // 4 groups x f16 per channel
+  static constexpr int VQ_BYTES = kTile * VQ_PITCH;
+  static constexpr int VS_BYTES = kTile * 8;  // 4 groups x f16 per token
+  static constexpr int OFF_KS = KQ_BYTES;
+  static constexpr int OFF_KM = OFF_KS + KS_BYTES;
+  static constexpr int OFF_VQ = OFF_KM + KS_BYTES;
+  static constexpr int OFF_VS = OFF_VQ + VQ_BYTES;
+  static constexpr int OFF_VM = OFF_VS + VS_BYTES;
+  static constexpr int STAGE = OFF_VM + VS_BYTES;
+};
+
+struct KiviParams {
+  const void* q; int64_t q_sb, q_sh; int q_dtype;
+  const uint32_t* kq; int64_t kq_sb, kq_sh, kq_sc;
+  const __half* ks; int64_t ks_sb, ks_sh, ks_sc;
+  const __half* km; int64_t km_sb, km_sh, km_sc;
+  const uint32_t* vq; int64_t vq_sb, vq_sh, vq_st;
+  const __half* vs; int64_t vs_sb, vs_sh, vs_st;
+  const __half* vm; int64_t vm_sb, vm_sh, vm_st;
+  int B, Hq, Hk, G, Sq;
+  int head_chunks, tiles_per_split;
+  float scale_log2;
+  float* part_m; float* part_l; float* part_o; int split_stride;
+};
+
+__device__ __forceinline__ float load_qk(const KiviParams& p, int64_t off) {
+  switch (p.q_dtype) {
+    case BD_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[off]);
+    case BD_F16: return __half2float(reinterpret_cast<const __half*>(p.q)[off]);
+    default: return reinterpret_cast<const float*>(p.q)[off];
+  }
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+template <int BITS>
+__global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const KiviParams p) {
+  using L = KL<BITS>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y / p.head_chunks;
+  const int chunk = blockIdx.y % p.head_chunks;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int t_begin = split * p.tiles_per_split * kTile;
+  const int t_end = min(p.Sq, t_begin + p.tiles_per_split * kTile);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
+  const int h0 = chunk * 8;
+  const int nheads = min(8, p.G - h0);
+  // QK accumulator row g <-> token rho (row g+8 <-> rho+8) inside a 16-token row block
+  const int rho = (g >> 1) + 4 * (g & 1);
+
+  const uint32_t* kq_base = p.kq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh;
+  const __half* ks_base = p.ks + int64_t(b) * p.ks_sb + int64_t(hk) * p.ks_sh;
+  const __half* km_base = p.km + int64_t(b) * p.km_sb + int64_t(hk) * p.km_sh;
+  const uint32_t* vq_base = p.vq + int64_t(b) * p.vq_sb + int64_t(hk) * p.vq_sh;
+  const __half* vs_base = p.vs + int64_t(b) * p.vs_sb + int64_t(hk) * p.vs_sh;
+  const __half* vm_base = p.vm + int64_t(b) * p.vm_sb + int64_t(hk) * p.vm_sh;
+
+  // query (fp32) for head g, channels tq + 4i
+  float qf[32];
+  {
+    const bool ok = g < nheads;
+    const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? g : 0)) * p.q_sh;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qf[i] = ok ? load_qk(p, qoff + tq + 4 * i) : 0.f;
+  }
+
+  const int words_end = (t_end + L::FPI - 1) / L::FPI;  // first word index past the split
+  const int groups_end = (t_end + 31) / 32;
+  auto load_tile = [&](int tile, int stage) {
+    const int t0 = t_begin + tile * kTile;
+    uint8_t* st = smem + stage * L::STAGE;
+    const uint32_t sbase = smem_u32(st);
+    constexpr int NCH = L::KQ_WORDS / 4;  // 16-byte chunks per channel row
+    for (int c = threadIdx.x; c < 128 * NCH; c += kWarpsK * 32) {
+      const int row = c / NCH, ck = c % NCH;
+      const int w0 = t0 / L::FPI + ck * 4;
+      const int valid = max(0, min(4, words_end - w0));
+      const uint32_t* src = kq_base + int64_t(row) * p.kq_sc + (valid ? w0 : 0);
+      cp_async16(sbase + row * L::KQ_PITCH + ck * 16, src, valid * 4);
+    }
+    {
+      const int row = threadIdx.x;  // 128 threads == 128 channels
+      const int gr0 = t0 / 32;
+      const int valid = max(0, min(4, groups_end - gr0));
+      cp_async8(sbase + L::OFF_KS + row * 8, ks_base + int64_t(row) * p.ks_sc + (valid ? gr0 : 0), valid * 2);
+      cp_async8(sbase + L::OFF_KM + row * 8, km_base + int64_t(row) * p.km_sc + (valid ? gr0 : 0), valid * 2);
+    }
+    constexpr int NVC = L::VQ_WORDS / 4;
+    for (int c = threadIdx.x; c < kTile * NVC; c += kWarpsK * 32) {
+      const int r = c / NVC, ck = c % NVC;
+      const int t = t0 + r;
+      const bool ok = t < t_end;
+      cp_async16(sbase + L::OFF_VQ + r * L::VQ_PITCH + ck * 16, vq_base + int64_t(ok ? t : 0) * p.vq_st + ck * 4,
+                 ok ? 16 : 0);
+    }
+    {
+      const int r = threadIdx.x;  // 128 threads == 128 tokens
+      const int t = t0 + r;
+      const bool ok = t < t_end;
+      cp_async8(sbase + L::OFF_VS + r * 8, vs_base + int64_t(ok ? t : 0) * p.vs_st, ok ? 8 : 0);
+      cp_async8(sbase + L::OFF_VM + r * 8, vm_base + int64_t(ok ? t : 0) * p.vm_st, ok ? 8 : 0);
+    }
+  };
+
+  float o[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float corr[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) corr[j][0] = corr[j][1] = corr[j][2] = corr[j][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+#pragma unroll
+  for (int s = 0; s < kStagesK - 1; ++s) {
+    if (s < ntiles) load_tile(s, s);
+    cp_async_commit();
+  }
+
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait<kStagesK - 2>();
+    __syncthreads();
+    {
+      const int nxt = it + kStagesK - 1;
+      if (nxt < ntiles) load_tile(nxt, nxt % kStagesK);
+      cp_async_commit();
+    }
+    const uint8_t* st = smem + (it % kStagesK) * L::STAGE;
+    const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
+    if (tb >= t_end) continue;
+
+    // ---- Q' = q * s_k (f16) and the per-head bias sum_c q_c m_c - 1024 sum_c Q'_c
+    uint32_t qb[8][2];
+    float bb0, bb1;
+    {
+      const __half* ksr = reinterpret_cast<const __half*>(st + L::OFF_KS);
+      const __half* kmr = reinterpret_cast<const __half*>(st + L::OFF_KM);
+      float sumq = 0.f, bias = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        __half hh[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 4 * j + e;
+          const int c = tq + 4 * i;
+          const float s = __half2float(ksr[c * 4 + warp]);
+          const float m = __half2float(kmr[c * 4 + warp]);
+          hh[e] = __float2half_rn(qf[i] * s);
+          sumq += __half2float(hh[e]);
+          bias = fmaf(qf[i], m, bias);
+        }
+        qb[j][0] = h2u(__halves2half2(hh[0], hh[1]));
+        qb[j][1] = h2u(__halves2half2(hh[2], hh[3]));
+      }
+      float be = bias - 1024.f * sumq;
+      be += __shfl_xor_sync(0xffffffffu, be, 1);
+      be += __shfl_xor_sync(0xffffffffu, be, 2);
+      bb0 = __shfl_sync(0xffffffffu, be, (2 * tq) * 4);
+      bb1 = __shfl_sync(0xffffffffu, be, (2 * tq + 1) * 4);
+    }
+
+    // ---- S^T for the warp's two 16-token row blocks
+    float s[2][4];
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) s[rb][0] = s[rb][1] = s[rb][2] = s[rb][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t U[2][4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = 16 * j + tq + 4 * e;
+        if (BITS == 2) {
+          const uint2 w2 = *reinterpret_cast<const uint2*>(st + c * L::KQ_PITCH + warp * 8);
+          U[0][e] = ((w2.x >> (2 * rho)) & 0x00030003u) | kMagic;
+          U[1][e] = ((w2.y >> (2 * rho)) & 0x00030003u) | kMagic;
+        } else {
+          const uint4 w4 = *reinterpret_cast<const uint4*>(st + c * L::KQ_PITCH + warp * 16);
+          const uint32_t sel = rho < 4 ? 0x5410u : 0x7632u;
+          const int sh = 4 * (rho & 3);
+          U[0][e] = ((prmt(w4.x, w4.y, sel) >> sh) & 0x000F000Fu) | kMagic;
+          U[1][e] = ((prmt(w4.z, w4.w, sel) >> sh) & 0x000F000Fu) | kMagic;
+        }
+      }
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        const uint32_t a0 = prmt(U[rb][0], U[rb][1], 0x5410u);
+        const uint32_t a1 = prmt(U[rb][0], U[rb][1], 0x7632u);
+        const uint32_t a2 = prmt(U[rb][2], U[rb][3], 0x5410u);
+        const uint32_t a3 = prmt(U[rb][2], U[rb][3], 0x7632u);
+        mma_f16(s[rb], a0, a1, a2, a3, qb[j][0], qb[j][1]);
+      }
+    }
+
+    // ---- online softmax over the 32 tokens (exp2 domain)
+    float pv[2][4];
+    {
+      const float bbj[2] = {bb0, bb1};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[4];
+#pragma unroll
+        for (int rb = 0; rb < 2; ++rb) {
+          const int tr = tb + 16 * rb + rho;
+          x[2 * rb] = tr < t_end ? (s[rb][j] + bbj[j]) * p.scale_log2 : -INFINITY;
+          x[2 * rb + 1] = tr + 8 < t_end ? (s[rb][2 + j] + bbj[j]) * p.scale_log2 : -INFINITY;
+        }
+        float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mnew = fmaxf(mrow[j], mx);
+        const float muse = mnew == -INFINITY ? 0.f : mnew;
+        const float alpha = exp2f(mrow[j] - muse);
+        mrow[j] = mnew;
+        float acc = 0.f;
+#pragma unroll
+        for (int rb = 0; rb < 2; ++rb) {
+          pv[rb][j] = exp2f(x[2 * rb] - muse);
+          pv[rb][2 + j] = exp2f(x[2 * rb + 1] - muse);
+          acc += pv[rb][j] + pv[rb][2 + j];
+        }
+        lrow[j] = lrow[j] * alpha + acc;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][j] *= alpha;
+          o[mt][2 + j] *= alpha;
+        }
+#pragma unroll
+        for (int gr = 0; gr < 4; ++gr) corr[j][gr] *= alpha;
+      }
+    }
+
+    // ---- P' = P * s_v per group, PV on the tensor cores
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      const int tl = 32 * warp + 16 * rb;  // tile-local first token of the row block
+      uint32_t pb[4][2];
+      {
+        const uint2 vs0 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tl + rho) * 8);
+        const uint2 vs1 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tl + rho + 8) * 8);
+        const uint2 vm0 = *reinterpret_cast<const uint2*>(st + L::OFF_VM + (tl + rho) * 8);
+        const uint2 vm1 = *reinterpret_cast<const uint2*>(st + L::OFF_VM + (tl + rho + 8) * 8);
+        const uint32_t hp0 = pack_f16x2(pv[rb][0], pv[rb][1]);
+        const uint32_t hp1 = pack_f16x2(pv[rb][2], pv[rb][3]);
+        const uint32_t s0w[2] = {vs0.x, vs0.y}, s1w[2] = {vs1.x, vs1.y};
+        const uint32_t m0w[2] = {vm0.x, vm0.y}, m1w[2] = {vm1.x, vm1.y};
+#pragma unroll
+        for (int gr = 0; gr < 4; ++gr) {
+          const uint32_t sel = (gr & 1) ? 0x3232u : 0x1010u;  // broadcast one f16 to both halves
+          const __half2 sc0 = u2h(prmt(s0w[gr >> 1], 0, sel));
+          const __half2 sc1 = u2h(prmt(s1w[gr >> 1], 0, sel));
+          const __half2 q0 = __hmul2(u2h(hp0), sc0);
+          const __half2 q1 = __hmul2(u2h(hp1), sc1);
+          pb[gr][0] = movmatrix_trans(h2u(q0));
+          pb[gr][1] = movmatrix_trans(h2u(q1));
+          const float2 f0 = __half22float2(q0), f1 = __half22float2(q1);
+          const float mn0 = __half2float(__low2half(u2h(prmt(m0w[gr >> 1], 0, sel))));
+          const float mn1 = __half2float(__low2half(u2h(prmt(m1w[gr >> 1], 0, sel))));
+          corr[0][gr] += pv[rb][0] * mn0 + pv[rb][2] * mn1 - 1024.f * (f0.x + f1.x);
+          corr[1][gr] += pv[rb][1] * mn0 + pv[rb][3] * mn1 - 1024.f * (f0.y + f1.y);
+        }
+      }
+      // value codes of tokens tl + tq + 4u, u = 0..3
+      if (BITS == 2) {
+        uint32_t W[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint8_t* row = st + L::OFF_VQ + (tl + tq + 4 * u) * L::VQ_PITCH;
+          const uint4 lo = *reinterpret_cast<const uint4*>(row);
+          const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
+          W[u][0] = lo.x; W[u][1] = lo.y; W[u][2] = lo.z; W[u][3] = lo.w;
+          W[u][4] = hi.x; W[u][5] = hi.y; W[u][6] = hi.z; W[u][7] = hi.w;
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          uint32_t Uu[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) Uu[u] = ((W[u][mt] >> (2 * g)) & 0x00030003u) | kMagic;
+          mma_f16(o[mt], prmt(Uu[0], Uu[1], 0x5410u), prmt(Uu[0], Uu[1], 0x7632u), prmt(Uu[2], Uu[3], 0x5410u),
+                  prmt(Uu[2], Uu[3], 0x7632u), pb[mt >> 1][0], pb[mt >> 1][1]);
+        }
+      } else {
+        const bool hiw = g >= 4;
+        const int sh = 4 * (g & 3);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t W[4][8];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint8_t* row = st + L::OFF_VQ + (tl + tq + 4 * u) * L::VQ_PITCH + half * 32;
+            const uint4 lo = *reinterpret_cast<const uint4*>(row);
+            const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
+            W[u][0] = lo.x; W[u][1] = lo.y; W[u][2] = lo.z; W[u][3] = lo.w;
+            W[u][4] = hi.x; W[u][5] = hi.y; W[u][6] = hi.z; W[u][7] = hi.w;
+          }
+#pragma unroll
+          for (int ml = 0; ml < 4; ++ml) {
+            const int mt = 4 * half + ml;
+            uint32_t Uu[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const uint32_t w = hiw ? W[u][2 * ml + 1] : W[u][2 * ml];
+              Uu[u] = ((w >> sh) & 0x000F000Fu) | kMagic;
+            }
+            mma_f16(o[mt], prmt(Uu[0], Uu[1], 0x5410u), prmt(Uu[0], Uu[1], 0x7632u),
+                    prmt(Uu[2], Uu[3], 0x5410u), prmt(Uu[2], Uu[3], 0x7632u), pb[mt >> 1][0], pb[mt >> 1][1]);
+          }
+        }
+      }
+    }
+  }
+
+  // ---- epilogue: reduce over rows, merge warps, write split partials
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float l = lrow[j];
+    l += __shfl_xor_sync(0xffffffffu, l, 4);
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+    lrow[j] = l;
+#pragma unroll
+    for (int gr = 0; gr < 4; ++gr) {
+      float c = corr[j][gr];
+      c += __shfl_xor_sync(0xffffffffu, c, 4);
+      c += __shfl_xor_sync(0xffffffffu, c, 8);
+      c += __shfl_xor_sync(0xffffffffu, c, 16);
+      corr[j][gr] = c;
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  float* red_m = reinterpret_cast<float*>(smem);  // [4][8]
+  float* red_l = red_m + kWarpsK * 8;             // [4][8]
+  float* red_o = red_l + kWarpsK * 8;             // [4][8][128]
+  if (g == 0) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      red_m[warp * 8 + 2 * tq + j] = mrow[j];
+      red_l[warp * 8 + 2 * tq + j] = lrow[j];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int h = 2 * tq + j;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarpsK; ++w) M = fmaxf(M, red_m[w * 8 + h]);
+    const float f = (M == -INFINITY) ? 0.f : exp2f(mrow[j] - M);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      int ca, cb;
+      if (BITS == 2) { ca = 16 * mt + g; cb = ca + 8; }
+      else { ca = 16 * mt + (g < 4 ? g : g + 4); cb = ca + 4; }
+      red_o[(warp * 8 + h) * 128 + ca] = (o[mt][j] + corr[j][mt >> 1]) * f;
+      red_o[(warp * 8 + h) * 128 + cb] = (o[mt][2 + j] + corr[j][mt >> 1]) * f;
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nheads * 128; idx += kWarpsK * 32) {
+    const int h = idx >> 7, c = idx & 127;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarpsK; ++w) M = fmaxf(M, red_m[w * 8 + h]);
+    float Lsum = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsK; ++w) {
+      const float f = (M == -INFINITY) ? 0.f : exp2f(red_m[w * 8 + h] - M);
+      Lsum += red_l[w * 8 + h] * f;
+      O += red_o[(w * 8 + h) * 128 + c];
+    }
+    const int hq = hk * p.G + h0 + h;
+    const int64_t pi = (int64_t(b) * p.Hq + hq) * p.split_stride + split;
+    p.part_o[pi * 128 + c] = O;
+    if (c == 0) {
+      p.part_m[pi] = M * kLn2K;
+      p.part_l[pi] = Lsum;
+    }
+  }
+}
+
+template <int BITS>
+int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
+  using L = KL<BITS>;
+  const size_t smem = std::max<size_t>(size_t(kStagesK) * L::STAGE, (2 * 4 * 8 + 4 * 8 * 128) * sizeof(float));
+  auto kern = kivi_decode_kernel<BITS>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                        "cudaFuncSetAttribute(kivi)");
+    if (rc) return rc;
+    attr[dev & 63] = true;
+  }
+  dim3 grid(n_splits, kp.Hk * kp.head_chunks, kp.B);
+  kern<<<grid, kWarpsK * 32, smem, st>>>(kp);
+  return cuda_check(cudaGetLastError(), "kivi_decode_kernel launch");
+}
+
+struct KiviPlan {
+  int n_kivi, tiles_per_split, n_res, head_chunks;
+};
+
+int kivi_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t Sq, int64_t R, KiviPlan* pl) {
+  const int G = int(Hq / Hk);
+  pl->head_chunks = (G + 7) / 8;
+  const int64_t ntiles = (Sq + kTile - 1) / kTile;
+  const int64_t pairs = B * Hk * pl->head_chunks;
+  const int64_t slots = 3LL * num_sms();
+  int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
+  const int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;
+  pl->n_kivi = ntiles > 0 ? int((ntiles + tps - 1) / tps) : 0;
+  pl->tiles_per_split = int(tps);
+  pl->n_res = R > 0 ? std::max(1, dense_split_count(B, Hq, Hk, R, 128, int(pairs))) : 0;
+  return BD_OK;
+}
+
+int check_kivi_inputs(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* Ks, const bd_tensor* Km,
+                      const bd_tensor* Kr, const bd_tensor* Vq, const bd_tensor* Vs, const bd_tensor* Vm,
+                      const bd_tensor* Vr, int bits, int group_size) {
+  int rc;
+  if (bits != 2 && bits != 4) return fail(BD_ERR_VALUE, "bits must be 2 or 4");
+  if (group_size != 32) return fail(BD_ERR_UNSUPPORTED, "group_size must be 32");
+  if ((rc = check_tensor(Q, "Q", 3)) || (rc = check_tensor(Kq, "Kq", 4, BD_I32)) ||
+      (rc = check_tensor(Ks, "K_scale", 4, BD_F16)) || (rc = check_tensor(Km, "K_mn", 4, BD_F16)) ||
+      (rc = check_tensor(Kr, "K_residual", 4, BD_BF16)) || (rc = check_tensor(Vq, "Vq", 4, BD_I32)) ||
+      (rc = check_tensor(Vs, "V_scale", 4, BD_F16)) || (rc = check_tensor(Vm, "V_mn", 4, BD_F16)) ||
+      (rc = check_tensor(Vr, "V_residual", 4, BD_BF16)))
+    return rc;
+  if (Q->dtype != BD_BF16 && Q->dtype != BD_F16 && Q->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "Q must be bf16, f16 or f32");
+  const int64_t B = Q->shape[0], Hq = Q->shape[1], D = Q->shape[2];
+  const int64_t Hk = Kq->shape[1];
+  const int fpi = 32 / bits;
+  if (D != 128) return fail(BD_ERR_UNSUPPORTED, "KIVI decode supports head_dim 128");
+  if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
+  const int64_t Sq = Kq->shape[3] * fpi;
+  if (Kq->shape[0] != B || Kq->shape[2] != D) return fail(BD_ERR_SHAPE, "Kq must be [B,Hk,D,Sq/fpi]");
+  for (const bd_tensor* t : {Ks, Km})
+    if (t->shape[0] != B || t->shape[1] != Hk || t->shape[2] != D || t->shape[3] * 32 != Sq)
+      return fail(BD_ERR_SHAPE, "K_scale/K_mn must be [B,Hk,D,Sq/32]");
+  if (Vq->shape[0] != B || Vq->shape[1] != Hk || Vq->shape[2] != Sq || Vq->shape[3] * fpi != D)
+    return fail(BD_ERR_SHAPE, "Vq must be [B,Hk,Sq,D/fpi], Sq matching Kq");
+  for (const bd_tensor* t : {Vs, Vm})
+    if (t->shape[0] != B || t->shape[1] != Hk || t->shape[2] != Sq || t->shape[3] * 32 != D)
+      return fail(BD_ERR_SHAPE, "V_scale/V_mn must be [B,Hk,Sq,D/32]");
+  for (const bd_tensor* t : {Kr, Vr})
+    if (t->shape[0] != B || t->shape[1] != Hk || t->shape[3] != D || t->shape[2] != Kr->shape[2])
+      return fail(BD_ERR_SHAPE, "K_residual/V_residual must be [B,Hk,R,D]");
+  if ((rc = check_rows_aligned(Kq, "Kq", 16)) || (rc = check_rows_aligned(Vq, "Vq", 16)) ||
+      (rc = check_rows_aligned(Ks, "K_scale", 8)) || (rc = check_rows_aligned(Km, "K_mn", 8)) ||
+      (rc = check_rows_aligned(Vs, "V_scale", 8)) || (rc = check_rows_aligned(Vm, "V_mn", 8)))
+    return rc;
+  if (Q->stride[2] != 1) return fail(BD_ERR_STRIDE, "Q innermost dim must be contiguous");
+  return BD_OK;
+}
+
+__global__ void empty_partials_kernel(float* m, float* l, float* o, int rows, int D) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  m[r] = -INFINITY;
+  l[r] = 0.f;
+  for (int c = 0; c < D; ++c) o[int64_t(r) * D + c] = 0.f;
+}
+
+// ---------------------------------------------------------------- KIVI pack
+template <typename T, int BITS>
+__global__ void kivi_pack_kernel(const T* __restrict__ x, int nlead, int64_t l0, int64_t l1, int64_t l2,
+                                 int64_t s0, int64_t s1, int64_t s2, int N, int64_t total_groups,
+                                 uint32_t* __restrict__ code, T* __restrict__ scale, T* __restrict__ mn) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid >= total_groups) return;
+  const int gpr = N / 32;
+  const int64_t row = gid / gpr;
+  const int grp = int(gid % gpr);
+  // row -> (i0, i1, i2) over up to three leading dims
+  const int64_t i2 = row % l2, r1 = row / l2;
+  const int64_t i1 = r1 % l1, i0 = r1 / l1;
+  const T* src = x + i0 * s0 + i1 * s1 + i2 * s2 + int64_t(grp) * 32;
+  float v[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = to_f32<T>(src[e]);
+  float lo = v[0], hi = v[0];
+#pragma unroll
+  for (int e = 1; e < 32; ++e) { lo = fminf(lo, v[e]); hi = fmaxf(hi, v[e]); }
+  constexpr int LV = (1 << BITS) - 1;
+  const float sc = __fdiv_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), float(LV));
+  constexpr int FPI = 32 / BITS;
+  uint32_t words[32 / FPI];
+#pragma unroll
+  for (int w = 0; w < 32 / FPI; ++w) words[w] = 0u;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    float qv = rintf(__fdiv_rn(__fsub_rn(v[e], lo), sc));
+    qv = fminf(fmaxf(qv, 0.f), float(LV));
+    words[e / FPI] |= uint32_t(qv) << ((e % FPI) * BITS);
+  }
+  const int64_t wbase = row * (N / FPI) + int64_t(grp) * (32 / FPI);
+#pragma unroll
+  for (int w = 0; w < 32 / FPI; ++w) code[wbase + w] = words[w];
+  scale[row * gpr + grp] = from_f32<T>(sc);
+  mn[row * gpr + grp] = from_f32<T>(lo);
+}
+
+// ---------------------------------------------------------------- KIVI GEMV
+// out[b,hq,m,n] = sum_k fA[b,hq,m,k] * (code(qB[b,hk,k,n]) * sc[b,hk,k,n/gs] + zr[b,hk,k,n/gs])
+struct GemvParams {
+  const __half* fa; int64_t fa_sb, fa_sh, fa_sm;
+  const uint32_t* qb; int64_t qb_sb, qb_sh, qb_sk;
+  const __half* sc; int64_t sc_sb, sc_sh, sc_sk;
+  const __half* zr; int64_t zr_sb, zr_sh, zr_sk;
+  __half* out; int64_t o_sb, o_sh, o_sm;
+  int B, Hq, Hk, M, K, N, bits, gs;
+};
+
+__global__ void kivi_gemv_kernel(const GemvParams p) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, hq = bh % p.Hq, hk = hq / (p.Hq / p.Hk);
+  if (n >= p.N) return;
+  const int fpi = 32 / p.bits;
+  const uint32_t mask = (1u << p.bits) - 1u;
+  const int sh = (n % fpi) * p.bits;
+  const uint32_t* qrow = p.qb + int64_t(b) * p.qb_sb + int64_t(hk) * p.qb_sh + n / fpi;
+  const __half* srow = p.sc + int64_t(b) * p.sc_sb + int64_t(hk) * p.sc_sh + n / p.gs;
+  const __half* zrow = p.zr + int64_t(b) * p.zr_sb + int64_t(hk) * p.zr_sh + n / p.gs;
+  for (int m = 0; m < p.M; ++m) {
+    const __half* arow = p.fa + int64_t(b) * p.fa_sb + int64_t(hq) * p.fa_sh + int64_t(m) * p.fa_sm;
+    float acc = 0.f;
+    for (int k = 0; k < p.K; ++k) {
+      const float c = float((qrow[int64_t(k) * p.qb_sk] >> sh) & mask);
+      const float w = c * __half2float(srow[int64_t(k) * p.sc_sk]) + __half2float(zrow[int64_t(k) * p.zr_sk]);
+      acc = fmaf(__half2float(arow[k]), w, acc);
+    }
+    p.out[int64_t(b) * p.o_sb + int64_t(hq) * p.o_sh + int64_t(m) * p.o_sm + n] = __float2half_rn(acc);
+  }
+}
+
+}  // namespace
+}  // namespace bd
+
+extern "C" {
+
+size_t bd_kivi_decode_attn_workspace(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_residual,
+                                     int bits) {
+  using namespace bd;
+  if (check_tensor(Q, "Q", 3) || check_tensor(Kq, "Kq", 4) || check_tensor(K_residual, "K_residual", 4)) return 0;
+  if (bits != 2 && bits != 4) return 0;
+  KiviPlan pl;
+  kivi_plan(Q->shape[0], Q->shape[1], Kq->shape[1], Kq->shape[3] * (32 / bits), K_residual->shape[2], &pl);
+  return partials_bytes(size_t(Q->shape[0] * Q->shape[1]), std::max(1, pl.n_kivi + pl.n_res), 128);
+}
+
+int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale, const bd_tensor* K_mn,
+                        const bd_tensor* K_residual, const bd_tensor* Vq, const bd_tensor* V_scale,
+                        const bd_tensor* V_mn, const bd_tensor* V_residual, int bits, int group_size, float scaling,
+                        const bd_tensor* out, void* workspace, size_t workspace_bytes, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_kivi_inputs(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_residual, bits, group_size)))
+    return rc;
+  if ((rc = check_tensor(out, "out", 3))) return rc;
+  if (out->dtype != BD_BF16 && out->dtype != BD_F16 && out->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "out must be bf16, f16 or f32");
+  for (int i = 0; i < 3; ++i)
+    if (out->shape[i] != Q->shape[i]) return fail(BD_ERR_SHAPE, "out must have Q's shape");
+  if (out->stride[2] != 1) return fail(BD_ERR_STRIDE, "out innermost dim must be contiguous");
+  const int64_t B = Q->shape[0], Hq = Q->shape[1], Hk = Kq->shape[1];
+  const int64_t Sq = Kq->shape[3] * (32 / bits), R = K_residual->shape[2];
+  if (B * Hq == 0) return BD_OK;
+  KiviPlan pl;
+  kivi_plan(B, Hq, Hk, Sq, R, &pl);
+  const int ntot = std::max(1, pl.n_kivi + pl.n_res);
+  const size_t need = partials_bytes(size_t(B * Hq), ntot, 128);
+  if (!workspace || workspace_bytes < need)
+    return fail(BD_ERR_WORKSPACE, "need " + std::to_string(need) + " workspace bytes");
+  Partials part = carve_partials(workspace, size_t(B * Hq), ntot, 128);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pl.n_kivi + pl.n_res == 0) {
+    // no keys at all: one empty partial per row -> NaN output like the reference's 0/0
+    const int rows = int(B * Hq);
+    empty_partials_kernel<<<(rows + 127) / 128, 128, 0, st>>>(part.m, part.l, part.o, rows, 128);
+    if ((rc = cuda_check(cudaGetLastError(), "empty_partials_kernel launch"))) return rc;
+    return launch_combine(part, int(B), int(Hq), 128, out, st);
+  }
+  if (pl.n_kivi > 0) {
+    KiviParams kp{};
+    kp.q = Q->data; kp.q_sb = Q->stride[0]; kp.q_sh = Q->stride[1]; kp.q_dtype = Q->dtype;
+    kp.kq = static_cast<const uint32_t*>(Kq->data); kp.kq_sb = Kq->stride[0]; kp.kq_sh = Kq->stride[1]; kp.kq_sc = Kq->stride[2];
+    kp.ks = static_cast<const __half*>(K_scale->data); kp.ks_sb = K_scale->stride[0]; kp.ks_sh = K_scale->stride[1]; kp.ks_sc = K_scale->stride[2];
+    kp.km = static_cast<const __half*>(K_mn->data); kp.km_sb = K_mn->stride[0]; kp.km_sh = K_mn->stride[1]; kp.km_sc = K_mn->stride[2];
+    kp.vq = static_cast<const uint32_t*>(Vq->data); kp.vq_sb = Vq->stride[0]; kp.vq_sh = Vq->stride[1]; kp.vq_st = Vq->stride[2];
+    kp.vs = static_cast<const __half*>(V_scale->data); kp.vs_sb = V_scale->stride[0]; kp.vs_sh = V_scale->stride[1]; kp.vs_st = V_scale->stride[2];
+    kp.vm = static_cast<const __half*>(V_mn->data); kp.vm_sb = V_mn->stride[0]; kp.vm_sh = V_mn->stride[1]; kp.vm_st = V_mn->stride[2];
+    kp.B = int(B); kp.Hq = int(Hq); kp.Hk = int(Hk); kp.G = int(Hq / Hk); kp.Sq = int(Sq);
+    kp.head_chunks = pl.head_chunks; kp.tiles_per_split = pl.tiles_per_split;
+    kp.scale_log2 = scaling * kLog2eK;
+    kp.part_m = part.m; kp.part_l = part.l; kp.part_o = part.o; kp.split_stride = ntot;
+    rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, st) : launch_kivi<4>(kp, pl.n_kivi, st);
+    if (rc) return rc;
+  }
+  if (pl.n_res > 0) {
+    if ((rc = launch_dense_partials(Q, K_residual, V_residual, scaling, part, pl.n_kivi, pl.n_res, st))) return rc;
+  }
+  return launch_combine(part, int(B), int(Hq), 128, out, st);
+}
+
+int bd_kivi_pack_last_dim(const bd_tensor* x, int group_size, int bits, const bd_tensor* code,
+                          const bd_tensor* scale, const bd_tensor* mn, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if (!x) return fail(BD_ERR_NULL, "x is NULL");
+  if (bits != 2 && bits != 4 && bits != 8) return fail(BD_ERR_VALUE, "bits must be 2, 4 or 8");
+  if (group_size != 32) return fail(BD_ERR_UNSUPPORTED, "group_size must be 32");
+  const int nd = x->ndim;
+  if (nd < 1 || nd > 4) return fail(BD_ERR_SHAPE, "x must have 1 to 4 dims");
+  if ((rc = check_tensor(x, "x", nd)) || (rc = check_tensor(code, "code", nd, BD_I32)) ||
+      (rc = check_tensor(scale, "scale", nd, x->dtype)) || (rc = check_tensor(mn, "mn", nd, x->dtype)))
+    return rc;
+  if (x->dtype != BD_F16 && x->dtype != BD_BF16 && x->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "x must be f16, bf16 or f32");
+  const int64_t N = x->shape[nd - 1];
+  if (N % 32) return fail(BD_ERR_SHAPE, "last dim must be a multiple of 32");
+  if (x->stride[nd - 1] != 1 && N > 1) return fail(BD_ERR_STRIDE, "x innermost dim must be contiguous");
+  const int fpi = 32 / bits;
+  int64_t rows = 1;
+  for (int i = 0; i + 1 < nd; ++i) {
+    rows *= x->shape[i];
+    if (code->shape[i] != x->shape[i] || scale->shape[i] != x->shape[i] || mn->shape[i] != x->shape[i])
+      return fail(BD_ERR_SHAPE, "leading dims of outputs must match x");
+  }
+  if (code->shape[nd - 1] * fpi != N || scale->shape[nd - 1] * 32 != N || mn->shape[nd - 1] * 32 != N)
+    return fail(BD_ERR_SHAPE, "code must be [..,N*bits/32], scale/mn [..,N/32]");
+  // outputs are written densely
+  auto dense = [&](const bd_tensor* t) {
+    int64_t s = 1;
+    for (int i = nd - 1; i >= 0; --i) {
+      if (t->shape[i] > 1 && t->stride[i] != s) return false;
+      s *= t->shape[i];
+    }
+    return true;
+  };
+  if (!dense(code) || !dense(scale) || !dense(mn)) return fail(BD_ERR_STRIDE, "code, scale, mn must be contiguous");
+  if (rows * N == 0) return BD_OK;
+  int64_t l[3] = {1, 1, 1}, s[3] = {0, 0, 0};
+  for (int i = 0; i + 1 < nd; ++i) { l[3 - (nd - 1) + i] = x->shape[i]; s[3 - (nd - 1) + i] = x->stride[i]; }
+  const int64_t total = rows * (N / 32);
+  const int threads = 128;
+  const unsigned blocks = unsigned((total + threads - 1) / threads);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t* cd = static_cast<uint32_t*>(code->data);
+#define BD_PACK(T, BT)                                                                                         \
+  if (bits == 2) kivi_pack_kernel<T, 2><<<blocks, threads, 0, st>>>(static_cast<const T*>(x->data), nd - 1, l[0], l[1], l[2], s[0], s[1], s[2], int(N), total, cd, static_cast<T*>(scale->data), static_cast<T*>(mn->data)); \
+  else if (bits == 4) kivi_pack_kernel<T, 4><<<blocks, threads, 0, st>>>(static_cast<const T*>(x->data), nd - 1, l[0], l[1], l[2], s[0], s[1], s[2], int(N), total, cd, static_cast<T*>(scale->data), static_cast<T*>(mn->data)); \
+  else kivi_pack_kernel<T, 8><<<blocks, threads, 0, st>>>(static_cast<const T*>(x->data), nd - 1, l[0], l[1], l[2], s[0], s[1], s[2], int(N), total, cd, static_cast<T*>(scale->data), static_cast<T*>(mn->data));
+  if (x->dtype == BD_F16) { BD_PACK(__half, BD_F16) }
+  else if (x->dtype == BD_BF16) { BD_PACK(__nv_bfloat16, BD_BF16) }
+  else { BD_PACK(float, BD_F32) }
+#undef BD_PACK
+  return cuda_check(cudaGetLastError(), "kivi_pack_kernel launch");
+}
+
+int bd_kivi_gemv_outer(int group_size, const bd_tensor* fA, const bd_tensor* qB, const bd_tensor* scales,
+                       const bd_tensor* zeros, int bits, const bd_tensor* out, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if (bits != 2 && bits != 4 && bits != 8) return fail(BD_ERR_VALUE, "bits must be 2, 4 or 8");
+  if (group_size <= 0) return fail(BD_ERR_VALUE, "group_size must be positive");
+  if ((rc = check_tensor(fA, "fA", 4, BD_F16)) || (rc = check_tensor(qB, "qB", 4, BD_I32)) ||
+      (rc = check_tensor(scales, "scales", 4, BD_F16)) || (rc = check_tensor(zeros, "zeros", 4, BD_F16)) ||
+      (rc = check_tensor(out, "out", 4, BD_F16)))
+    return rc;
+  const int64_t B = fA->shape[0], Hq = fA->shape[1], M = fA->shape[2], K = fA->shape[3];
+  const int64_t Hk = qB->shape[1], N = qB->shape[3] * (32 / bits);
+  if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "fA heads must be a multiple of qB heads");
+  if (qB->shape[0] != B || qB->shape[2] != K) return fail(BD_ERR_SHAPE, "qB must be [B,Hk,K,N*bits/32]");
+  if (N % group_size) return fail(BD_ERR_SHAPE, "N must be a multiple of group_size");
+  for (const bd_tensor* t : {scales, zeros})
+    if (t->shape[0] != B || t->shape[1] != Hk || t->shape[2] != K || t->shape[3] * group_size != N)
+      return fail(BD_ERR_SHAPE, "scales/zeros must be [B,Hk,K,N/group_size]");
+  if (out->shape[0] != B || out->shape[1] != Hq || out->shape[2] != M || out->shape[3] != N)
+    return fail(BD_ERR_SHAPE, "out must be [B,Hq,M,N]");
+  if ((fA->stride[3] != 1 && K > 1) || (qB->stride[3] != 1 && qB->shape[3] > 1) || (scales->stride[3] != 1 && scales->shape[3] > 1) ||
+      (zeros->stride[3] != 1 && zeros->shape[3] > 1) || (out->stride[3] != 1 && N > 1))
+    return fail(BD_ERR_STRIDE, "innermost dims must be contiguous");
+  if (B * Hq * M * N == 0) return BD_OK;
+  GemvParams p{};
+  p.fa = static_cast<const __half*>(fA->data); p.fa_sb = fA->stride[0]; p.fa_sh = fA->stride[1]; p.fa_sm = fA->stride[2];
+  p.qb = static_cast<const uint32_t*>(qB->data); p.qb_sb = qB->stride[0]; p.qb_sh = qB->stride[1]; p.qb_sk = qB->stride[2];
+  p.sc = static_cast<const __half*>(scales->data); p.sc_sb = scales->stride[0]; p.sc_sh = scales->stride[1]; p.sc_sk = scales->stride[2];
+  p.zr = static_cast<const __half*>(zeros->data); p.zr_sb = zeros->stride[0]; p.zr_sh = zeros->stride[1]; p.zr_sk = zeros->stride[2];
+  p.out = static_cast<__half*>(out->data); p.o_sb = out->stride[0]; p.o_sh = out->stride[1]; p.o_sm = out->stride[2];
+  p.B = int(B); p.Hq = int(Hq); p.Hk = int(Hk); p.M = int(M); p.K = int(K); p.N = int(N); p.bits = bits; p.gs = group_size;
+  dim3 grid(unsigned((N + 127) / 128), unsigned(B * Hq));
+  kivi_gemv_kernel<<<grid, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "kivi_gemv_kernel launch");
+}
+
+}  // extern "C"
