@@ -29,16 +29,28 @@ I = ctypes.c_int
 F = ctypes.c_float
 
 
-def rows_aligned(t, align=16):
-    """Return t, or a contiguous copy when its rows are not `align`-byte addressable."""
+def _is_rows_aligned(t, align):
     es = t.element_size()
-    ok = t.data_ptr() % align == 0 and (t.dim() == 0 or t.stride(-1) == 1 or t.shape[-1] <= 1)
-    if ok:
-        for i in range(t.dim() - 1):
-            if t.shape[i] > 1 and (t.stride(i) * es) % align:
-                ok = False
-                break
-    return t if ok else t.contiguous()
+    if t.data_ptr() % align or not (t.dim() == 0 or t.stride(-1) == 1 or t.shape[-1] <= 1):
+        return False
+    return all(t.shape[i] <= 1 or (t.stride(i) * es) % align == 0 for i in range(t.dim() - 1))
+
+
+def rows_aligned(t, align=16):
+    """Return t, or a copy whose rows start on `align`-byte boundaries.
+
+    The copy pads the innermost dim of its storage (the returned view has t's shape),
+    so every leading stride is a multiple of `align` bytes.
+    """
+    if _is_rows_aligned(t, align):
+        return t
+    es = t.element_size()
+    n = t.shape[-1]
+    per = max(1, align // es)
+    n_pad = (n + per - 1) // per * per
+    buf = torch.zeros(tuple(t.shape[:-1]) + (n_pad,), dtype=t.dtype, device=t.device)
+    buf[..., :n] = t
+    return buf[..., :n]
 
 
 def inner_contig(t):
@@ -160,3 +172,130 @@ def kivi_gemv(group_size, fA, qB, scales, zeros, bits):
         int(bits), ctypes.byref(ds[4]), N.stream_of(fA))
     N.check(rc, "bd_kivi_gemv_outer")
     return out
+
+
+def sparse_score(q3, k, scale, zero, scaling, bits, group_size):
+    """q3 [B,Hq,D]; k bf16/fp8 [B,Hk,S,D] or packed u8 -> scores [B,Hq,S] f32."""
+    N.require_cuda(q3, k, scale, zero)
+    k = rows_aligned(k)
+    q3 = inner_contig(q3)
+    B, Hq, D = q3.shape
+    S = k.shape[2]
+    if bits in (2, 4):
+        if scale is None or zero is None:
+            raise ValueError("packed scores need scale and zero")
+        if scale.dtype not in (torch.bfloat16, torch.float16):
+            scale = scale.to(torch.bfloat16)
+            zero = zero.to(torch.bfloat16)
+        scale = scale.contiguous()
+        zero = zero.contiguous()
+    scores = torch.empty(B, Hq, S, dtype=torch.float32, device=q3.device)
+    ds = [N.desc(q3), N.desc(k), N.desc(scale), N.desc(zero), N.desc(scores)]
+    rc = _fn("bd_sparse_score", [P, P, P, P, F, I, I, P, VP])(
+        ctypes.byref(ds[0]), ctypes.byref(ds[1]), N.ref(ds[2]), N.ref(ds[3]), float(scaling), int(bits),
+        int(group_size), ctypes.byref(ds[4]), N.stream_of(q3))
+    N.check(rc, "bd_sparse_score")
+    return scores
+
+
+def pack_score_keys(k, bits, group_size):
+    N.require_cuda(k)
+    k = inner_contig(k)
+    B, H, S, D = k.shape
+    packed = torch.empty(B, H, S, D * bits // 8, dtype=torch.uint8, device=k.device)
+    scale = torch.empty(B, H, S, D // group_size, dtype=k.dtype, device=k.device)
+    zero = torch.empty_like(scale)
+    ds = [N.desc(t) for t in (k, packed, scale, zero)]
+    rc = _fn("bd_pack_score_keys", [P, I, I, P, P, P, VP])(
+        ctypes.byref(ds[0]), int(bits), int(group_size), ctypes.byref(ds[1]), ctypes.byref(ds[2]),
+        ctypes.byref(ds[3]), N.stream_of(k))
+    N.check(rc, "bd_pack_score_keys")
+    return packed, scale, zero
+
+
+def topk(scores, k, sorted=True, want_values=True, idx_dtype=torch.int64):
+    """Top-k over the last dim (lower index wins ties); scores f32 with <= 3 dims."""
+    N.require_cuda(scores)
+    if scores.dtype != torch.float32:
+        scores = scores.float()
+    lead = scores.shape[:-1]
+    n = scores.shape[-1]
+    s = scores if scores.dim() <= 3 else scores.reshape(-1, n)
+    s = inner_contig(s)
+    idx = torch.empty(tuple(s.shape[:-1]) + (k,), dtype=idx_dtype, device=s.device)
+    vals = torch.empty(tuple(s.shape[:-1]) + (k,), dtype=torch.float32, device=s.device) if want_values else None
+    ds, di, dv = N.desc(s), N.desc(idx), N.desc(vals)
+    rc = _fn("bd_topk", [P, I, I, P, P, VP])(ctypes.byref(ds), int(k), int(bool(sorted)), N.ref(dv), ctypes.byref(di),
+                                             N.stream_of(s))
+    N.check(rc, "bd_topk")
+    idx = idx.reshape(tuple(lead) + (k,))
+    return (vals.reshape(tuple(lead) + (k,)) if vals is not None else None), idx
+
+
+def gather_attn(q3, k, v, idx, scaling, out):
+    N.require_cuda(q3, k, v, idx, out)
+    k, v = rows_aligned(k), rows_aligned(v)
+    q3 = inner_contig(q3)
+    idx = inner_contig(idx)
+    if idx.dtype not in (torch.int32, torch.int64):
+        idx = idx.long()
+    dq, di = N.desc(q3), N.desc(idx)
+    nws = _fn("bd_sparse_gather_attn_workspace", [P, P], SZ)(ctypes.byref(dq), ctypes.byref(di))
+    buf, nb = _ws(nws, q3.device)
+    dk, dv, do = N.desc(k), N.desc(v), N.desc(out)
+    rc = _fn("bd_sparse_gather_attn", [P, P, P, P, F, P, VP, SZ, VP])(
+        ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(di), float(scaling), ctypes.byref(do),
+        _ptr(buf), nb, N.stream_of(q3))
+    N.check(rc, "bd_sparse_gather_attn")
+    return out
+
+
+def quest_page_minmax(k, page):
+    N.require_cuda(k)
+    k = inner_contig(k)
+    B, H, S, D = k.shape
+    np_ = (S + page - 1) // page
+    kmin = torch.empty(B, H, np_, D, dtype=k.dtype, device=k.device)
+    kmax = torch.empty_like(kmin)
+    dk, dmn, dmx = N.desc(k), N.desc(kmin), N.desc(kmax)
+    rc = _fn("bd_quest_page_minmax", [P, I, P, P, VP])(ctypes.byref(dk), int(page), ctypes.byref(dmn),
+                                                       ctypes.byref(dmx), N.stream_of(k))
+    N.check(rc, "bd_quest_page_minmax")
+    return kmin, kmax
+
+
+def quest_page_bounds(q3, kmin, kmax, scaling, force_from_page=None):
+    N.require_cuda(q3, kmin, kmax)
+    q3 = inner_contig(q3)
+    kmin = rows_aligned(kmin.to(torch.bfloat16))
+    kmax = rows_aligned(kmax.to(torch.bfloat16))
+    B, Hq, _ = q3.shape
+    np_ = kmin.shape[2]
+    bounds = torch.empty(B, Hq, np_, dtype=torch.float32, device=q3.device)
+    ff = np_ if force_from_page is None else int(force_from_page)
+    ds = [N.desc(t) for t in (q3, kmin, kmax, bounds)]
+    rc = _fn("bd_quest_page_bounds", [P, P, P, F, I, P, VP])(
+        ctypes.byref(ds[0]), ctypes.byref(ds[1]), ctypes.byref(ds[2]), float(scaling), ff, ctypes.byref(ds[3]),
+        N.stream_of(q3))
+    N.check(rc, "bd_quest_page_bounds")
+    return bounds
+
+
+def quest_select(q3, kmin, kmax, S, kb, page, scaling, force_from_page=None, idx_dtype=torch.int64):
+    N.require_cuda(q3, kmin, kmax)
+    q3 = inner_contig(q3)
+    kmin = rows_aligned(kmin.to(torch.bfloat16))
+    kmax = rows_aligned(kmax.to(torch.bfloat16))
+    B, Hq, _ = q3.shape
+    np_ = kmin.shape[2]
+    npick = min(max(1, (kb + page - 1) // page), np_)
+    idx = torch.empty(B, Hq, npick * page, dtype=idx_dtype, device=q3.device)
+    ff = np_ if force_from_page is None else int(force_from_page)
+    dq, dmn, dmx, di = N.desc(q3), N.desc(kmin), N.desc(kmax), N.desc(idx)
+    nws = _fn("bd_quest_select_workspace", [P, P, I, I], SZ)(ctypes.byref(dq), ctypes.byref(dmn), int(kb), int(page))
+    buf, nb = _ws(nws, q3.device)
+    rc = _fn("bd_quest_select", [P, P, P, I, I, I, F, I, P, VP, SZ, VP])(
+        ctypes.byref(dq), ctypes.byref(dmn), ctypes.byref(dmx), int(S), int(kb), int(page), float(scaling), ff,
+        ctypes.byref(di), _ptr(buf), nb, N.stream_of(q3))
+    N.check(rc, "bd_quest_select")
+    return idx

@@ -38,3 +38,85 @@ def decode_attn_fp8(q, k, v):
     out = torch.empty(q3.shape, dtype=q.dtype, device=q.device)
     _ops.decode_attn(q3, k, v, 1.0, out)
     return out.unsqueeze(2)
+
+
+def sparse_score_scalar(q, k_score, scaling, *, score_bits=16, BLOCK_N=128):
+    """Pass-1 exact scores [B,H_q,S] fp32 = scaling * q.k over bf16 (16) or fp8 (8) keys.
+
+    ref: src/attention_kernels.py:1113-1133.
+    """
+    q3 = _squeeze_q(q)
+    if score_bits == 16:
+        if k_score.dtype != torch.bfloat16:
+            raise ValueError("score_bits=16 expects bf16 keys")
+        if q3.dtype != torch.bfloat16:
+            q3 = q3.to(torch.bfloat16)
+    elif score_bits == 8:
+        if k_score.dtype != torch.float8_e4m3fn:
+            raise ValueError("score_bits=8 expects fp8 e4m3 keys")
+    else:
+        raise ValueError("Unsupported score_bits")
+    return _ops.sparse_score(q3, k_score, None, None, scaling, score_bits, 32)
+
+
+def sparse_score_packed(q, k_packed, scale, zero, scaling, *, score_bits=4, group_size=32, BLOCK_N=128):
+    """Pass-1 scores [B,H_q,S] fp32 from uint8-packed 2/4-bit keys (k = code*scale + zero).
+
+    ref: src/attention_kernels.py:1136-1222.
+    """
+    if score_bits not in (2, 4):
+        raise ValueError("Unsupported score_bits")
+    return _ops.sparse_score(_squeeze_q(q), k_packed, scale, zero, scaling, score_bits, group_size)
+
+
+def quantize_and_pack_score_keys(k, score_bits, group_size):
+    """Per-token groups of `group_size` channels -> (packed uint8, scale, zero) in k.dtype.
+
+    ref: src/attention_kernels.py:1225-1249 (bit-exact: fp32 min/max, IEEE divide,
+    round-half-even, low bits first).
+    """
+    if score_bits not in (2, 4):
+        raise ValueError("Unsupported score_bits")
+    return _ops.pack_score_keys(k, score_bits, group_size)
+
+
+def sparse_gather_attn(q, k, v, idx, scaling, BLOCK_K=64):
+    """Exact softmax attention over gathered key positions idx [B,H_q,kb].
+
+    ref: src/attention_kernels.py:1037-1059. Output bf16 for fp8 V, else v.dtype.
+    Positions outside [0, S) are skipped (the reference kernel reads them unchecked).
+    """
+    q3 = _squeeze_q(q)
+    out_dtype = torch.bfloat16 if v.dtype == torch.float8_e4m3fn else v.dtype
+    out = torch.empty(q3.shape, dtype=out_dtype, device=q.device)
+    _ops.gather_attn(q3, k, v, idx, scaling, out)
+    return out.unsqueeze(2)
+
+
+def _budget(frac, S):
+    return max(1, int(round(frac * S)))
+
+
+def sparse_decode_scalar(q, k_score_or_packed, scale, zero, k_val, v_val, frac, scaling, *, score_bits,
+                         group_size=32, BLOCK_N=128, BLOCK_K=64):
+    """Two-pass sparse decode: score all keys -> top-kb (lower index wins ties) -> gather.
+
+    ref: src/attention_kernels.py:1252-1263. kb = max(1, round(frac*S)).
+    """
+    if score_bits in (16, 8):
+        scores = sparse_score_scalar(q, k_score_or_packed, scaling, score_bits=score_bits)
+    else:
+        scores = sparse_score_packed(q, k_score_or_packed, scale, zero, scaling, score_bits=score_bits,
+                                     group_size=group_size)
+    kb = _budget(frac, scores.shape[-1])
+    _, idx = _ops.topk(scores, kb, sorted=False, want_values=False, idx_dtype=torch.int32)
+    return sparse_gather_attn(q, k_val, v_val, idx, scaling)
+
+
+def topk(scores, k, sorted=True):
+    """Top-k along the last dim; equal values keep the lower index first.
+
+    Replaces ``scores.topk(k)`` (src/attention_kernels.py:1069,1262). Returns
+    (values fp32, indices int64).
+    """
+    return _ops.topk(scores, k, sorted=sorted)

@@ -13,16 +13,18 @@
 //  * A 128-token tile of codes, scales and minima streams into shared memory through a
 //    cp.async pipeline; each of the 4 warps owns 32 tokens = one key group.
 //  * Keys: score = sum_c q_c (code*s_c + m_c) = sum_c (q_c s_c) code + sum_c q_c m_c.
-//    The scale folds into Q' = q*s (f16, per warp per group) and the minimum into a
-//    per-(head, group) bias, so the contraction runs on the tensor cores over raw
-//    codes: S^T[16 tok x 8 heads] += codes[16 x 16] . Q'^T[16 x 8] (mma.sync f16).
-//  * Codes become MMA operands in registers without any shared-memory staging: the
-//    f16 bit pattern 0x6400|c is the value 1024+c, so one shift and one LOP3 per
-//    word yield two f16 operands; the 1024*sum(Q') offset is subtracted once per
-//    group. Register pairs along the contraction dim come from PRMT of two words.
-//  * Values: O^T[16 ch x 8 heads] += codes^T[16 x 16 tok] . P'^T[16 tok x 8], with the
-//    per-token scale folded into P' = P*s_v (one version per 32-channel group) and
-//    the minimum + 1024 offset folded into a per-(head, group) correction.
+//    The scale folds into Q' = q*s (f16, HMUL2 per warp per group), so the contraction
+//    runs on the tensor cores over raw codes: S^T[16 tok x 8 heads] += codes . Q'^T
+//    (mma.sync m16n8k16 f16 -> f32); the per-(head, group) bias sum_c q_c m_c is one
+//    more MMA with the group's minima as the only non-zero A row.
+//  * Codes become MMA operands in registers with no shared-memory staging of unpacked
+//    data: a 2-bit (4-bit) field masked into the low mantissa bits of an f16 is the
+//    exact subnormal code*2^-24, so one shift and one AND per word give two operands;
+//    the 2^24 factor is applied to the fp32 accumulators. Register pairs along the
+//    contraction dim come from one PRMT of two words.
+//  * Values: O^T[16 ch x 8 heads] += codes^T[16 ch x 16 tok] . P'^T[16 tok x 8], with the
+//    per-token scale folded into P' = P*s_v (one version per 32-channel group); the
+//    minima contribute sum_t P_t m_t per (group, head), again one MMA per row block.
 //  * Row/token permutations are chosen so every shared-memory read is conflict-free
 //    and the movmatrix transpose of P lands directly in the PV operand layout.
 //  * The bf16 residual window runs through the dense split kernel into the same
@@ -41,13 +43,13 @@ constexpr int kTile = 128;  // tokens per tile
 constexpr int kStagesK = 3;
 constexpr float kLog2eK = 1.4426950408889634f;
 constexpr float kLn2K = 0.6931471805599453f;
-constexpr uint32_t kMagic = 0x64006400u;  // two f16 1024.0
+constexpr float kSub = 16777216.f;  // 2^24: f16 subnormal code c has value c * 2^-24
 
 template <int BITS>
 struct KL {
   static constexpr int FPI = 32 / BITS;
   static constexpr int KQ_WORDS = kTile / FPI;          // words per channel per tile
-  static constexpr int KQ_PITCH = BITS == 2 ? 32 : 80;  // smem bytes per channel row
+  static constexpr int KQ_PITCH = BITS == 2 ? 48 : 80;  // smem bytes per channel row (padded)
   static constexpr int VQ_WORDS = 128 / FPI;            // words per token (D = 128)
   static constexpr int VQ_PITCH = BITS == 2 ? 32 : 80;
   static constexpr int KQ_BYTES = 128 * KQ_PITCH;
@@ -60,6 +62,7 @@ struct KL {
   static constexpr int OFF_VS = OFF_VQ + VQ_BYTES;
   static constexpr int OFF_VM = OFF_VS + VS_BYTES;
   static constexpr int STAGE = OFF_VM + VS_BYTES;
+  static constexpr int T_BYTES = 2 * 4 * 128 * 2;  // transposed key scale/min [2][4 groups][128 ch] f16
 };
 
 struct KiviParams {
@@ -86,11 +89,14 @@ __device__ __forceinline__ float load_qk(const KiviParams& p, int64_t off) {
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 template <int BITS>
 __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const KiviParams p) {
   using L = KL<BITS>;
   extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* tsm = smem + kStagesK * L::STAGE;  // transposed key scale / min of the current tile
   const int split = blockIdx.x;
   const int hk = blockIdx.y / p.head_chunks;
   const int chunk = blockIdx.y % p.head_chunks;
@@ -102,7 +108,8 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
   const int h0 = chunk * 8;
   const int nheads = min(8, p.G - h0);
-  // QK accumulator row g <-> token rho (row g+8 <-> rho+8) inside a 16-token row block
+  // QK accumulator row g <-> token rho (row g+8 <-> rho+8) inside a 16-token row block;
+  // chosen so that the movmatrix transpose of P is the PV operand for tokens tq+4u.
   const int rho = (g >> 1) + 4 * (g & 1);
 
   const uint32_t* kq_base = p.kq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh;
@@ -112,21 +119,40 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
   const __half* vs_base = p.vs + int64_t(b) * p.vs_sb + int64_t(hk) * p.vs_sh;
   const __half* vm_base = p.vm + int64_t(b) * p.vm_sb + int64_t(hk) * p.vm_sh;
 
-  // query (fp32) for head g, channels tq + 4i
-  float qf[32];
+  // query of head g as f16 pairs in MMA k order: qh[j][0] = channels 16j+2tq,+1;
+  // qh[j][1] = 16j+8+2tq,+1. A power-of-two pre-scale keeps |q| <= 2^8 in f16.
+  uint32_t qh[8][2];
+  float score_mul = p.scale_log2;
   {
     const bool ok = g < nheads;
     const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? g : 0)) * p.q_sh;
+    float qv[8][4];
+    float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) qf[i] = ok ? load_qk(p, qoff + tq + 4 * i) : 0.f;
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qv[j][e] = ok ? load_qk(p, qoff + 16 * j + 2 * tq + (e & 1) + (e >> 1) * 8) : 0.f;
+        amax = fmaxf(amax, fabsf(qv[j][e]));
+      }
+    amax = warp_max(amax);
+    int ex = 0;
+    frexpf(amax, &ex);
+    const int shift = ex > 8 ? ex - 8 : 0;
+    const float qs = ldexpf(1.f, -shift);
+    score_mul = ldexpf(p.scale_log2, shift);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      qh[j][0] = pack_f16x2(qv[j][0] * qs, qv[j][1] * qs);
+      qh[j][1] = pack_f16x2(qv[j][2] * qs, qv[j][3] * qs);
+    }
   }
 
   const int words_end = (t_end + L::FPI - 1) / L::FPI;  // first word index past the split
   const int groups_end = (t_end + 31) / 32;
   auto load_tile = [&](int tile, int stage) {
     const int t0 = t_begin + tile * kTile;
-    uint8_t* st = smem + stage * L::STAGE;
-    const uint32_t sbase = smem_u32(st);
+    const uint32_t sbase = smem_u32(smem + stage * L::STAGE);
     constexpr int NCH = L::KQ_WORDS / 4;  // 16-byte chunks per channel row
     for (int c = threadIdx.x; c < 128 * NCH; c += kWarpsK * 32) {
       const int row = c / NCH, ck = c % NCH;
@@ -162,9 +188,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
   float o[8][4];
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-  float corr[2][4];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) corr[j][0] = corr[j][1] = corr[j][2] = corr[j][3] = 0.f;
+  float cacc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g<4: sum_t P_t * m_v[t][group g], heads 2tq,2tq+1
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
 #pragma unroll
@@ -182,40 +206,41 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
       cp_async_commit();
     }
     const uint8_t* st = smem + (it % kStagesK) * L::STAGE;
+    {
+      // transpose key scale / min of this tile to [group][channel] (one channel per thread)
+      const uint2 s4 = *reinterpret_cast<const uint2*>(st + L::OFF_KS + threadIdx.x * 8);
+      const uint2 m4 = *reinterpret_cast<const uint2*>(st + L::OFF_KM + threadIdx.x * 8);
+      uint16_t* ts = reinterpret_cast<uint16_t*>(tsm);
+      ts[0 * 128 + threadIdx.x] = uint16_t(s4.x); ts[1 * 128 + threadIdx.x] = uint16_t(s4.x >> 16);
+      ts[2 * 128 + threadIdx.x] = uint16_t(s4.y); ts[3 * 128 + threadIdx.x] = uint16_t(s4.y >> 16);
+      ts[4 * 128 + threadIdx.x] = uint16_t(m4.x); ts[5 * 128 + threadIdx.x] = uint16_t(m4.x >> 16);
+      ts[6 * 128 + threadIdx.x] = uint16_t(m4.y); ts[7 * 128 + threadIdx.x] = uint16_t(m4.y >> 16);
+    }
+    __syncthreads();
     const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
     if (tb >= t_end) continue;
 
-    // ---- Q' = q * s_k (f16) and the per-head bias sum_c q_c m_c - 1024 sum_c Q'_c
+    // ---- Q' = q * s_k (f16) and bias = sum_c q_c m_c (one MMA chain, minima in A row 0)
     uint32_t qb[8][2];
     float bb0, bb1;
     {
-      const __half* ksr = reinterpret_cast<const __half*>(st + L::OFF_KS);
-      const __half* kmr = reinterpret_cast<const __half*>(st + L::OFF_KM);
-      float sumq = 0.f, bias = 0.f;
+      const uint8_t* tsr = tsm + warp * 256;         // scales of group `warp`
+      const uint8_t* tmr = tsm + (4 + warp) * 256;   // minima of group `warp`
+      float bacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        __half hh[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = 4 * j + e;
-          const int c = tq + 4 * i;
-          const float s = __half2float(ksr[c * 4 + warp]);
-          const float m = __half2float(kmr[c * 4 + warp]);
-          hh[e] = __float2half_rn(qf[i] * s);
-          sumq += __half2float(hh[e]);
-          bias = fmaf(qf[i], m, bias);
-        }
-        qb[j][0] = h2u(__halves2half2(hh[0], hh[1]));
-        qb[j][1] = h2u(__halves2half2(hh[2], hh[3]));
+        const int c0 = 16 * j + 2 * tq;
+        qb[j][0] = h2u(__hmul2(u2h(qh[j][0]), u2h(lds_u32(tsr + c0 * 2))));
+        qb[j][1] = h2u(__hmul2(u2h(qh[j][1]), u2h(lds_u32(tsr + (c0 + 8) * 2))));
+        const uint32_t m01 = g == 0 ? lds_u32(tmr + c0 * 2) : 0u;
+        const uint32_t m89 = g == 0 ? lds_u32(tmr + (c0 + 8) * 2) : 0u;
+        mma_f16(bacc, m01, 0u, m89, 0u, qh[j][0], qh[j][1]);
       }
-      float be = bias - 1024.f * sumq;
-      be += __shfl_xor_sync(0xffffffffu, be, 1);
-      be += __shfl_xor_sync(0xffffffffu, be, 2);
-      bb0 = __shfl_sync(0xffffffffu, be, (2 * tq) * 4);
-      bb1 = __shfl_sync(0xffffffffu, be, (2 * tq + 1) * 4);
+      bb0 = __shfl_sync(0xffffffffu, bacc[0], tq);
+      bb1 = __shfl_sync(0xffffffffu, bacc[1], tq);
     }
 
-    // ---- S^T for the warp's two 16-token row blocks
+    // ---- S^T (scaled by 2^-24) for the warp's two 16-token row blocks
     float s[2][4];
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) s[rb][0] = s[rb][1] = s[rb][2] = s[rb][3] = 0.f;
@@ -224,27 +249,23 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
       uint32_t U[2][4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int c = 16 * j + tq + 4 * e;
+        const int c = 16 * j + 2 * tq + (e & 1) + (e >> 1) * 8;
         if (BITS == 2) {
           const uint2 w2 = *reinterpret_cast<const uint2*>(st + c * L::KQ_PITCH + warp * 8);
-          U[0][e] = ((w2.x >> (2 * rho)) & 0x00030003u) | kMagic;
-          U[1][e] = ((w2.y >> (2 * rho)) & 0x00030003u) | kMagic;
+          U[0][e] = (w2.x >> (2 * rho)) & 0x00030003u;
+          U[1][e] = (w2.y >> (2 * rho)) & 0x00030003u;
         } else {
           const uint4 w4 = *reinterpret_cast<const uint4*>(st + c * L::KQ_PITCH + warp * 16);
           const uint32_t sel = rho < 4 ? 0x5410u : 0x7632u;
           const int sh = 4 * (rho & 3);
-          U[0][e] = ((prmt(w4.x, w4.y, sel) >> sh) & 0x000F000Fu) | kMagic;
-          U[1][e] = ((prmt(w4.z, w4.w, sel) >> sh) & 0x000F000Fu) | kMagic;
+          U[0][e] = (prmt(w4.x, w4.y, sel) >> sh) & 0x000F000Fu;
+          U[1][e] = (prmt(w4.z, w4.w, sel) >> sh) & 0x000F000Fu;
         }
       }
 #pragma unroll
-      for (int rb = 0; rb < 2; ++rb) {
-        const uint32_t a0 = prmt(U[rb][0], U[rb][1], 0x5410u);
-        const uint32_t a1 = prmt(U[rb][0], U[rb][1], 0x7632u);
-        const uint32_t a2 = prmt(U[rb][2], U[rb][3], 0x5410u);
-        const uint32_t a3 = prmt(U[rb][2], U[rb][3], 0x7632u);
-        mma_f16(s[rb], a0, a1, a2, a3, qb[j][0], qb[j][1]);
-      }
+      for (int rb = 0; rb < 2; ++rb)
+        mma_f16(s[rb], prmt(U[rb][0], U[rb][1], 0x5410u), prmt(U[rb][0], U[rb][1], 0x7632u),
+                prmt(U[rb][2], U[rb][3], 0x5410u), prmt(U[rb][2], U[rb][3], 0x7632u), qb[j][0], qb[j][1]);
     }
 
     // ---- online softmax over the 32 tokens (exp2 domain)
@@ -257,8 +278,8 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
           const int tr = tb + 16 * rb + rho;
-          x[2 * rb] = tr < t_end ? (s[rb][j] + bbj[j]) * p.scale_log2 : -INFINITY;
-          x[2 * rb + 1] = tr + 8 < t_end ? (s[rb][2 + j] + bbj[j]) * p.scale_log2 : -INFINITY;
+          x[2 * rb] = tr < t_end ? fmaf(s[rb][j], kSub, bbj[j]) * score_mul : -INFINITY;
+          x[2 * rb + 1] = tr + 8 < t_end ? fmaf(s[rb][2 + j], kSub, bbj[j]) * score_mul : -INFINITY;
         }
         float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
@@ -281,40 +302,39 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
           o[mt][j] *= alpha;
           o[mt][2 + j] *= alpha;
         }
-#pragma unroll
-        for (int gr = 0; gr < 4; ++gr) corr[j][gr] *= alpha;
+        cacc[j] *= alpha;
+        cacc[2 + j] *= alpha;
       }
     }
 
-    // ---- P' = P * s_v per group, PV on the tensor cores
+    // ---- P' = P * s_v per group; PV and the value-minimum term on the tensor cores
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) {
       const int tl = 32 * warp + 16 * rb;  // tile-local first token of the row block
       uint32_t pb[4][2];
+      const uint32_t hp0 = pack_f16x2(pv[rb][0], pv[rb][1]);
+      const uint32_t hp1 = pack_f16x2(pv[rb][2], pv[rb][3]);
       {
         const uint2 vs0 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tl + rho) * 8);
         const uint2 vs1 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tl + rho + 8) * 8);
-        const uint2 vm0 = *reinterpret_cast<const uint2*>(st + L::OFF_VM + (tl + rho) * 8);
-        const uint2 vm1 = *reinterpret_cast<const uint2*>(st + L::OFF_VM + (tl + rho + 8) * 8);
-        const uint32_t hp0 = pack_f16x2(pv[rb][0], pv[rb][1]);
-        const uint32_t hp1 = pack_f16x2(pv[rb][2], pv[rb][3]);
         const uint32_t s0w[2] = {vs0.x, vs0.y}, s1w[2] = {vs1.x, vs1.y};
-        const uint32_t m0w[2] = {vm0.x, vm0.y}, m1w[2] = {vm1.x, vm1.y};
 #pragma unroll
         for (int gr = 0; gr < 4; ++gr) {
           const uint32_t sel = (gr & 1) ? 0x3232u : 0x1010u;  // broadcast one f16 to both halves
-          const __half2 sc0 = u2h(prmt(s0w[gr >> 1], 0, sel));
-          const __half2 sc1 = u2h(prmt(s1w[gr >> 1], 0, sel));
-          const __half2 q0 = __hmul2(u2h(hp0), sc0);
-          const __half2 q1 = __hmul2(u2h(hp1), sc1);
-          pb[gr][0] = movmatrix_trans(h2u(q0));
-          pb[gr][1] = movmatrix_trans(h2u(q1));
-          const float2 f0 = __half22float2(q0), f1 = __half22float2(q1);
-          const float mn0 = __half2float(__low2half(u2h(prmt(m0w[gr >> 1], 0, sel))));
-          const float mn1 = __half2float(__low2half(u2h(prmt(m1w[gr >> 1], 0, sel))));
-          corr[0][gr] += pv[rb][0] * mn0 + pv[rb][2] * mn1 - 1024.f * (f0.x + f1.x);
-          corr[1][gr] += pv[rb][1] * mn0 + pv[rb][3] * mn1 - 1024.f * (f0.y + f1.y);
+          pb[gr][0] = movmatrix_trans(h2u(__hmul2(u2h(hp0), u2h(prmt(s0w[gr >> 1], 0, sel)))));
+          pb[gr][1] = movmatrix_trans(h2u(__hmul2(u2h(hp1), u2h(prmt(s1w[gr >> 1], 0, sel)))));
         }
+      }
+      {
+        // value minima: A rows = groups (g < 4), k = tokens tq, tq+4 | tq+8, tq+12
+        const uint32_t pt0 = movmatrix_trans(hp0), pt1 = movmatrix_trans(hp1);
+        uint32_t a0 = 0u, a2 = 0u;
+        if (g < 4) {
+          const uint8_t* vmr = st + L::OFF_VM + 2 * g;
+          a0 = lds_u16(vmr + (tl + tq) * 8) | (lds_u16(vmr + (tl + tq + 4) * 8) << 16);
+          a2 = lds_u16(vmr + (tl + tq + 8) * 8) | (lds_u16(vmr + (tl + tq + 12) * 8) << 16);
+        }
+        mma_f16(cacc, a0, 0u, a2, 0u, pt0, pt1);
       }
       // value codes of tokens tl + tq + 4u, u = 0..3
       if (BITS == 2) {
@@ -331,7 +351,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
         for (int mt = 0; mt < 8; ++mt) {
           uint32_t Uu[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) Uu[u] = ((W[u][mt] >> (2 * g)) & 0x00030003u) | kMagic;
+          for (int u = 0; u < 4; ++u) Uu[u] = (W[u][mt] >> (2 * g)) & 0x00030003u;
           mma_f16(o[mt], prmt(Uu[0], Uu[1], 0x5410u), prmt(Uu[0], Uu[1], 0x7632u), prmt(Uu[2], Uu[3], 0x5410u),
                   prmt(Uu[2], Uu[3], 0x7632u), pb[mt >> 1][0], pb[mt >> 1][1]);
         }
@@ -356,7 +376,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const uint32_t w = hiw ? W[u][2 * ml + 1] : W[u][2 * ml];
-              Uu[u] = ((w >> sh) & 0x000F000Fu) | kMagic;
+              Uu[u] = (w >> sh) & 0x000F000Fu;
             }
             mma_f16(o[mt], prmt(Uu[0], Uu[1], 0x5410u), prmt(Uu[0], Uu[1], 0x7632u),
                     prmt(Uu[2], Uu[3], 0x5410u), prmt(Uu[2], Uu[3], 0x7632u), pb[mt >> 1][0], pb[mt >> 1][1]);
@@ -374,14 +394,13 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
     l += __shfl_xor_sync(0xffffffffu, l, 8);
     l += __shfl_xor_sync(0xffffffffu, l, 16);
     lrow[j] = l;
+  }
+  // value-minimum term of group gr for heads 2tq+j lives in lane (gr, tq)
+  float corr[4][2];
 #pragma unroll
-    for (int gr = 0; gr < 4; ++gr) {
-      float c = corr[j][gr];
-      c += __shfl_xor_sync(0xffffffffu, c, 4);
-      c += __shfl_xor_sync(0xffffffffu, c, 8);
-      c += __shfl_xor_sync(0xffffffffu, c, 16);
-      corr[j][gr] = c;
-    }
+  for (int gr = 0; gr < 4; ++gr) {
+    corr[gr][0] = __shfl_sync(0xffffffffu, cacc[0], gr * 4 + tq);
+    corr[gr][1] = __shfl_sync(0xffffffffu, cacc[1], gr * 4 + tq);
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -408,8 +427,8 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
       int ca, cb;
       if (BITS == 2) { ca = 16 * mt + g; cb = ca + 8; }
       else { ca = 16 * mt + (g < 4 ? g : g + 4); cb = ca + 4; }
-      red_o[(warp * 8 + h) * 128 + ca] = (o[mt][j] + corr[j][mt >> 1]) * f;
-      red_o[(warp * 8 + h) * 128 + cb] = (o[mt][2 + j] + corr[j][mt >> 1]) * f;
+      red_o[(warp * 8 + h) * 128 + ca] = fmaf(o[mt][j], kSub, corr[mt >> 1][j]) * f;
+      red_o[(warp * 8 + h) * 128 + cb] = fmaf(o[mt][2 + j], kSub, corr[mt >> 1][j]) * f;
     }
   }
   __syncthreads();
@@ -438,7 +457,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const Kivi
 template <int BITS>
 int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
   using L = KL<BITS>;
-  const size_t smem = std::max<size_t>(size_t(kStagesK) * L::STAGE, (2 * 4 * 8 + 4 * 8 * 128) * sizeof(float));
+  const size_t smem = std::max<size_t>(size_t(kStagesK) * L::STAGE + L::T_BYTES, (2 * 4 * 8 + 4 * 8 * 128) * sizeof(float));
   auto kern = kivi_decode_kernel<BITS>;
   static bool attr[64] = {false};
   int dev = 0;

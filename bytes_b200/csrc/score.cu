@@ -1,0 +1,532 @@
+// Pass-1 score kernels of the two-pass sparse decode and the score-key packer.
+//
+// Follows src/attention_kernels.py of the reference (saifmb0/bytes):
+//   sparse_score_scalar  (:1077-1133)  scores = scaling * q.k over bf16 / fp8 keys
+//   sparse_score_packed  (:1136-1222)  k = code*scale + zero from uint8-packed 2/4-bit
+//                                      keys, per-token groups of `group_size` channels
+//   quantize_and_pack_score_keys (:1225-1249)
+// Output scores [B,Hq,S] fp32.
+//
+// Design: one CTA per (batch, KV head, head chunk, token split); K tiles stream into
+// shared memory (cp.async, 3 stages); all G query heads of the KV head are scored from
+// the same tile on the tensor cores (S^T[16 tok x 8 heads] = K . Q^T, mma.sync). Packed
+// codes are unpacked in registers as exact f16 subnormals (code*2^-24): one shift and one
+// AND give two MMA operands. Per-token scale/zero enter in fp32 after the contraction:
+// score = sum_g s_g * (sum_{c in g} q_c code_c) + z_g * (sum_{c in g} q_c).
+#include "common.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace bd {
+namespace {
+
+constexpr int kSW = 4;         // warps per CTA
+constexpr int kSStages = 3;
+constexpr float kSub = 16777216.f;
+
+// KT: 16 = bf16 keys, 8 = fp8 keys, 4 / 2 = packed bits
+template <int KT, int D>
+struct SL {
+  static constexpr int RB = KT == 16 ? 1 : (KT == 8 ? 2 : 4);  // 16-token row blocks per warp per tile
+  static constexpr int TILE = 16 * kSW * RB;
+  static constexpr int ROWB = KT == 16 ? D * 2 : (KT == 8 ? D : D * KT / 8);
+  // packed rows are read by 8 lanes at a time with 16-byte loads: pitches chosen conflict-free
+  static constexpr int PITCH = (KT == 16 || KT == 8) ? ROWB + 16 : (ROWB == 16 ? 16 : (ROWB == 32 ? 48 : 80));
+  static constexpr int KBYTES = TILE * PITCH;
+  static constexpr int SZB = (KT == 16 || KT == 8) ? 0 : TILE * (D / 16) * 2;  // scale tile, worst case gs=16
+  static constexpr int STAGE = KBYTES + 2 * SZB;
+};
+
+struct ScoreParams {
+  const void* q; int64_t q_sb, q_sh; int q_dtype;
+  const uint8_t* k; int64_t k_sb, k_sh, k_ss;  // strides in elements of k's dtype (bytes for packed/fp8)
+  const uint16_t* sc; int64_t sc_sb, sc_sh, sc_ss;  // scale (bf16/f16 bits) [B,Hk,S,D/gs]
+  const uint16_t* zr; int64_t zr_sb, zr_sh, zr_ss;
+  int sz_bf16;
+  int gs;  // group size (packed only)
+  float* out; int64_t o_sb, o_sh;
+  int B, Hq, Hk, G, S;
+  int head_chunks, heads_per_chunk, tiles_per_split;
+  float scaling;
+};
+
+__device__ __forceinline__ float load_qs(const ScoreParams& p, int64_t off) {
+  switch (p.q_dtype) {
+    case BD_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[off]);
+    case BD_F16: return __half2float(reinterpret_cast<const __half*>(p.q)[off]);
+    default: return reinterpret_cast<const float*>(p.q)[off];
+  }
+}
+__device__ __forceinline__ float h16_to_f(uint16_t u, int is_bf16) {
+  return is_bf16 ? __uint_as_float(uint32_t(u) << 16) : __half2float(__ushort_as_half(u));
+}
+
+template <int KT, int D, int NT>
+__global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p) {
+  using L = SL<KT, D>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int KSTEPS = D / 16;
+  constexpr int NGMAX = D / 16;  // max groups (gs >= 16)
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y / p.head_chunks;
+  const int chunk = blockIdx.y % p.head_chunks;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int t_begin = split * p.tiles_per_split * L::TILE;
+  const int t_end = min(p.S, t_begin + p.tiles_per_split * L::TILE);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + L::TILE - 1) / L::TILE : 0;
+  const int h0 = chunk * p.heads_per_chunk;
+  const int nheads = min(p.heads_per_chunk, p.G - h0);
+  const uint8_t* kbase = p.k + (int64_t(b) * p.k_sb + int64_t(hk) * p.k_sh) * (KT == 16 ? 2 : 1);
+
+  // ---- B fragments (query), channel order depends on the key layout
+  uint32_t qb[KSTEPS][NT][2];
+  float score_mul = p.scaling;
+  float qsum[NGMAX][NT][2];  // packed keys: per-group sum of the f16 query, heads 2tq,2tq+1
+  {
+    float qv[KSTEPS][NT][4];
+    float amax = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int hl = nt * 8 + g;
+        const bool ok = hl < nheads;
+        const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? hl : 0)) * p.q_sh;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int c;
+          if (KT == 16) c = kk * 16 + 2 * tq + (e & 1) + (e >> 1) * 8;  // ldmatrix order
+          else if (KT == 8) c = kk * 16 + 4 * tq + e;                    // fp8 byte order
+          else if (KT == 2) c = kk * 16 + tq + 8 * (e & 1) + 4 * (e >> 1);  // fields tq, tq+8 | tq+4, tq+12
+          else c = kk * 16 + tq + 4 * (e & 1) + 8 * (e >> 1);             // fields tq, tq+4 | 8+tq, 12+tq
+          qv[kk][nt][e] = ok ? load_qs(p, qoff + c) : 0.f;
+          amax = fmaxf(amax, fabsf(qv[kk][nt][e]));
+        }
+      }
+    float qs = 1.f;
+    if (KT != 16) {
+      amax = warp_max(amax);
+      int ex = 0;
+      frexpf(amax, &ex);
+      const int shift = ex > 14 ? ex - 14 : 0;
+      qs = ldexpf(1.f, -shift);
+      score_mul = ldexpf(p.scaling, shift);
+    }
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (KT == 16) {
+          qb[kk][nt][0] = pack_bf16x2(qv[kk][nt][0], qv[kk][nt][1]);
+          qb[kk][nt][1] = pack_bf16x2(qv[kk][nt][2], qv[kk][nt][3]);
+        } else {
+          qb[kk][nt][0] = pack_f16x2(qv[kk][nt][0] * qs, qv[kk][nt][1] * qs);
+          qb[kk][nt][1] = pack_f16x2(qv[kk][nt][2] * qs, qv[kk][nt][3] * qs);
+        }
+      }
+    if (KT == 2 || KT == 4) {
+      // per-group sums of the f16 query for heads 2tq, 2tq+1: lane (g,tq) sums its 4
+      // channels of head g per k-step, reduce over tq, then fetch heads 2tq(+1).
+      float part[KSTEPS][NT];
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float2 a = __half22float2(*reinterpret_cast<__half2*>(&qb[kk][nt][0]));
+          const float2 c = __half22float2(*reinterpret_cast<__half2*>(&qb[kk][nt][1]));
+          float v = (a.x + a.y) + (c.x + c.y);
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          part[kk][nt] = v;  // sum over the 16 channels of k-step kk, head g (+nt*8)
+        }
+      const int kpg = p.gs / 16;  // k-steps per group
+#pragma unroll
+      for (int gi = 0; gi < NGMAX; ++gi)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float v = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < KSTEPS; ++kk)
+            if (kk / kpg == gi) v += part[kk][nt];
+          qsum[gi][nt][0] = __shfl_sync(0xffffffffu, v, (2 * tq) * 4);
+          qsum[gi][nt][1] = __shfl_sync(0xffffffffu, v, (2 * tq + 1) * 4);
+        }
+    }
+  }
+
+  const int ngroups = (KT == 2 || KT == 4) ? D / p.gs : 0;
+  const uint8_t* scb = (KT == 2 || KT == 4)
+      ? reinterpret_cast<const uint8_t*>(p.sc + int64_t(b) * p.sc_sb + int64_t(hk) * p.sc_sh) : nullptr;
+  const uint8_t* zrb = (KT == 2 || KT == 4)
+      ? reinterpret_cast<const uint8_t*>(p.zr + int64_t(b) * p.zr_sb + int64_t(hk) * p.zr_sh) : nullptr;
+  auto load_tile = [&](int tile, int stage) {
+    const int t0 = t_begin + tile * L::TILE;
+    const uint32_t ks = smem_u32(smem + stage * L::STAGE);
+    constexpr int CH = L::ROWB / 16;
+    for (int c = threadIdx.x; c < L::TILE * CH; c += kSW * 32) {
+      const int r = c / CH, cc = c % CH;
+      const int t = t0 + r;
+      const bool ok = t < t_end;
+      const int64_t rowoff = int64_t(ok ? t : t_begin) * p.k_ss * (KT == 16 ? 2 : 1);
+      cp_async16(ks + r * L::PITCH + cc * 16, kbase + rowoff + cc * 16, ok ? 16 : 0);
+    }
+    if (KT == 2 || KT == 4) {
+      // scale / zero rows of this tile are one contiguous block (token-major, ngroups f16 each)
+      const int bytes_tile = L::TILE * ngroups * 2;
+      const int64_t off0 = int64_t(t0) * ngroups * 2;
+      const int64_t lim = int64_t(t_end) * ngroups * 2;
+      for (int c = threadIdx.x; c < bytes_tile / 16; c += kSW * 32) {
+        const int64_t off = off0 + c * 16;
+        const int64_t rem = lim - off;
+        const int valid = rem <= 0 ? 0 : (rem >= 16 ? 16 : int(rem));
+        cp_async16(ks + L::KBYTES + c * 16, scb + (valid ? off : 0), valid);
+        cp_async16(ks + L::KBYTES + L::SZB + c * 16, zrb + (valid ? off : 0), valid);
+      }
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < kSStages - 1; ++s) {
+    if (s < ntiles) load_tile(s, s);
+    cp_async_commit();
+  }
+
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait<kSStages - 2>();
+    __syncthreads();
+    {
+      const int nxt = it + kSStages - 1;
+      if (nxt < ntiles) load_tile(nxt, nxt % kSStages);
+      cp_async_commit();
+    }
+    const uint8_t* st = smem + (it % kSStages) * L::STAGE;
+    const uint32_t ks = smem_u32(st);
+    const uint16_t* ssc = reinterpret_cast<const uint16_t*>(st + L::KBYTES);
+    const uint16_t* szr = reinterpret_cast<const uint16_t*>(st + L::KBYTES + L::SZB);
+#pragma unroll
+    for (int rb = 0; rb < L::RB; ++rb) {
+      const int r0 = (warp * L::RB + rb) * 16;  // tile-local first row
+      const int t0 = t_begin + it * L::TILE + r0;
+      if (t0 >= t_end) break;
+      float acc[NGMAX][NT][4];
+#pragma unroll
+      for (int gi = 0; gi < NGMAX; ++gi)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[gi][nt][0] = acc[gi][nt][1] = acc[gi][nt][2] = acc[gi][nt][3] = 0.f;
+      if (KT == 16) {
+        const int arow = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(a0, a1, a2, a3, ks + arow * L::PITCH + (kk * 16 + (lane >> 4) * 8) * 2);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_bf16(acc[0][nt], a0, a1, a2, a3, qb[kk][nt][0], qb[kk][nt][1]);
+        }
+      } else if (KT == 8) {
+        const int arow = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int k2 = 0; k2 < KSTEPS / 2; ++k2) {
+          uint32_t r0_, r1_, r2_, r3_;
+          ldmatrix_x4(r0_, r1_, r2_, r3_, ks + arow * L::PITCH + k2 * 32 + (lane >> 4) * 16);
+          const uint32_t x0 = e4m3x2_to_f16x2(r0_), x1 = e4m3x2_to_f16x2(r1_);
+          const uint32_t x2 = e4m3x2_to_f16x2(r0_ >> 16), x3 = e4m3x2_to_f16x2(r1_ >> 16);
+          const uint32_t y0 = e4m3x2_to_f16x2(r2_), y1 = e4m3x2_to_f16x2(r3_);
+          const uint32_t y2 = e4m3x2_to_f16x2(r2_ >> 16), y3 = e4m3x2_to_f16x2(r3_ >> 16);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            mma_f16(acc[0][nt], x0, x1, x2, x3, qb[2 * k2][nt][0], qb[2 * k2][nt][1]);
+            mma_f16(acc[0][nt], y0, y1, y2, y3, qb[2 * k2 + 1][nt][0], qb[2 * k2 + 1][nt][1]);
+          }
+        }
+      } else {
+        // packed codes: token rows g and g+8 of the row block
+        constexpr int WPR = L::ROWB / 4;  // words per token row
+        uint32_t wa[WPR], wb[WPR];
+#pragma unroll
+        for (int w4 = 0; w4 < WPR / 4; ++w4) {
+          const uint4 x = *reinterpret_cast<const uint4*>(st + (r0 + g) * L::PITCH + w4 * 16);
+          const uint4 y = *reinterpret_cast<const uint4*>(st + (r0 + g + 8) * L::PITCH + w4 * 16);
+          wa[4 * w4] = x.x; wa[4 * w4 + 1] = x.y; wa[4 * w4 + 2] = x.z; wa[4 * w4 + 3] = x.w;
+          wb[4 * w4] = y.x; wb[4 * w4 + 1] = y.y; wb[4 * w4 + 2] = y.z; wb[4 * w4 + 3] = y.w;
+        }
+        const int kpg = p.gs / 16;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          if (KT == 2) {
+            a0 = (wa[kk] >> (2 * tq)) & 0x00030003u;
+            a1 = (wb[kk] >> (2 * tq)) & 0x00030003u;
+            a2 = (wa[kk] >> (2 * tq + 8)) & 0x00030003u;
+            a3 = (wb[kk] >> (2 * tq + 8)) & 0x00030003u;
+          } else {
+            a0 = (wa[2 * kk] >> (4 * tq)) & 0x000F000Fu;
+            a1 = (wb[2 * kk] >> (4 * tq)) & 0x000F000Fu;
+            a2 = (wa[2 * kk + 1] >> (4 * tq)) & 0x000F000Fu;
+            a3 = (wb[2 * kk + 1] >> (4 * tq)) & 0x000F000Fu;
+          }
+#pragma unroll
+          for (int gi = 0; gi < NGMAX; ++gi)
+            if (kk / kpg == gi)
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) mma_f16(acc[gi][nt], a0, a1, a2, a3, qb[kk][nt][0], qb[kk][nt][1]);
+        }
+      }
+      // ---- epilogue: scale/zero, write scores
+      const int ta = t0 + g, tb2 = t0 + g + 8;
+      float res[NT][4];
+      if (KT == 16 || KT == 8) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) res[nt][e] = acc[0][nt][e] * score_mul;
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) res[nt][0] = res[nt][1] = res[nt][2] = res[nt][3] = 0.f;
+#pragma unroll
+        for (int gi = 0; gi < NGMAX; ++gi) {
+          if (gi >= ngroups) break;
+          const int la = r0 + g, lb = r0 + g + 8;  // tile-local rows (zero-filled past the end)
+          const float sa = h16_to_f(ssc[la * ngroups + gi], p.sz_bf16);
+          const float za = h16_to_f(szr[la * ngroups + gi], p.sz_bf16);
+          const float sb = h16_to_f(ssc[lb * ngroups + gi], p.sz_bf16);
+          const float zb = h16_to_f(szr[lb * ngroups + gi], p.sz_bf16);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              res[nt][j] += fmaf(acc[gi][nt][j] * kSub, sa, qsum[gi][nt][j] * za);
+              res[nt][2 + j] += fmaf(acc[gi][nt][2 + j] * kSub, sb, qsum[gi][nt][j] * zb);
+            }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) res[nt][e] *= score_mul;
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int hl = nt * 8 + 2 * tq + j;
+          if (hl >= nheads) continue;
+          float* orow = p.out + int64_t(b) * p.o_sb + int64_t(hk * p.G + h0 + hl) * p.o_sh;
+          if (ta < t_end) orow[ta] = res[nt][j];
+          if (tb2 < t_end) orow[tb2] = res[nt][2 + j];
+        }
+    }
+  }
+}
+
+template <int KT, int D, int NT>
+int launch_score(const ScoreParams& p, int n_splits, cudaStream_t st) {
+  using L = SL<KT, D>;
+  const size_t smem = size_t(kSStages) * L::STAGE;
+  auto kern = score_kernel<KT, D, NT>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                        "cudaFuncSetAttribute(score)");
+    if (rc) return rc;
+    attr[dev & 63] = true;
+  }
+  dim3 grid(n_splits, p.Hk * p.head_chunks, p.B);
+  kern<<<grid, kSW * 32, smem, st>>>(p);
+  return cuda_check(cudaGetLastError(), "score_kernel launch");
+}
+
+template <int KT, int D>
+int launch_score_nt(const ScoreParams& p, int nt, int n_splits, cudaStream_t st) {
+  return nt == 1 ? launch_score<KT, D, 1>(p, n_splits, st) : launch_score<KT, D, 2>(p, n_splits, st);
+}
+
+int tile_tokens(int kt) { return 16 * kSW * (kt == 16 ? 1 : (kt == 8 ? 2 : 4)); }
+
+// ------------------------------------------------------------ score-key pack
+template <typename T, int BITS>
+__global__ void pack_score_keys_kernel(const T* __restrict__ k, int64_t rows, int64_t r_h, int64_t s_b, int64_t s_h,
+                                       int64_t s_s, int S, int D, int gs, uint8_t* __restrict__ packed,
+                                       T* __restrict__ scale, T* __restrict__ zero) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int ng = D / gs;
+  if (gid >= rows * ng) return;
+  const int64_t row = gid / ng;  // (b, h, s) flattened
+  const int grp = int(gid % ng);
+  const int64_t sidx = row % S, bh = row / S;
+  const int64_t h = bh % r_h, bb = bh / r_h;
+  const T* src = k + bb * s_b + h * s_h + sidx * s_s + int64_t(grp) * gs;
+  float lo = INFINITY, hi = -INFINITY;
+  for (int e = 0; e < gs; ++e) {
+    const float x = to_f32<T>(src[e]);
+    lo = fminf(lo, x);
+    hi = fmaxf(hi, x);
+  }
+  constexpr int LV = (1 << BITS) - 1;
+  const float sc = __fdiv_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), float(LV));
+  constexpr int EPB = 8 / BITS;
+  uint8_t* dst = packed + row * (D / EPB) + int64_t(grp) * (gs / EPB);
+  for (int e0 = 0; e0 < gs; e0 += EPB) {
+    uint32_t byte = 0;
+#pragma unroll
+    for (int i = 0; i < EPB; ++i) {
+      float qv = rintf(__fdiv_rn(__fsub_rn(to_f32<T>(src[e0 + i]), lo), sc));
+      qv = fminf(fmaxf(qv, 0.f), float(LV));
+      byte |= uint32_t(qv) << (i * BITS);
+    }
+    dst[e0 / EPB] = uint8_t(byte);
+  }
+  scale[row * ng + grp] = from_f32<T>(sc);
+  zero[row * ng + grp] = from_f32<T>(lo);
+}
+
+}  // namespace
+}  // namespace bd
+
+extern "C" {
+
+int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* scale, const bd_tensor* zero,
+                    float scaling, int score_bits, int group_size, const bd_tensor* scores, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(k, "k", 4)) ||
+      (rc = check_tensor(scores, "scores", 3, BD_F32)))
+    return rc;
+  if (q->dtype != BD_BF16 && q->dtype != BD_F16 && q->dtype != BD_F32) return fail(BD_ERR_DTYPE, "q must be bf16/f16/f32");
+  const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
+  const int64_t Hk = k->shape[1], S = k->shape[2];
+  if (k->shape[0] != B || Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "k must be [B,Hk,S,*] with Hq % Hk == 0");
+  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  int kt;
+  if (score_bits == 16) {
+    if (k->dtype != BD_BF16 || k->shape[3] != D) return fail(BD_ERR_DTYPE, "score_bits=16 needs bf16 k [B,Hk,S,D]");
+    if (q->dtype != BD_BF16) return fail(BD_ERR_DTYPE, "score_bits=16 needs a bf16 query");
+    kt = 16;
+  } else if (score_bits == 8) {
+    if (k->dtype != BD_F8E4M3 || k->shape[3] != D) return fail(BD_ERR_DTYPE, "score_bits=8 needs fp8 e4m3 k [B,Hk,S,D]");
+    kt = 8;
+  } else if (score_bits == 4 || score_bits == 2) {
+    if (k->dtype != BD_U8 || k->shape[3] * (8 / score_bits) != D)
+      return fail(BD_ERR_SHAPE, "packed k must be uint8 [B,Hk,S,D*bits/8]");
+    if (group_size != 16 && group_size != 32 && group_size != 64 && group_size != 128)
+      return fail(BD_ERR_UNSUPPORTED, "group_size must be 16, 32, 64 or 128");
+    if (D % group_size) return fail(BD_ERR_SHAPE, "head_dim must be a multiple of group_size");
+    if ((rc = check_tensor(scale, "scale", 4)) || (rc = check_tensor(zero, "zero", 4))) return rc;
+    if (scale->dtype != zero->dtype || (scale->dtype != BD_BF16 && scale->dtype != BD_F16))
+      return fail(BD_ERR_DTYPE, "scale/zero must both be bf16 or both f16");
+    for (const bd_tensor* t : {scale, zero})
+      if (t->shape[0] != B || t->shape[1] != Hk || t->shape[2] != S || t->shape[3] != D / group_size)
+        return fail(BD_ERR_SHAPE, "scale/zero must be [B,Hk,S,D/group_size]");
+    for (const bd_tensor* t : {scale, zero}) {
+      const int64_t ng = D / group_size;
+      if ((t->stride[3] != 1 && ng > 1) || (t->stride[2] != ng && S > 1))
+        return fail(BD_ERR_STRIDE, "scale/zero must be token-major contiguous within each (batch, head)");
+      if (reinterpret_cast<uintptr_t>(t->data) % 16 || (t->shape[1] > 1 && (t->stride[1] * 2) % 16) ||
+          (t->shape[0] > 1 && (t->stride[0] * 2) % 16))
+        return fail(BD_ERR_ALIGN, "scale/zero (batch, head) blocks must start on 16-byte boundaries");
+    }
+    kt = score_bits;
+  } else {
+    return fail(BD_ERR_VALUE, "Unsupported score_bits");
+  }
+  if (scores->shape[0] != B || scores->shape[1] != Hq || scores->shape[2] != S || (scores->stride[2] != 1 && S > 1))
+    return fail(BD_ERR_SHAPE, "scores must be [B,Hq,S] with contiguous rows");
+  if (q->stride[2] != 1) return fail(BD_ERR_STRIDE, "q innermost dim must be contiguous");
+  if ((rc = check_rows_aligned(k, "k"))) return rc;
+  if (B * Hq * S == 0) return BD_OK;
+  ScoreParams p{};
+  p.q = q->data; p.q_sb = q->stride[0]; p.q_sh = q->stride[1]; p.q_dtype = q->dtype;
+  p.k = static_cast<const uint8_t*>(k->data); p.k_sb = k->stride[0]; p.k_sh = k->stride[1]; p.k_ss = k->stride[2];
+  if (kt == 2 || kt == 4) {
+    p.sc = static_cast<const uint16_t*>(scale->data); p.sc_sb = scale->stride[0]; p.sc_sh = scale->stride[1]; p.sc_ss = scale->stride[2];
+    p.zr = static_cast<const uint16_t*>(zero->data); p.zr_sb = zero->stride[0]; p.zr_sh = zero->stride[1]; p.zr_ss = zero->stride[2];
+    p.sz_bf16 = scale->dtype == BD_BF16;
+    p.gs = group_size;
+  }
+  p.out = static_cast<float*>(scores->data); p.o_sb = scores->stride[0]; p.o_sh = scores->stride[1];
+  p.B = int(B); p.Hq = int(Hq); p.Hk = int(Hk); p.G = int(Hq / Hk); p.S = int(S);
+  const int nt = p.G <= 8 ? 1 : 2;
+  p.heads_per_chunk = 8 * nt;
+  p.head_chunks = (p.G + p.heads_per_chunk - 1) / p.heads_per_chunk;
+  p.scaling = scaling;
+  const int64_t tt = tile_tokens(kt);
+  const int64_t ntiles = (S + tt - 1) / tt;
+  const int64_t pairs = B * Hk * p.head_chunks;
+  const int64_t slots = 2LL * num_sms();
+  int64_t splits = pairs >= slots ? 1 : slots / pairs;
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, ntiles));
+  const int64_t tps = (ntiles + splits - 1) / splits;
+  splits = (ntiles + tps - 1) / tps;
+  p.tiles_per_split = int(tps);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int ns = int(splits);
+  if (D == 128) {
+    switch (kt) {
+      case 16: return launch_score_nt<16, 128>(p, nt, ns, st);
+      case 8: return launch_score_nt<8, 128>(p, nt, ns, st);
+      case 4: return launch_score_nt<4, 128>(p, nt, ns, st);
+      default: return launch_score_nt<2, 128>(p, nt, ns, st);
+    }
+  }
+  switch (kt) {
+    case 16: return launch_score_nt<16, 64>(p, nt, ns, st);
+    case 8: return launch_score_nt<8, 64>(p, nt, ns, st);
+    case 4: return launch_score_nt<4, 64>(p, nt, ns, st);
+    default: return launch_score_nt<2, 64>(p, nt, ns, st);
+  }
+}
+
+int bd_pack_score_keys(const bd_tensor* k, int score_bits, int group_size, const bd_tensor* packed,
+                       const bd_tensor* scale, const bd_tensor* zero, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if (score_bits != 2 && score_bits != 4) return fail(BD_ERR_VALUE, "Unsupported score_bits");
+  if ((rc = check_tensor(k, "k", 4)) || (rc = check_tensor(packed, "packed", 4, BD_U8)) ||
+      (rc = check_tensor(scale, "scale", 4, k->dtype)) || (rc = check_tensor(zero, "zero", 4, k->dtype)))
+    return rc;
+  if (k->dtype != BD_BF16 && k->dtype != BD_F16 && k->dtype != BD_F32) return fail(BD_ERR_DTYPE, "k must be bf16/f16/f32");
+  const int64_t B = k->shape[0], H = k->shape[1], S = k->shape[2], D = k->shape[3];
+  if (group_size <= 0 || D % group_size || group_size % (8 / score_bits))
+    return fail(BD_ERR_SHAPE, "head_dim must be a multiple of group_size");
+  const int epb = 8 / score_bits;
+  const int64_t ng = D / group_size;
+  if (packed->shape[0] != B || packed->shape[1] != H || packed->shape[2] != S || packed->shape[3] != D / epb)
+    return fail(BD_ERR_SHAPE, "packed must be [B,H,S,D*bits/8]");
+  for (const bd_tensor* t : {scale, zero})
+    if (t->shape[0] != B || t->shape[1] != H || t->shape[2] != S || t->shape[3] != ng)
+      return fail(BD_ERR_SHAPE, "scale/zero must be [B,H,S,D/group_size]");
+  auto dense = [](const bd_tensor* t) {
+    int64_t s = 1;
+    for (int i = 3; i >= 0; --i) {
+      if (t->shape[i] > 1 && t->stride[i] != s) return false;
+      s *= t->shape[i];
+    }
+    return true;
+  };
+  if (!dense(packed) || !dense(scale) || !dense(zero)) return fail(BD_ERR_STRIDE, "outputs must be contiguous");
+  if (k->stride[3] != 1 && D > 1) return fail(BD_ERR_STRIDE, "k innermost dim must be contiguous");
+  const int64_t rows = B * H * S;
+  if (rows * D == 0) return BD_OK;
+  const int64_t total = rows * ng;
+  const unsigned blocks = unsigned((total + 127) / 128);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define BD_PSK(T)                                                                                                  \
+  if (score_bits == 2)                                                                                             \
+    pack_score_keys_kernel<T, 2><<<blocks, 128, 0, st>>>(static_cast<const T*>(k->data), rows, H, k->stride[0],    \
+        k->stride[1], k->stride[2], int(S), int(D), group_size, static_cast<uint8_t*>(packed->data),               \
+        static_cast<T*>(scale->data), static_cast<T*>(zero->data));                                                \
+  else                                                                                                             \
+    pack_score_keys_kernel<T, 4><<<blocks, 128, 0, st>>>(static_cast<const T*>(k->data), rows, H, k->stride[0],    \
+        k->stride[1], k->stride[2], int(S), int(D), group_size, static_cast<uint8_t*>(packed->data),               \
+        static_cast<T*>(scale->data), static_cast<T*>(zero->data));
+  if (k->dtype == BD_BF16) { BD_PSK(__nv_bfloat16) }
+  else if (k->dtype == BD_F16) { BD_PSK(__half) }
+  else { BD_PSK(float) }
+#undef BD_PSK
+  return cuda_check(cudaGetLastError(), "pack_score_keys_kernel launch");
+}
+
+}  // extern "C"

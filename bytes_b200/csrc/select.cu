@@ -1,0 +1,732 @@
+// Top-k selection, sparse gather-attention and Quest page selection.
+//
+// References (saifmb0/bytes):
+//   scores.topk(kb)                src/attention_kernels.py:1069,1262 (torch radix select)
+//   select_topk('exact')           benchmarks/sparse_attention.py:287-309
+//   sparse_gather_attn             src/attention_kernels.py:987-1059
+//   attend_topk                    benchmarks/sparse_attention.py:367-387
+//   _quest_select                  benchmarks/sparse_attention.py:328-364
+//
+// Top-k (one CTA per row): fp32 scores map to order-preserving u32 keys (-0 folded into
+// +0). An MSB-first 8-bit radix select over the row (held in shared memory when it fits)
+// finds the k-th key T and how many keys equal to T to keep; an ordered warp-ballot
+// compaction then emits every key > T plus the lowest-index keys == T, in ascending index
+// order. Ties are therefore broken by lower index, exactly like a stable descending sort.
+// Optionally the k winners are bitonic-sorted by (key desc, index asc).
+#include "common.cuh"
+#include "decode_shared.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace bd {
+namespace {
+
+constexpr int kTkThreads = 1024;
+constexpr int kTkWarps = kTkThreads / 32;
+constexpr int kSmemRowMax = 45 * 1024;  // keys held in shared memory up to this row length
+
+__device__ __forceinline__ uint32_t f2key(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) == 0) u = 0;  // -0 == +0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+struct TopkParams {
+  const float* scores; int64_t row_stride; int rows_per_b; int64_t b_stride;  // row r -> (r / rows_per_b, r % rows_per_b)
+  int n, k;
+  float* vals; int64_t v_rs;        // optional
+  void* idx; int64_t i_rs; int idx64;
+  int sorted;
+};
+
+// Block-wide exclusive scan of one value per warp (32 warps). Returns this warp's base
+// and writes the total to *total. Uses red[] (32 ints).
+__device__ __forceinline__ int warp_base_scan(int v, int* red, int* total) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int x = red[lane];
+    int incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    red[lane] = incl - x;
+    if (lane == 31) red[32] = incl;
+  }
+  __syncthreads();
+  const int base = red[warp];
+  *total = red[32];
+  __syncthreads();
+  return base;
+}
+
+template <bool SMEM_ROW>
+__global__ void __launch_bounds__(kTkThreads, 1) topk_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int hist[256];
+  __shared__ int red[33];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_remaining;
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* src = p.scores + int64_t(row / p.rows_per_b) * p.b_stride + int64_t(row % p.rows_per_b) * p.row_stride;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
+  const int n = p.n, k = min(p.k, p.n);
+  auto key_at = [&](int i) -> uint32_t { return SMEM_ROW ? keys[i] : f2key(src[i]); };
+
+  // ---- load + first-digit histogram
+  for (int i = threadIdx.x; i < 256; i += kTkThreads) hist[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += kTkThreads) {
+    const uint32_t kk = f2key(src[i]);
+    if (SMEM_ROW) keys[i] = kk;
+    atomicAdd(&hist[kk >> 24], 1);
+  }
+  __syncthreads();
+
+  uint32_t prefix = 0, mask = 0;
+  int remaining = k;
+  if (k < n) {
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      if (pass > 0) {
+        for (int i = threadIdx.x; i < 256; i += kTkThreads) hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += kTkThreads) {
+          const uint32_t kk = key_at(i);
+          if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255], 1);
+        }
+        __syncthreads();
+      }
+      if (warp == 0) {
+        // lane l owns digits 255-8l .. 248-8l (descending)
+        int c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * lane - j]; sum += c[j]; }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int excl = incl - sum;
+        const bool here = excl < remaining && incl >= remaining;
+        if (here) {
+          int acc = excl, d = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (acc + c[j] >= remaining) { d = 255 - 8 * lane - j; break; }
+            acc += c[j];
+          }
+          s_prefix = prefix | (uint32_t(d) << shift);
+          s_remaining = remaining - acc;
+        }
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      remaining = s_remaining;
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+  }
+  // threshold T = prefix; keep all keys > T and the `remaining` lowest-index keys == T.
+  const uint32_t T = prefix;
+  const int keep_eq = remaining;
+  const bool take_all = k >= n;
+
+  // ---- ordered compaction: warp w walks a contiguous segment
+  const int seg = ((n + kTkWarps - 1) / kTkWarps + 31) & ~31;
+  const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
+  const unsigned lt = (1u << lane) - 1u;
+  int eq_cnt = 0;
+  if (!take_all)
+    for (int i0 = s0; i0 < s1; i0 += 32) {
+      const int i = i0 + lane;
+      const bool eq = i < s1 && key_at(i) == T;
+      eq_cnt += __popc(__ballot_sync(0xffffffffu, eq));
+    }
+  int eq_total;
+  const int eq_base = warp_base_scan(eq_cnt, red, &eq_total);
+  int sel_cnt = 0;
+  {
+    int eq_run = eq_base;
+    for (int i0 = s0; i0 < s1; i0 += 32) {
+      const int i = i0 + lane;
+      const uint32_t kk = i < s1 ? key_at(i) : 0u;
+      const bool eq = i < s1 && kk == T;
+      const unsigned eb = __ballot_sync(0xffffffffu, eq);
+      const int rank = eq_run + __popc(eb & lt);
+      const bool sel = i < s1 && (take_all || kk > T || (eq && rank < keep_eq));
+      sel_cnt += __popc(__ballot_sync(0xffffffffu, sel));
+      eq_run += __popc(eb);
+    }
+  }
+  int sel_total;
+  const int sel_base = warp_base_scan(sel_cnt, red, &sel_total);
+  // winners go to shared memory (after the row keys) as (key, index) pairs when sorting,
+  // else straight to the outputs in index order
+  uint32_t* wk = reinterpret_cast<uint32_t*>(smem + (SMEM_ROW ? size_t(n) * 4 : 0));
+  const int kpow = p.sorted ? (k <= 1 ? 1 : 1 << (32 - __clz(k - 1))) : 0;
+  int* wi = reinterpret_cast<int*>(wk + kpow);
+  {
+    int eq_run = eq_base, pos = sel_base;
+    for (int i0 = s0; i0 < s1; i0 += 32) {
+      const int i = i0 + lane;
+      const uint32_t kk = i < s1 ? key_at(i) : 0u;
+      const bool eq = i < s1 && kk == T;
+      const unsigned eb = __ballot_sync(0xffffffffu, eq);
+      const int rank = eq_run + __popc(eb & lt);
+      const bool sel = i < s1 && (take_all || kk > T || (eq && rank < keep_eq));
+      const unsigned sb = __ballot_sync(0xffffffffu, sel);
+      if (sel) {
+        const int o = pos + __popc(sb & lt);
+        if (p.sorted) {
+          wk[o] = kk;
+          wi[o] = i;
+        } else {
+          if (p.vals) p.vals[int64_t(row) * p.v_rs + o] = key2f(kk);
+          if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + o] = i;
+          else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + o] = i;
+        }
+      }
+      pos += __popc(sb);
+      eq_run += __popc(eb);
+    }
+  }
+  if (!p.sorted) return;
+  __syncthreads();
+  // ---- bitonic sort of kpow (key desc, index asc); padding sorts last
+  for (int i = k + threadIdx.x; i < kpow; i += kTkThreads) { wk[i] = 0u; wi[i] = 0x7fffffff; }
+  __syncthreads();
+  for (int size = 2; size <= kpow; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int t = threadIdx.x; t < kpow / 2; t += kTkThreads) {
+        const int lo = 2 * t - (t & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc_block = ((lo & size) == 0);  // first half of each block sorts "before"
+        const uint32_t ka = wk[lo], kb = wk[hi];
+        const int ia = wi[lo], ib = wi[hi];
+        // "a before b" if key larger, or equal key and smaller index
+        const bool a_first = (ka > kb) || (ka == kb && ia < ib);
+        if (a_first != desc_block) {
+          wk[lo] = kb; wk[hi] = ka;
+          wi[lo] = ib; wi[hi] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int o = threadIdx.x; o < k; o += kTkThreads) {
+    if (p.vals) p.vals[int64_t(row) * p.v_rs + o] = key2f(wk[o]);
+    if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + o] = wi[o];
+    else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + o] = wi[o];
+  }
+}
+
+// ------------------------------------------------------------------ gather-attend
+struct GatherParams {
+  const void* q; int64_t q_sb, q_sh; int q_dtype;
+  const uint8_t* k; int64_t k_sb, k_sh, k_ss;
+  const uint8_t* v; int64_t v_sb, v_sh, v_ss;
+  const void* idx; int64_t i_sb, i_sh; int idx64;
+  int B, Hq, Hk, G, S, kb;
+  float scaling;
+  int rows_per_split, nsplit;
+  float* part_m; float* part_l; float* part_o;
+};
+
+template <int D, bool FP8>
+__global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) {
+  constexpr int CPL = D / 8;  // channels per lane (8 lanes per row)
+  constexpr int ELT = FP8 ? 1 : 2;
+  __shared__ float red_m[16], red_l[16];
+  __shared__ float red_o[16][D];
+  const int split = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+  const int hk = hq / p.G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 3, sub = lane & 7;  // 4 row groups of 8 lanes per warp
+  const int gid = warp * 4 + grp;             // 16 row groups per CTA
+  float qv[CPL];
+  {
+    const int64_t qo = int64_t(b) * p.q_sb + int64_t(hq) * p.q_sh + sub * CPL;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      float x;
+      if (p.q_dtype == BD_BF16) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[qo + c]);
+      else if (p.q_dtype == BD_F16) x = __half2float(reinterpret_cast<const __half*>(p.q)[qo + c]);
+      else x = reinterpret_cast<const float*>(p.q)[qo + c];
+      qv[c] = x;
+    }
+  }
+  const uint8_t* kb_ = p.k + (int64_t(b) * p.k_sb + int64_t(hk) * p.k_sh) * ELT + sub * CPL * ELT;
+  const uint8_t* vb_ = p.v + (int64_t(b) * p.v_sb + int64_t(hk) * p.v_sh) * ELT + sub * CPL * ELT;
+  const int r_begin = split * p.rows_per_split;
+  const int r_end = min(p.kb, r_begin + p.rows_per_split);
+  float m = -INFINITY, l = 0.f, acc[CPL];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) acc[c] = 0.f;
+  auto row_index = [&](int r) -> int64_t {
+    const int64_t off = int64_t(b) * p.i_sb + int64_t(hq) * p.i_sh + r;
+    return p.idx64 ? reinterpret_cast<const int64_t*>(p.idx)[off] : int64_t(reinterpret_cast<const int32_t*>(p.idx)[off]);
+  };
+  constexpr int WPL = CPL * ELT / 4;  // 32-bit words per lane per row (2, 4 or 8)
+  for (int r = r_begin + gid; r < r_end; r += 16) {
+    const int64_t t = row_index(r);
+    const bool ok = t >= 0 && t < p.S;
+    uint32_t kw[WPL], vw[WPL];
+#pragma unroll
+    for (int w = 0; w < WPL; ++w) kw[w] = vw[w] = 0u;
+    if (ok) {
+      const uint8_t* kr = kb_ + t * p.k_ss * ELT;
+      const uint8_t* vr = vb_ + t * p.v_ss * ELT;
+      if (WPL == 2) {
+        const uint2 a = __ldg(reinterpret_cast<const uint2*>(kr)), c = __ldg(reinterpret_cast<const uint2*>(vr));
+        kw[0] = a.x; kw[1] = a.y; vw[0] = c.x; vw[1] = c.y;
+      } else {
+#pragma unroll
+        for (int u = 0; u < WPL / 4; ++u) {
+          const uint4 a = __ldg(reinterpret_cast<const uint4*>(kr) + u), c = __ldg(reinterpret_cast<const uint4*>(vr) + u);
+          kw[4 * u] = a.x; kw[4 * u + 1] = a.y; kw[4 * u + 2] = a.z; kw[4 * u + 3] = a.w;
+          vw[4 * u] = c.x; vw[4 * u + 1] = c.y; vw[4 * u + 2] = c.z; vw[4 * u + 3] = c.w;
+        }
+      }
+    }
+    float kf[CPL], vf[CPL];
+#pragma unroll
+    for (int w = 0; w < WPL; ++w) {
+      if (FP8) {
+        const uint32_t k01 = e4m3x2_to_f16x2(kw[w]), k23 = e4m3x2_to_f16x2(kw[w] >> 16);
+        const uint32_t v01 = e4m3x2_to_f16x2(vw[w]), v23 = e4m3x2_to_f16x2(vw[w] >> 16);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&k01));
+        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&k23));
+        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&v01));
+        const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v23));
+        kf[4 * w] = a.x; kf[4 * w + 1] = a.y; kf[4 * w + 2] = c.x; kf[4 * w + 3] = c.y;
+        vf[4 * w] = d.x; vf[4 * w + 1] = d.y; vf[4 * w + 2] = e.x; vf[4 * w + 3] = e.y;
+      } else {
+        kf[2 * w] = __uint_as_float(kw[w] << 16);
+        kf[2 * w + 1] = __uint_as_float(kw[w] & 0xffff0000u);
+        vf[2 * w] = __uint_as_float(vw[w] << 16);
+        vf[2 * w + 1] = __uint_as_float(vw[w] & 0xffff0000u);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) s = fmaf(qv[c], kf[c], s);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if (!ok) continue;  // masked position: contributes nothing (uniform within the 8-lane group)
+    s *= p.scaling;
+    const float mn = fmaxf(m, s);
+    const float alpha = __expf(m - mn);
+    const float pw = __expf(s - mn);
+    l = l * alpha + pw;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) acc[c] = fmaf(pw, vf[c], acc[c] * alpha);
+    m = mn;
+  }
+  // merge the 16 row groups
+  if (sub == 0) { red_m[gid] = m; red_l[gid] = l; }
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) red_o[gid][sub * CPL + c] = acc[c];
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += 128) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) M = fmaxf(M, red_m[i]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float f = M == -INFINITY ? 0.f : __expf(red_m[i] - M);
+      L += red_l[i] * f;
+      O += red_o[i][c] * f;
+    }
+    const int64_t pi = (int64_t(b) * p.Hq + hq) * p.nsplit + split;
+    p.part_o[pi * D + c] = O;
+    if (c == 0) { p.part_m[pi] = M; p.part_l[pi] = L; }
+  }
+}
+
+// ------------------------------------------------------------------ Quest
+template <typename T>
+__global__ void quest_minmax_kernel(const T* __restrict__ k, int64_t s_b, int64_t s_h, int64_t s_s, int Hk, int S,
+                                    int D, int page, int np, T* __restrict__ kmin, T* __restrict__ kmax) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, h, page, d)
+  const int64_t total = int64_t(gridDim.y) * Hk * np * D;
+  (void)total;
+  const int b = blockIdx.y;
+  if (gid >= int64_t(Hk) * np * D) return;
+  const int d = int(gid % D);
+  const int64_t r = gid / D;
+  const int pg = int(r % np), h = int(r / np);
+  const T* src = k + int64_t(b) * s_b + int64_t(h) * s_h + d;
+  const int t0 = pg * page, t1 = min(S, t0 + page);
+  float lo = INFINITY, hi = -INFINITY;
+  for (int t = t0; t < t1; ++t) {
+    const float x = to_f32<T>(src[int64_t(t) * s_s]);
+    lo = fminf(lo, x);
+    hi = fmaxf(hi, x);
+  }
+  const int64_t o = ((int64_t(b) * Hk + h) * np + pg) * D + d;
+  kmin[o] = from_f32<T>(lo);
+  kmax[o] = from_f32<T>(hi);
+}
+
+// bound[b,hq,p] = scaling * sum_d max(q_d*kmin_pd, q_d*kmax_pd); pages >= force_from -> +inf
+constexpr int kQPages = 64;  // pages per CTA (one thread each)
+
+template <int D>
+__global__ void __launch_bounds__(kQPages) quest_bounds_kernel(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh,
+                                                         const __nv_bfloat16* kmin, const __nv_bfloat16* kmax,
+                                                         int64_t m_sb, int64_t m_sh, int64_t m_sp, int Hq, int Hk,
+                                                         int np, float scaling, int force_from, float* bounds) {
+  constexpr int PITCH = D * 2 + 16;
+  __shared__ __align__(16) uint8_t sm[2][kQPages * PITCH];
+  const int b = blockIdx.z, hk = blockIdx.y, p0 = blockIdx.x * kQPages;
+  const int G = Hq / Hk;
+  const int npg = min(kQPages, np - p0);
+  // stage the pages' min and max rows (padded pitch: conflict-free 16-byte reads)
+  for (int c = threadIdx.x; c < npg * (D / 8); c += kQPages) {
+    const int r = c / (D / 8), cc = c % (D / 8);
+    const int64_t go = int64_t(b) * m_sb + int64_t(hk) * m_sh + int64_t(p0 + r) * m_sp + cc * 8;
+    cp_async16(smem_u32(&sm[0][r * PITCH + cc * 16]), kmin + go, 16);
+    cp_async16(smem_u32(&sm[1][r * PITCH + cc * 16]), kmax + go, 16);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  const int r = threadIdx.x;
+  if (r >= npg) return;
+  const int pg = p0 + r;
+  for (int h0 = 0; h0 < G; h0 += 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c8 = 0; c8 < D / 8; ++c8) {
+      const uint4 lo4 = *reinterpret_cast<const uint4*>(&sm[0][r * PITCH + c8 * 16]);
+      const uint4 hi4 = *reinterpret_cast<const uint4*>(&sm[1][r * PITCH + c8 * 16]);
+      const uint32_t lw[4] = {lo4.x, lo4.y, lo4.z, lo4.w}, hw[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        if (h0 + hh >= G) break;
+        const int64_t qo = int64_t(b) * q_sb + int64_t(hk * G + h0 + hh) * q_sh + c8 * 8;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float mnv = __uint_as_float(e ? (lw[w] & 0xffff0000u) : (lw[w] << 16));
+            const float mxv = __uint_as_float(e ? (hw[w] & 0xffff0000u) : (hw[w] << 16));
+            float qd;
+            const int64_t qi = qo + 2 * w + e;
+            if (q_dtype == BD_BF16) qd = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(q)[qi]);
+            else if (q_dtype == BD_F16) qd = __half2float(reinterpret_cast<const __half*>(q)[qi]);
+            else qd = reinterpret_cast<const float*>(q)[qi];
+            acc[hh] += fmaxf(qd * mnv, qd * mxv);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      if (h0 + hh >= G) break;
+      const float v = pg >= force_from ? INFINITY : acc[hh] * scaling;
+      bounds[(int64_t(b) * Hq + hk * G + h0 + hh) * np + pg] = v;
+    }
+  }
+}
+
+__global__ void quest_expand_kernel(const int64_t* pidx, int npick, int page, int S, int rows, void* out, int out64,
+                                    int64_t o_rs) {
+  const int row = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= npick * page || row >= rows) return;
+  const int64_t pg = pidx[int64_t(row) * npick + i / page];
+  int64_t t = pg * page + i % page;
+  if (t > int64_t(S) - 1) t = int64_t(S) - 1;
+  if (out64) reinterpret_cast<int64_t*>(out)[int64_t(row) * o_rs + i] = t;
+  else reinterpret_cast<int32_t*>(out)[int64_t(row) * o_rs + i] = int32_t(t);
+}
+
+int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, int64_t row_stride, int n, int k,
+             float* vals, int64_t v_rs, void* idx, int idx64, int64_t i_rs, int sorted, cudaStream_t st) {
+  TopkParams p{};
+  p.scores = scores; p.row_stride = row_stride; p.rows_per_b = rows_per_b; p.b_stride = b_stride;
+  p.n = n; p.k = k; p.vals = vals; p.v_rs = v_rs; p.idx = idx; p.i_rs = i_rs; p.idx64 = idx64; p.sorted = sorted;
+  const int kk = std::min(k, n);
+  size_t wbytes = 0;
+  if (sorted) {
+    int kp = 1;
+    while (kp < std::max(kk, 1)) kp <<= 1;
+    wbytes = size_t(kp) * 8;
+  }
+  const bool in_smem = n <= kSmemRowMax;
+  const size_t smem = (in_smem ? size_t(n) * 4 : 0) + wbytes;
+  if (smem > 220 * 1024) return fail(BD_ERR_UNSUPPORTED, "top-k: sorted output of this many elements does not fit");
+  int rc;
+  if (in_smem) {
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+      if ((rc = cuda_check(cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024),
+                           "cudaFuncSetAttribute(topk)")))
+        return rc;
+      attr[dev & 63] = true;
+    }
+    topk_kernel<true><<<rows, kTkThreads, smem, st>>>(p);
+  } else {
+    static bool attr2[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr2[dev & 63]) {
+      if ((rc = cuda_check(cudaFuncSetAttribute(topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024),
+                           "cudaFuncSetAttribute(topk)")))
+        return rc;
+      attr2[dev & 63] = true;
+    }
+    topk_kernel<false><<<rows, kTkThreads, smem, st>>>(p);
+  }
+  return cuda_check(cudaGetLastError(), "topk_kernel launch");
+}
+
+}  // namespace
+}  // namespace bd
+
+extern "C" {
+
+int bd_topk(const bd_tensor* scores, int k, int sorted, const bd_tensor* values, const bd_tensor* indices,
+            bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if (!scores) return fail(BD_ERR_NULL, "scores is NULL");
+  const int nd = scores->ndim;
+  if (nd < 1 || nd > 3) return fail(BD_ERR_SHAPE, "scores must have 1 to 3 dims");
+  if ((rc = check_tensor(scores, "scores", nd, BD_F32)) || (rc = check_tensor(indices, "indices", nd))) return rc;
+  if (indices->dtype != BD_I64 && indices->dtype != BD_I32) return fail(BD_ERR_DTYPE, "indices must be int64 or int32");
+  if (values && (rc = check_tensor(values, "values", nd, BD_F32))) return rc;
+  const int64_t n = scores->shape[nd - 1];
+  if (k < 0) return fail(BD_ERR_VALUE, "k must be >= 0");
+  if (k > n) return fail(BD_ERR_VALUE, "selected index k out of range");
+  if (n > INT32_MAX / 2) return fail(BD_ERR_UNSUPPORTED, "row too long");
+  int64_t rows = 1;
+  for (int i = 0; i + 1 < nd; ++i) {
+    rows *= scores->shape[i];
+    if (indices->shape[i] != scores->shape[i] || (values && values->shape[i] != scores->shape[i]))
+      return fail(BD_ERR_SHAPE, "leading dims of outputs must match scores");
+  }
+  if (indices->shape[nd - 1] != k || (values && values->shape[nd - 1] != k))
+    return fail(BD_ERR_SHAPE, "outputs must have k in the last dim");
+  if (scores->stride[nd - 1] != 1 && n > 1) return fail(BD_ERR_STRIDE, "scores rows must be contiguous");
+  // rows addressed as (outer, inner) over at most two leading dims
+  int64_t rows_per_b = nd == 3 ? scores->shape[1] : (nd == 2 ? scores->shape[0] : 1);
+  int64_t row_stride = nd >= 2 ? scores->stride[nd - 2] : 0;
+  int64_t b_stride = nd == 3 ? scores->stride[0] : 0;
+  auto dense_rows = [&](const bd_tensor* t) {
+    if (t->stride[nd - 1] != 1 && k > 1) return false;
+    int64_t s = k;
+    for (int i = nd - 2; i >= 0; --i) {
+      if (t->shape[i] > 1 && t->stride[i] != s) return false;
+      s *= t->shape[i];
+    }
+    return true;
+  };
+  if (!dense_rows(indices) || (values && !dense_rows(values))) return fail(BD_ERR_STRIDE, "outputs must be contiguous");
+  if (rows == 0 || k == 0) return BD_OK;
+  if (rows > INT32_MAX) return fail(BD_ERR_UNSUPPORTED, "too many rows");
+  return run_topk(static_cast<const float*>(scores->data), int(rows), int(rows_per_b), b_stride, row_stride, int(n), k,
+                  values ? static_cast<float*>(values->data) : nullptr, k, indices->data, indices->dtype == BD_I64, k,
+                  sorted, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t bd_sparse_gather_attn_workspace(const bd_tensor* q, const bd_tensor* idx) {
+  using namespace bd;
+  if (check_tensor(q, "q", 3) || check_tensor(idx, "idx", 3)) return 0;
+  const int64_t rows = q->shape[0] * q->shape[1];
+  const int64_t kb = idx->shape[2];
+  const int64_t want = std::max<int64_t>(1, (2LL * num_sms() * 1) / std::max<int64_t>(rows, 1));
+  const int64_t nsplit = std::max<int64_t>(1, std::min<int64_t>(want, (kb + 63) / 64));
+  return partials_bytes(size_t(rows), int(nsplit), int(q->shape[2]));
+}
+
+int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
+                          float scaling, const bd_tensor* out, void* workspace, size_t workspace_bytes,
+                          bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(k, "k", 4)) || (rc = check_tensor(v, "v", 4)) ||
+      (rc = check_tensor(idx, "idx", 3)) || (rc = check_tensor(out, "out", 3)))
+    return rc;
+  if (k->dtype != v->dtype || (k->dtype != BD_BF16 && k->dtype != BD_F8E4M3))
+    return fail(BD_ERR_DTYPE, "k and v must both be bf16 or both fp8 e4m3");
+  if (idx->dtype != BD_I32 && idx->dtype != BD_I64) return fail(BD_ERR_DTYPE, "idx must be int32 or int64");
+  if (q->dtype != BD_BF16 && q->dtype != BD_F16 && q->dtype != BD_F32) return fail(BD_ERR_DTYPE, "q must be bf16/f16/f32");
+  const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
+  const int64_t Hk = k->shape[1], S = k->shape[2], kb = idx->shape[2];
+  if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
+  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  for (int i = 0; i < 4; ++i)
+    if (k->shape[i] != v->shape[i]) return fail(BD_ERR_SHAPE, "k and v shapes differ");
+  if (k->shape[0] != B || k->shape[3] != D || idx->shape[0] != B || idx->shape[1] != Hq)
+    return fail(BD_ERR_SHAPE, "expect q [B,Hq,D], k/v [B,Hk,S,D], idx [B,Hq,kb]");
+  if (out->shape[0] != B || out->shape[1] != Hq || out->shape[2] != D || out->stride[2] != 1)
+    return fail(BD_ERR_SHAPE, "out must be [B,Hq,D] with contiguous rows");
+  if (idx->stride[2] != 1 && kb > 1) return fail(BD_ERR_STRIDE, "idx rows must be contiguous");
+  if (q->stride[2] != 1) return fail(BD_ERR_STRIDE, "q innermost dim must be contiguous");
+  if ((rc = check_rows_aligned(k, "k")) || (rc = check_rows_aligned(v, "v"))) return rc;
+  if (B * Hq == 0) return BD_OK;
+  const int64_t rows = B * Hq;
+  const int64_t want = std::max<int64_t>(1, (2LL * num_sms()) / rows);
+  const int nsplit = int(std::max<int64_t>(1, std::min<int64_t>(want, (kb + 63) / 64)));
+  const size_t need = partials_bytes(size_t(rows), nsplit, int(D));
+  if (!workspace || workspace_bytes < need) return fail(BD_ERR_WORKSPACE, "need " + std::to_string(need) + " workspace bytes");
+  Partials part = carve_partials(workspace, size_t(rows), nsplit, int(D));
+  GatherParams p{};
+  p.q = q->data; p.q_sb = q->stride[0]; p.q_sh = q->stride[1]; p.q_dtype = q->dtype;
+  p.k = static_cast<const uint8_t*>(k->data); p.k_sb = k->stride[0]; p.k_sh = k->stride[1]; p.k_ss = k->stride[2];
+  p.v = static_cast<const uint8_t*>(v->data); p.v_sb = v->stride[0]; p.v_sh = v->stride[1]; p.v_ss = v->stride[2];
+  p.idx = idx->data; p.i_sb = idx->stride[0]; p.i_sh = idx->stride[1]; p.idx64 = idx->dtype == BD_I64;
+  p.B = int(B); p.Hq = int(Hq); p.Hk = int(Hk); p.G = int(Hq / Hk); p.S = int(S); p.kb = int(kb);
+  p.scaling = scaling;
+  p.rows_per_split = int((kb + nsplit - 1) / nsplit);
+  p.nsplit = nsplit;
+  p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(nsplit, unsigned(Hq), unsigned(B));
+  const bool fp8 = k->dtype == BD_F8E4M3;
+  if (D == 128) {
+    if (fp8) gather_attn_kernel<128, true><<<grid, 128, 0, st>>>(p);
+    else gather_attn_kernel<128, false><<<grid, 128, 0, st>>>(p);
+  } else {
+    if (fp8) gather_attn_kernel<64, true><<<grid, 128, 0, st>>>(p);
+    else gather_attn_kernel<64, false><<<grid, 128, 0, st>>>(p);
+  }
+  if ((rc = cuda_check(cudaGetLastError(), "gather_attn_kernel launch"))) return rc;
+  return launch_combine(part, int(B), int(Hq), int(D), out, st);
+}
+
+int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, const bd_tensor* kmax,
+                         bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_tensor(k, "k", 4)) || (rc = check_tensor(kmin, "kmin", 4, k->dtype)) ||
+      (rc = check_tensor(kmax, "kmax", 4, k->dtype)))
+    return rc;
+  if (page <= 0) return fail(BD_ERR_VALUE, "page must be positive");
+  if (k->dtype != BD_BF16 && k->dtype != BD_F16 && k->dtype != BD_F32) return fail(BD_ERR_DTYPE, "k must be bf16/f16/f32");
+  const int64_t B = k->shape[0], H = k->shape[1], S = k->shape[2], D = k->shape[3];
+  const int64_t np = (S + page - 1) / page;
+  for (const bd_tensor* t : {kmin, kmax}) {
+    if (t->shape[0] != B || t->shape[1] != H || t->shape[2] != np || t->shape[3] != D)
+      return fail(BD_ERR_SHAPE, "kmin/kmax must be [B,H,ceil(S/page),D]");
+    if (t->stride[3] != 1 || t->stride[2] != D || t->stride[1] != np * D || (B > 1 && t->stride[0] != H * np * D))
+      return fail(BD_ERR_STRIDE, "kmin/kmax must be contiguous");
+  }
+  if (B * H * np * D == 0) return BD_OK;
+  const int64_t per_b = H * np * D;
+  dim3 grid(unsigned((per_b + 255) / 256), unsigned(B));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (k->dtype == BD_BF16)
+    quest_minmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(k->data), k->stride[0],
+        k->stride[1], k->stride[2], int(H), int(S), int(D), page, int(np), static_cast<__nv_bfloat16*>(kmin->data),
+        static_cast<__nv_bfloat16*>(kmax->data));
+  else if (k->dtype == BD_F16)
+    quest_minmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(k->data), k->stride[0], k->stride[1],
+        k->stride[2], int(H), int(S), int(D), page, int(np), static_cast<__half*>(kmin->data),
+        static_cast<__half*>(kmax->data));
+  else
+    quest_minmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(k->data), k->stride[0], k->stride[1],
+        k->stride[2], int(H), int(S), int(D), page, int(np), static_cast<float*>(kmin->data),
+        static_cast<float*>(kmax->data));
+  return cuda_check(cudaGetLastError(), "quest_minmax_kernel launch");
+}
+
+int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* kmax, float scaling,
+                         int force_from_page, const bd_tensor* bounds, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(kmin, "kmin", 4, BD_BF16)) ||
+      (rc = check_tensor(kmax, "kmax", 4, BD_BF16)) || (rc = check_tensor(bounds, "bounds", 3, BD_F32)))
+    return rc;
+  const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
+  const int64_t Hk = kmin->shape[1], np = kmin->shape[2];
+  if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
+  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  for (int i = 0; i < 4; ++i)
+    if (kmin->shape[i] != kmax->shape[i] || kmin->stride[i] != kmax->stride[i])
+      return fail(BD_ERR_SHAPE, "kmin and kmax must have the same shape and layout");
+  if (kmin->shape[0] != B || kmin->shape[3] != D) return fail(BD_ERR_SHAPE, "kmin must be [B,Hk,np,D]");
+  if (bounds->shape[0] != B || bounds->shape[1] != Hq || bounds->shape[2] != np || bounds->stride[2] != 1 ||
+      bounds->stride[1] != np || (B > 1 && bounds->stride[0] != Hq * np))
+    return fail(BD_ERR_SHAPE, "bounds must be contiguous [B,Hq,np]");
+  if (q->stride[2] != 1) return fail(BD_ERR_STRIDE, "q innermost dim must be contiguous");
+  if ((rc = check_rows_aligned(kmin, "kmin")) || (rc = check_rows_aligned(kmax, "kmax"))) return rc;
+  if (B * Hq * np == 0) return BD_OK;
+  dim3 grid(unsigned((np + kQPages - 1) / kQPages), unsigned(Hk), unsigned(B));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  auto* mn = static_cast<const __nv_bfloat16*>(kmin->data);
+  auto* mx = static_cast<const __nv_bfloat16*>(kmax->data);
+  if (D == 128)
+    quest_bounds_kernel<128><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
+        kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
+        static_cast<float*>(bounds->data));
+  else
+    quest_bounds_kernel<64><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
+        kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
+        static_cast<float*>(bounds->data));
+  return cuda_check(cudaGetLastError(), "quest_bounds_kernel launch");
+}
+
+size_t bd_quest_select_workspace(const bd_tensor* q, const bd_tensor* kmin, int kb, int page) {
+  using namespace bd;
+  if (check_tensor(q, "q", 3) || check_tensor(kmin, "kmin", 4) || page <= 0) return 0;
+  const int64_t np = kmin->shape[2];
+  const int64_t npick = std::min<int64_t>(std::max<int64_t>(1, (kb + page - 1) / page), np);
+  const int64_t rows = q->shape[0] * q->shape[1];
+  return size_t(rows * np * 4 + rows * npick * 8 + 512);
+}
+
+int bd_quest_select(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* kmax, int S, int kb, int page,
+                    float scaling, int force_from_page, const bd_tensor* idx_out, void* workspace,
+                    size_t workspace_bytes, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(kmin, "kmin", 4)) || (rc = check_tensor(idx_out, "idx", 3)))
+    return rc;
+  if (page <= 0 || kb < 0 || S <= 0) return fail(BD_ERR_VALUE, "page, kb and S must be positive");
+  const int64_t B = q->shape[0], Hq = q->shape[1];
+  const int64_t np = kmin->shape[2];
+  if (np != (S + page - 1) / page) return fail(BD_ERR_SHAPE, "page metadata does not match S and page");
+  const int64_t npick = std::min<int64_t>(std::max<int64_t>(1, (kb + page - 1) / page), np);
+  if (idx_out->dtype != BD_I32 && idx_out->dtype != BD_I64) return fail(BD_ERR_DTYPE, "idx must be int32 or int64");
+  if (idx_out->shape[0] != B || idx_out->shape[1] != Hq || idx_out->shape[2] != npick * page || idx_out->stride[2] != 1 ||
+      idx_out->stride[1] != npick * page || (B > 1 && idx_out->stride[0] != Hq * npick * page))
+    return fail(BD_ERR_SHAPE, "idx must be contiguous [B,Hq,npick*page]");
+  const int64_t rows = B * Hq;
+  const size_t need = size_t(rows * np * 4 + rows * npick * 8 + 512);
+  if (!workspace || workspace_bytes < need) return fail(BD_ERR_WORKSPACE, "need " + std::to_string(need) + " workspace bytes");
+  if (rows == 0) return BD_OK;
+  uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255);
+  float* bounds = reinterpret_cast<float*>(base);
+  int64_t* pidx = reinterpret_cast<int64_t*>((base + size_t(rows * np * 4) + 255) & ~uintptr_t(255));
+  bd_tensor bt{};
+  bt.data = bounds; bt.dtype = BD_F32; bt.ndim = 3;
+  bt.shape[0] = B; bt.shape[1] = Hq; bt.shape[2] = np;
+  bt.stride[0] = Hq * np; bt.stride[1] = np; bt.stride[2] = 1;
+  if ((rc = bd_quest_page_bounds(q, kmin, kmax, scaling, force_from_page, &bt, stream))) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if ((rc = run_topk(bounds, int(rows), int(rows), 0, np, int(np), int(npick), nullptr, 0, pidx, 1, npick, 1, st)))
+    return rc;
+  dim3 grid(unsigned((npick * page + 255) / 256), unsigned(rows));
+  quest_expand_kernel<<<grid, 256, 0, st>>>(pidx, int(npick), page, S, int(rows), idx_out->data,
+                                            idx_out->dtype == BD_I64, npick * page);
+  return cuda_check(cudaGetLastError(), "quest_expand_kernel launch");
+}
+
+}  // extern "C"

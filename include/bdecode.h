@@ -87,6 +87,101 @@ int bd_decode_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tens
 int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o,
                    const bd_tensor* out, bd_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * KIVI 2/4-bit KV-cache decode (fused: packed-cache split-KV kernel + bf16
+ * residual window + log-sum-exp combine). Q [B,Hq,D=128] bf16/f16/f32;
+ * Kq int32 [B,Hk,D,Sq*bits/32]; K_scale,K_mn f16 [B,Hk,D,Sq/32];
+ * Vq int32 [B,Hk,Sq,D*bits/32]; V_scale,V_mn f16 [B,Hk,Sq,D/32];
+ * K_residual,V_residual bf16 [B,Hk,R,D]; out [B,Hq,D]; group_size 32.
+ * scaling multiplies q.k (the reference step uses 1/sqrt(D)).
+ * Row pitches: Kq/Vq rows 16-byte aligned, scale/min rows 8-byte aligned.
+ * ref: kivi_decode_attn  benchmarks/kivi_latency.py:59 (which calls the external
+ *      cuda_bmm_fA_qB_outer twice plus torch matmul/softmax) */
+size_t bd_kivi_decode_attn_workspace(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_residual,
+                                     int bits);
+int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale, const bd_tensor* K_mn,
+                        const bd_tensor* K_residual, const bd_tensor* Vq, const bd_tensor* V_scale,
+                        const bd_tensor* V_mn, const bd_tensor* V_residual, int bits, int group_size, float scaling,
+                        const bd_tensor* out, void* workspace, size_t workspace_bytes, bd_stream_t stream);
+
+/* Group-wise asymmetric quantize + pack along the last dim: per group of 32,
+ * scale = max(max-min, 1e-8)/(2^bits-1) (fp32, IEEE divide), code =
+ * clamp(round_half_even((x-min)/scale)); element e -> word e/(32/bits), bit
+ * offset (e%(32/bits))*bits. x [...,N] f16/bf16/f32 (1-4 dims); code int32
+ * [...,N*bits/32]; scale, mn [...,N/32] in x's dtype (all contiguous).
+ * ref: triton_quantize_and_pack_along_last_dim (external KIVI, called at
+ *      benchmarks/kivi_latency.py:123; layout pinned by :26-35) */
+int bd_kivi_pack_last_dim(const bd_tensor* x, int group_size, int bits, const bd_tensor* code,
+                          const bd_tensor* scale, const bd_tensor* mn, bd_stream_t stream);
+
+/* out[b,hq,m,n] = sum_k fA[b,hq,m,k] * (code(qB)[b,hq/G,k,n]*scales + zeros), f16.
+ * fA f16 [B,Hq,M,K]; qB int32 [B,Hk,K,N*bits/32]; scales,zeros f16
+ * [B,Hk,K,N/group_size]; out f16 [B,Hq,M,N].
+ * ref: cuda_bmm_fA_qB_outer (external KIVI, called at benchmarks/kivi_latency.py:67,83) */
+int bd_kivi_gemv_outer(int group_size, const bd_tensor* fA, const bd_tensor* qB, const bd_tensor* scales,
+                       const bd_tensor* zeros, int bits, const bd_tensor* out, bd_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Pass-1 scores [B,Hq,S] f32 = scaling * q.k over all keys.
+ * score_bits 16: k bf16 [B,Hk,S,D];  8: k fp8 e4m3 [B,Hk,S,D];
+ * 4 / 2: k uint8 [B,Hk,S,D*bits/8] (channel c at byte c/(8/bits), shift
+ * (c%(8/bits))*bits), key = code*scale + zero with scale/zero bf16 or f16
+ * [B,Hk,S,D/group_size] (token-major, contiguous per (b,h)).
+ * ref: sparse_score_scalar  src/attention_kernels.py:1113
+ *      sparse_score_packed  src/attention_kernels.py:1199 */
+int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* scale, const bd_tensor* zero,
+                    float scaling, int score_bits, int group_size, const bd_tensor* scores, bd_stream_t stream);
+
+/* Per-token groups of group_size channels: fp32 min/max, scale =
+ * max(max-min,1e-8)/(2^bits-1), code = clamp(round_half_even((k-min)/scale)),
+ * 8/bits codes per byte, low bits first. k [B,H,S,D] bf16/f16/f32; packed u8
+ * [B,H,S,D*bits/8]; scale, zero (= min) [B,H,S,D/group_size] in k's dtype.
+ * ref: quantize_and_pack_score_keys  src/attention_kernels.py:1225 */
+int bd_pack_score_keys(const bd_tensor* k, int score_bits, int group_size, const bd_tensor* packed,
+                       const bd_tensor* scale, const bd_tensor* zero, bd_stream_t stream);
+
+/* Top-k along the last dim of scores [R] / [R0,R1] / [B,R1,n] f32: keys larger
+ * first, equal values keep the lower index first (a stable descending sort).
+ * sorted=1 orders the k winners by (value desc, index asc); sorted=0 returns
+ * them in ascending index order. values (optional) f32 and indices int64/int32
+ * have k in the last dim. k <= n.
+ * ref: scores.topk(kb, dim=-1)  src/attention_kernels.py:1069,1262
+ *      select_topk('exact')     benchmarks/sparse_attention.py:287-309 */
+int bd_topk(const bd_tensor* scores, int k, int sorted, const bd_tensor* values, const bd_tensor* indices,
+            bd_stream_t stream);
+
+/* Exact softmax(scaling * q.k_sel) . v_sel over per-query-head key positions
+ * idx [B,Hq,kb] (int32/int64; duplicates count once per occurrence, positions
+ * outside [0,S) are skipped). q [B,Hq,D]; k,v [B,Hk,S,D] bf16 or fp8 e4m3;
+ * out [B,Hq,D] (bf16 for fp8 values in the reference).
+ * ref: sparse_gather_attn  src/attention_kernels.py:1037; attend_topk
+ *      benchmarks/sparse_attention.py:367 */
+size_t bd_sparse_gather_attn_workspace(const bd_tensor* q, const bd_tensor* idx);
+int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
+                          float scaling, const bd_tensor* out, void* workspace, size_t workspace_bytes,
+                          bd_stream_t stream);
+
+/* Quest page metadata: elementwise min / max of each page of `page` tokens
+ * (a ragged last page covers the real tokens only). k [B,H,S,D]; kmin, kmax
+ * [B,H,ceil(S/page),D] in k's dtype.
+ * ref: _quest_select  benchmarks/sparse_attention.py:334-341 */
+int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, const bd_tensor* kmax,
+                         bd_stream_t stream);
+/* bound[b,hq,p] = scaling * sum_d max(q_d*kmin_pd, q_d*kmax_pd) (fp32), with
+ * pages p >= force_from_page set to +inf (the reference's forced recent window;
+ * pass a value >= np for none). kmin/kmax bf16 [B,Hk,np,D]; bounds f32 [B,Hq,np].
+ * ref: benchmarks/sparse_attention.py:342-355 */
+int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* kmax, float scaling,
+                         int force_from_page, const bd_tensor* bounds, bd_stream_t stream);
+/* Page bounds -> top npick = min(max(1,ceil(kb/page)), np) pages (lower page
+ * wins ties, ordered by bound desc) -> token indices page*p + o clamped to S-1:
+ * idx [B,Hq,npick*page] int32/int64.
+ * ref: _quest_select  benchmarks/sparse_attention.py:356-364 */
+size_t bd_quest_select_workspace(const bd_tensor* q, const bd_tensor* kmin, int kb, int page);
+int bd_quest_select(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* kmax, int S, int kb, int page,
+                    float scaling, int force_from_page, const bd_tensor* idx_out, void* workspace,
+                    size_t workspace_bytes, bd_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
