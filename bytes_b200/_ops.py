@@ -118,7 +118,7 @@ def lse_combine(m, l, o, out_dtype=torch.bfloat16):
     return out
 
 
-def kivi_decode(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, bits, group_size, scaling, out):
+def kivi_decode(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, bits, group_size, scaling, out, stages=7):
     N.require_cuda(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, out)
     Kq, Vq = rows_aligned(Kq, 16), rows_aligned(Vq, 16)
     Ks, Km, Vs, Vm = (rows_aligned(t, 8) for t in (Ks, Km, Vs, Vm))
@@ -129,9 +129,9 @@ def kivi_decode(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, bits, group_size, scaling, o
         ctypes.byref(ds[0]), ctypes.byref(ds[1]), ctypes.byref(ds[4]), int(bits))
     buf, nb = _ws(nws, Q3.device)
     do = N.desc(out)
-    rc = _fn("bd_kivi_decode_attn", [P] * 9 + [I, I, F, P, VP, SZ, VP])(
+    rc = _fn("bd_kivi_decode_attn_stages", [P] * 9 + [I, I, F, P, VP, SZ, I, VP])(
         *[ctypes.byref(d) for d in ds], int(bits), int(group_size), float(scaling), ctypes.byref(do), _ptr(buf), nb,
-        N.stream_of(Q3))
+        int(stages), N.stream_of(Q3))
     N.check(rc, "bd_kivi_decode_attn")
     return out
 
@@ -299,3 +299,89 @@ def quest_select(q3, kmin, kmax, S, kb, page, scaling, force_from_page=None, idx
         ctypes.byref(di), _ptr(buf), nb, N.stream_of(q3))
     N.check(rc, "bd_quest_select")
     return idx
+
+
+def pq_decode(lut, k_idx, v=None, v_scale=None, v_idx=None, v_cent=None, k_out=None, q_out=None,
+              block_table=None, context_lens=None, block_size=0, out_dtype=torch.bfloat16):
+    """PQ-LUT decode; returns [B,Hq,D]."""
+    N.require_cuda(lut, k_idx, v, v_scale, v_idx, v_cent, k_out, q_out, block_table, context_lens)
+    lut = lut if lut.dtype == torch.float32 else lut.float()
+    k_idx = inner_contig(k_idx)
+    if v is not None:
+        v = rows_aligned(v)
+    if v_cent is not None and v_cent.dtype != torch.float32:
+        v_cent = v_cent.float()
+    if k_out is not None and k_out.shape[-1] == 0:
+        k_out, q_out = None, None
+    if k_out is not None and k_out.dtype not in (torch.bfloat16, torch.float16):
+        k_out = k_out.to(torch.bfloat16)
+    if block_table is not None:
+        block_table = block_table.to(torch.int32)
+        context_lens = context_lens.to(torch.int32)
+    B, Hq = lut.shape[:2]
+    D = v.shape[-1] if v is not None else v_cent.shape[0] * v_cent.shape[2]
+    out = torch.empty(B, Hq, D, dtype=out_dtype, device=lut.device)
+    ds = {n: N.desc(t) for n, t in dict(lut=lut, k_idx=k_idx, k_out=k_out, q_out=q_out, v=v, v_scale=v_scale,
+                                        v_idx=v_idx, v_cent=v_cent, bt=block_table, cl=context_lens,
+                                        out=out).items()}
+    nws = _fn("bd_pq_decode_workspace", [P, P, P, P, P, P, P, I], SZ)(
+        N.ref(ds["lut"]), N.ref(ds["k_idx"]), N.ref(ds["v"]), N.ref(ds["v_idx"]), N.ref(ds["v_cent"]),
+        N.ref(ds["bt"]), N.ref(ds["cl"]), int(block_size))
+    buf, nb = _ws(nws, lut.device)
+    rc = _fn("bd_pq_decode", [P] * 10 + [I, P, VP, SZ, VP])(
+        N.ref(ds["lut"]), N.ref(ds["k_idx"]), N.ref(ds["k_out"]), N.ref(ds["q_out"]), N.ref(ds["v"]),
+        N.ref(ds["v_scale"]), N.ref(ds["v_idx"]), N.ref(ds["v_cent"]), N.ref(ds["bt"]), N.ref(ds["cl"]),
+        int(block_size), N.ref(ds["out"]), _ptr(buf), nb, N.stream_of(lut))
+    N.check(rc, "bd_pq_decode")
+    return out
+
+
+def pq_scores(lut, k_idx, k_out=None, q_out=None):
+    N.require_cuda(lut, k_idx, k_out, q_out)
+    lut = lut if lut.dtype == torch.float32 else lut.float()
+    k_idx = inner_contig(k_idx)
+    if k_out is not None and k_out.shape[-1] == 0:
+        k_out, q_out = None, None
+    if k_out is not None and k_out.dtype not in (torch.bfloat16, torch.float16):
+        k_out = k_out.to(torch.bfloat16)
+    B, Hq = lut.shape[:2]
+    S = k_idx.shape[2]
+    scores = torch.empty(B, Hq, S, dtype=torch.float32, device=lut.device)
+    ds = [N.desc(t) for t in (lut, k_idx, k_out, q_out, scores)]
+    rc = _fn("bd_pq_scores", [P, P, P, P, P, VP])(N.ref(ds[0]), N.ref(ds[1]), N.ref(ds[2]), N.ref(ds[3]),
+                                                  N.ref(ds[4]), N.stream_of(lut))
+    N.check(rc, "bd_pq_scores")
+    return scores
+
+
+def pq_build_lut(q3, centroids):
+    N.require_cuda(q3, centroids)
+    centroids = centroids if centroids.dtype == torch.float32 else centroids.float()
+    B, H, D = q3.shape
+    M, K, _ = centroids.shape
+    lut = torch.empty(B, H, M, K, dtype=torch.float32, device=q3.device)
+    ds = [N.desc(t) for t in (q3, centroids, lut)]
+    rc = _fn("bd_pq_build_lut", [P, P, P, VP])(*[ctypes.byref(d) for d in ds], N.stream_of(q3))
+    N.check(rc, "bd_pq_build_lut")
+    return lut
+
+
+def pq_encode(x2, centroids, codes_dtype=torch.int64):
+    N.require_cuda(x2, centroids)
+    x2 = inner_contig(x2)
+    centroids = centroids if centroids.dtype == torch.float32 else centroids.float()
+    codes = torch.empty(x2.shape[0], centroids.shape[0], dtype=codes_dtype, device=x2.device)
+    ds = [N.desc(t) for t in (x2, centroids, codes)]
+    rc = _fn("bd_pq_encode", [P, P, P, VP])(*[ctypes.byref(d) for d in ds], N.stream_of(x2))
+    N.check(rc, "bd_pq_encode")
+    return codes
+
+
+def asym_fakequant_5d(x5, levels):
+    """x5: a 5-d strided view (o0, o1, o2, group axis, inner) -> contiguous fake-quant output."""
+    N.require_cuda(x5)
+    y = torch.empty(x5.shape, dtype=x5.dtype, device=x5.device)
+    dx, dy = N.desc(x5), N.desc(y)
+    rc = _fn("bd_asym_fakequant", [P, I, P, VP])(ctypes.byref(dx), int(levels), ctypes.byref(dy), N.stream_of(x5))
+    N.check(rc, "bd_asym_fakequant")
+    return y

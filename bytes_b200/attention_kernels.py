@@ -120,3 +120,91 @@ def topk(scores, k, sorted=True):
     (values fp32, indices int64).
     """
     return _ops.topk(scores, k, sorted=sorted)
+
+
+def _v_for_pq(v):
+    return v if v.dtype in (torch.bfloat16, torch.float8_e4m3fn, torch.int8) else v.to(torch.bfloat16)
+
+
+def decode_attn_dequant(q, k_idx, centroids, v, d_sub=8):
+    """Dense decode over PQ-reconstructed keys, no scale. ref: src/attention_kernels.py:267-296.
+
+    Served as LUT[b,h,j,c] = q_j . centroids[j,c] followed by the LUT path (the same sum
+    over channels, grouped by subspace). Output dtype q.dtype.
+    """
+    q3 = _squeeze_q(q)
+    lut = _ops.pq_build_lut(q3, centroids)
+    out = _ops.pq_decode(lut, k_idx, v=_v_for_pq(v), out_dtype=q.dtype)
+    return out.unsqueeze(2)
+
+
+def decode_attn_pq_lut(lut, k_idx, v):
+    """LUT-scored decode (scale folded into the LUT by the caller). ref: src/attention_kernels.py:365-392.
+
+    lut [B,H_q,M,K] fp32; k_idx uint8 [B,H_k,S,M]; v [B,H_k,S,D] -> [B,H_q,1,D] in v.dtype.
+    """
+    out = _ops.pq_decode(lut, k_idx, v=_v_for_pq(v), out_dtype=v.dtype)
+    return out.unsqueeze(2)
+
+
+def decode_attn_pq_lut_kv(lut, k_idx, v_idx, v_centroids, d_sub_v=8):
+    """LUT scores + PQ-reconstructed values. ref: src/attention_kernels.py:471-500.
+
+    Output dtype v_centroids.dtype.
+    """
+    out = _ops.pq_decode(lut, k_idx, v_idx=v_idx, v_cent=v_centroids, out_dtype=v_centroids.dtype)
+    return out.unsqueeze(2)
+
+
+def paged_attn_pq_lut_kv(lut, k_idx_paged, v_idx_paged, v_centroids, block_table, context_lens, block_size=16):
+    """Paged LUT-KV decode. ref: src/attention_kernels.py:588-619 (context_lens per sequence,
+    token t at block_table[b, t // block_size], offset t % block_size)."""
+    out = _ops.pq_decode(lut, k_idx_paged, v_idx=v_idx_paged, v_cent=v_centroids, block_table=block_table,
+                         context_lens=context_lens, block_size=block_size, out_dtype=v_centroids.dtype)
+    return out.unsqueeze(2)
+
+
+def _asym_out(v):
+    return torch.bfloat16 if v.dtype == torch.float8_e4m3fn else v.dtype
+
+
+def decode_attn_pq_lut_asym(lut, k_idx, k_out, q_out, v, BLOCK_N=256):
+    """LUT scores + exact outlier channels q_out.k_out; fp8/bf16 V. ref: src/attention_kernels.py:713-750."""
+    out = _ops.pq_decode(lut, k_idx, v=_v_for_pq(v), k_out=k_out, q_out=q_out, out_dtype=_asym_out(v))
+    return out.unsqueeze(2)
+
+
+def paged_attn_pq_lut_asym(lut, k_idx_paged, k_out_paged, q_out, v_paged, block_table, context_lens,
+                           block_size=16, BLOCK_N=256):
+    """Paged asymmetric PQ-LUT decode. ref: src/attention_kernels.py:858-898."""
+    out = _ops.pq_decode(lut, k_idx_paged, v=_v_for_pq(v_paged), k_out=k_out_paged, q_out=q_out,
+                         block_table=block_table, context_lens=context_lens, block_size=block_size,
+                         out_dtype=_asym_out(v_paged))
+    return out.unsqueeze(2)
+
+
+def sparse_score_pq_lut_asym(lut, k_idx, k_out, q_out, BLOCK_N=256):
+    """Pass-1 LUT + outlier scores [B,H_q,S] fp32. ref: src/attention_kernels.py:960-984."""
+    return _ops.pq_scores(lut, k_idx, k_out, q_out)
+
+
+def sparse_decode_pq_lut(lut, k_idx, k_out, q_out, q, k, v, frac, scaling, BLOCK_N=256, BLOCK_K=64):
+    """LUT-score all keys -> top-kb (lower index wins ties) -> exact gather attention.
+
+    ref: src/attention_kernels.py:1062-1070.
+    """
+    scores = sparse_score_pq_lut_asym(lut, k_idx, k_out, q_out)
+    kb = _budget(frac, scores.shape[-1])
+    _, idx = _ops.topk(scores, kb, sorted=False, want_values=False, idx_dtype=torch.int32)
+    return sparse_gather_attn(q, k, v, idx, scaling)
+
+
+def decode_attn_pq_lut_int8v(lut, k_idx, v_int8, v_scale):
+    """Config-2 extension (no counterpart in the reference): LUT-scored keys with int8
+    values and a per-token f16 scale (V = v_int8 * v_scale). lut [B,H_q,M,K];
+    k_idx uint8 [B,H_k,S,M]; v_int8 [B,H_k,S,D]; v_scale f16 [B,H_k,S] -> bf16 [B,H_q,1,D].
+    """
+    if v_scale.dtype != torch.float16:
+        v_scale = v_scale.to(torch.float16)
+    out = _ops.pq_decode(lut, k_idx, v=v_int8, v_scale=v_scale, out_dtype=torch.bfloat16)
+    return out.unsqueeze(2)

@@ -628,10 +628,25 @@ size_t bd_kivi_decode_attn_workspace(const bd_tensor* Q, const bd_tensor* Kq, co
   return partials_bytes(size_t(Q->shape[0] * Q->shape[1]), std::max(1, pl.n_kivi + pl.n_res), 128);
 }
 
+int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale,
+                               const bd_tensor* K_mn, const bd_tensor* K_residual, const bd_tensor* Vq,
+                               const bd_tensor* V_scale, const bd_tensor* V_mn, const bd_tensor* V_residual, int bits,
+                               int group_size, float scaling, const bd_tensor* out, void* workspace,
+                               size_t workspace_bytes, int stages, bd_stream_t stream);
+
 int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale, const bd_tensor* K_mn,
                         const bd_tensor* K_residual, const bd_tensor* Vq, const bd_tensor* V_scale,
                         const bd_tensor* V_mn, const bd_tensor* V_residual, int bits, int group_size, float scaling,
                         const bd_tensor* out, void* workspace, size_t workspace_bytes, bd_stream_t stream) {
+  return bd_kivi_decode_attn_stages(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_residual, bits, group_size,
+                                    scaling, out, workspace, workspace_bytes, 7, stream);
+}
+
+int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale,
+                               const bd_tensor* K_mn, const bd_tensor* K_residual, const bd_tensor* Vq,
+                               const bd_tensor* V_scale, const bd_tensor* V_mn, const bd_tensor* V_residual, int bits,
+                               int group_size, float scaling, const bd_tensor* out, void* workspace,
+                               size_t workspace_bytes, int stages, bd_stream_t stream) {
   using namespace bd;
   int rc;
   if ((rc = check_kivi_inputs(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_residual, bits, group_size)))
@@ -660,7 +675,7 @@ int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor
     if ((rc = cuda_check(cudaGetLastError(), "empty_partials_kernel launch"))) return rc;
     return launch_combine(part, int(B), int(Hq), 128, out, st);
   }
-  if (pl.n_kivi > 0) {
+  if (pl.n_kivi > 0 && (stages & 1)) {
     KiviParams kp{};
     kp.q = Q->data; kp.q_sb = Q->stride[0]; kp.q_sh = Q->stride[1]; kp.q_dtype = Q->dtype;
     kp.kq = static_cast<const uint32_t*>(Kq->data); kp.kq_sb = Kq->stride[0]; kp.kq_sh = Kq->stride[1]; kp.kq_sc = Kq->stride[2];
@@ -676,9 +691,10 @@ int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor
     rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, st) : launch_kivi<4>(kp, pl.n_kivi, st);
     if (rc) return rc;
   }
-  if (pl.n_res > 0) {
+  if (pl.n_res > 0 && (stages & 2)) {
     if ((rc = launch_dense_partials(Q, K_residual, V_residual, scaling, part, pl.n_kivi, pl.n_res, st))) return rc;
   }
+  if (!(stages & 4)) return BD_OK;
   return launch_combine(part, int(B), int(Hq), 128, out, st);
 }
 

@@ -104,6 +104,16 @@ int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor
                         const bd_tensor* V_mn, const bd_tensor* V_residual, int bits, int group_size, float scaling,
                         const bd_tensor* out, void* workspace, size_t workspace_bytes, bd_stream_t stream);
 
+/* Profiling form of bd_kivi_decode_attn: launches only the selected stages of the
+ * step (bit 0: packed-cache split kernel, bit 1: residual-window kernel, bit 2:
+ * combine). stages = 7 is bd_kivi_decode_attn. Used to time kernels one by one.
+ * ref: none (measurement helper around kivi_decode_attn). */
+int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale,
+                               const bd_tensor* K_mn, const bd_tensor* K_residual, const bd_tensor* Vq,
+                               const bd_tensor* V_scale, const bd_tensor* V_mn, const bd_tensor* V_residual, int bits,
+                               int group_size, float scaling, const bd_tensor* out, void* workspace,
+                               size_t workspace_bytes, int stages, bd_stream_t stream);
+
 /* Group-wise asymmetric quantize + pack along the last dim: per group of 32,
  * scale = max(max-min, 1e-8)/(2^bits-1) (fp32, IEEE divide), code =
  * clamp(round_half_even((x-min)/scale)); element e -> word e/(32/bits), bit
@@ -181,6 +191,49 @@ size_t bd_quest_select_workspace(const bd_tensor* q, const bd_tensor* kmin, int 
 int bd_quest_select(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* kmax, int S, int kb, int page,
                     float scaling, int force_from_page, const bd_tensor* idx_out, void* workspace,
                     size_t workspace_bytes, bd_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * PQ-LUT decode: scores[t] = sum_j lut[b,hq,j,k_idx[t,j]] (+ sum_c q_out[hq,c] *
+ * k_out[t,c] when k_out is given, C_out <= 8), softmax, then P.V with V one of:
+ * bf16 / fp8 e4m3 [.,Hk,S,D] (v), int8 [B,Hk,S,D] with f16 per-token v_scale
+ * [B,Hk,S], or PQ codes v_idx u8 [.,Hk,S,M_v] + v_centroids f32 [M_v,K_v,d_sub_v].
+ * Paged when block_table int32 [B,max_blocks] and context_lens int32 [B] are
+ * given (k_idx / k_out / values then [num_blocks,Hk,block_size,.]).
+ * lut f32 [B,Hq,M,K] (M <= 64, K <= 256); k_idx u8; out [B,Hq,D].
+ * ref: decode_attn_pq_lut        src/attention_kernels.py:365
+ *      decode_attn_pq_lut_kv     src/attention_kernels.py:471
+ *      paged_attn_pq_lut_kv      src/attention_kernels.py:588
+ *      decode_attn_pq_lut_asym   src/attention_kernels.py:713
+ *      paged_attn_pq_lut_asym    src/attention_kernels.py:858
+ *      (int8 values: configuration extension, no counterpart in the reference) */
+size_t bd_pq_decode_workspace(const bd_tensor* lut, const bd_tensor* k_idx, const bd_tensor* v,
+                              const bd_tensor* v_idx, const bd_tensor* v_centroids, const bd_tensor* block_table,
+                              const bd_tensor* context_lens, int block_size);
+int bd_pq_decode(const bd_tensor* lut, const bd_tensor* k_idx, const bd_tensor* k_out, const bd_tensor* q_out,
+                 const bd_tensor* v, const bd_tensor* v_scale, const bd_tensor* v_idx, const bd_tensor* v_centroids,
+                 const bd_tensor* block_table, const bd_tensor* context_lens, int block_size, const bd_tensor* out,
+                 void* workspace, size_t workspace_bytes, bd_stream_t stream);
+/* Scores only [B,Hq,S] f32 (LUT + outliers).
+ * ref: sparse_score_pq_lut_asym  src/attention_kernels.py:960 */
+int bd_pq_scores(const bd_tensor* lut, const bd_tensor* k_idx, const bd_tensor* k_out, const bd_tensor* q_out,
+                 const bd_tensor* scores, bd_stream_t stream);
+/* lut[b,h,j,c] = sum_i q[b,h,j*d_sub+i] * centroids[j,c,i]; q [B,H,D]; centroids f32
+ * [M,K,d_sub]; lut f32 [B,H,M,K] contiguous.
+ * ref: the LUT einsum of benchmarks/test_correctness.py:181-182 and the key
+ *      reconstruction of decode_attn_dequant src/attention_kernels.py:267 */
+int bd_pq_build_lut(const bd_tensor* q, const bd_tensor* centroids, const bd_tensor* lut, bd_stream_t stream);
+/* codes[n,j] = argmin_c ||x[n, j*d_sub:(j+1)*d_sub] - centroids[j,c]||^2 (fp32, first
+ * index on ties). x [N,D] f32/bf16/f16; codes [N,M] u8 or int64.
+ * ref: ProductQuantizer.quantize  src/quantization.py:160 */
+int bd_pq_encode(const bd_tensor* x, const bd_tensor* centroids, const bd_tensor* codes, bd_stream_t stream);
+
+/* Asymmetric uniform fake-quant over axis 3 of a 5-d strided view x (o0,o1,o2,
+ * group,inner): y = clamp(round((x-min)/scale),0,levels-1)*scale + min with scale =
+ * clamp(max-min,1e-8)/(levels-1), every step rounded in x's dtype (f32/bf16/f16);
+ * y contiguous, same shape and dtype.
+ * ref: _asym_uniform_fakequant  src/quantization.py:432; KIVIQuantizer
+ *      quantize_key / quantize_value  src/quantization.py:468-501 */
+int bd_asym_fakequant(const bd_tensor* x, int levels, const bd_tensor* y, bd_stream_t stream);
 
 #ifdef __cplusplus
 }
