@@ -174,6 +174,24 @@ def kivi_gemv(group_size, fA, qB, scales, zeros, bits):
     return out
 
 
+def _token_major_aligned(t):
+    """[B,H,S,G] with contiguous (S,G) rows per (b,h) and every (b,h) block starting on a
+    16-byte boundary (the score kernel stages whole tiles of it with 16-byte copies)."""
+    B, H, S, G = t.shape
+    es = t.element_size()
+    ok = (t.stride(3) == 1 or G == 1) and (t.stride(2) == G or S == 1) and t.data_ptr() % 16 == 0
+    ok = ok and (H == 1 or (t.stride(1) * es) % 16 == 0) and (B == 1 or (t.stride(0) * es) % 16 == 0)
+    if ok:
+        return t
+    per = max(1, 16 // (G * es)) if (G * es) < 16 else 1
+    S_pad = (S + per - 1) // per * per
+    while (S_pad * G * es) % 16:
+        S_pad += 1
+    buf = torch.zeros(B, H, S_pad, G, dtype=t.dtype, device=t.device)
+    buf[:, :, :S] = t
+    return buf[:, :, :S]
+
+
 def sparse_score(q3, k, scale, zero, scaling, bits, group_size):
     """q3 [B,Hq,D]; k bf16/fp8 [B,Hk,S,D] or packed u8 -> scores [B,Hq,S] f32."""
     N.require_cuda(q3, k, scale, zero)
@@ -187,8 +205,8 @@ def sparse_score(q3, k, scale, zero, scaling, bits, group_size):
         if scale.dtype not in (torch.bfloat16, torch.float16):
             scale = scale.to(torch.bfloat16)
             zero = zero.to(torch.bfloat16)
-        scale = scale.contiguous()
-        zero = zero.contiguous()
+        scale = _token_major_aligned(scale)
+        zero = _token_major_aligned(zero)
     scores = torch.empty(B, Hq, S, dtype=torch.float32, device=q3.device)
     ds = [N.desc(q3), N.desc(k), N.desc(scale), N.desc(zero), N.desc(scores)]
     rc = _fn("bd_sparse_score", [P, P, P, P, F, I, I, P, VP])(

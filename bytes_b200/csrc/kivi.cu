@@ -93,7 +93,7 @@ __device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) { return *reinterp
 __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 template <int BITS>
-__global__ void __launch_bounds__(kWarpsK * 32, 3) kivi_decode_kernel(const KiviParams p) {
+__global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const KiviParams p) {
   using L = KL<BITS>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* tsm = smem + kStagesK * L::STAGE;  // transposed key scale / min of the current tile
@@ -482,7 +482,7 @@ int kivi_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t Sq, int64_t R, KiviPlan
   pl->head_chunks = (G + 7) / 8;
   const int64_t ntiles = (Sq + kTile - 1) / kTile;
   const int64_t pairs = B * Hk * pl->head_chunks;
-  const int64_t slots = 3LL * num_sms();
+  const int64_t slots = 4LL * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
   const int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;

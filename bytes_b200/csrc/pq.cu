@@ -578,7 +578,7 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
       else if (v->dtype == BD_F8E4M3) vk = V_FP8;
       else if (v->dtype == BD_I8) {
         vk = V_INT8;
-        if ((rc = check_tensor(v_scale, "v_scale", 3, BD_F16))) return rc;
+        if (!ws_query && (rc = check_tensor(v_scale, "v_scale", 3, BD_F16))) return rc;
       } else return fail(BD_ERR_DTYPE, "v must be bf16, fp8 e4m3 or int8 (+ v_scale)");
       if ((rc = check_rows_aligned(v, "v"))) return rc;
     }

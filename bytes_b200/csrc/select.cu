@@ -278,8 +278,11 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
     return p.idx64 ? reinterpret_cast<const int64_t*>(p.idx)[off] : int64_t(reinterpret_cast<const int32_t*>(p.idx)[off]);
   };
   constexpr int WPL = CPL * ELT / 4;  // 32-bit words per lane per row (2, 4 or 8)
-  for (int r = r_begin + gid; r < r_end; r += 16) {
-    const int64_t t = row_index(r);
+  // all four 8-lane row groups of a warp iterate together (the shuffles below need every
+  // lane of the warp); a group whose row is past the end is predicated off
+  for (int rw = r_begin + warp * 4; rw < r_end; rw += 16) {
+    const int r = rw + grp;
+    const int64_t t = r < r_end ? row_index(r) : -1;
     const bool ok = t >= 0 && t < p.S;
     uint32_t kw[WPL], vw[WPL];
 #pragma unroll
