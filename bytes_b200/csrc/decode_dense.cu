@@ -20,6 +20,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 namespace bd {
 
@@ -542,6 +543,34 @@ int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* 
   return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
 }
 
+// ---- static scratch for bd_decode_attn_noalloc --------------------------------------
+// Some callers have no way to allocate device memory for us: a serving runtime that
+// reserves all of HBM for its KV pages at start-up and forbids later cudaMalloc, or a
+// plain C / FFI host that only owns the q/k/v/out buffers. For them the split partials
+// live in this fixed array, which every GPU that loads the library keeps (4 MiB) until
+// the process exits. In host code the symbol is only a stand-in, so its device address
+// is looked up once per device with cudaGetSymbolAddress.
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[64] = {nullptr};
+
+int static_scratch_address(void** ptr) {
+  int dev = 0;
+  int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(BD_ERR_UNSUPPORTED, "device index out of range for the static scratch");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* a = nullptr;
+    if ((rc = cuda_check(cudaGetSymbolAddress(&a, g_decode_scratch), "cudaGetSymbolAddress(static scratch)")))
+      return rc;
+    g_scratch_addr[dev] = a;
+  }
+  *ptr = g_scratch_addr[dev];
+  return BD_OK;
+}
+
 }  // namespace bd
 
 extern "C" {
@@ -592,6 +621,28 @@ int bd_decode_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, c
   c.mode = 0;
   lse_combine_kernel<<<int(rows), pl.D, pl.n_splits * sizeof(float), st>>>(c);
   return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+}
+
+// Variant of bd_decode_attn for callers that cannot hand us a workspace: its split
+// partials go to a fixed, file-scope device buffer instead (see static_scratch_address).
+int bd_decode_attn_noalloc(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* out,
+                           float scaling, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if ((rc = validate(q, k, v))) return rc;
+  Plan pl;
+  if ((rc = make_plan(q, k, &pl))) return rc;
+  if (pl.n_splits == 1 || q->shape[0] * q->shape[1] == 0)
+    return bd_decode_attn(q, k, v, out, scaling, nullptr, 0, stream);  // no scratch needed
+  const size_t need = ws_bytes(q, pl);
+  if (need > kStaticScratchBytes)
+    return fail(BD_ERR_UNSUPPORTED, "this call needs " + std::to_string(need) +
+                                        " bytes of split scratch but the static scratch holds " +
+                                        std::to_string(kStaticScratchBytes) +
+                                        "; use bd_decode_attn with a caller workspace");
+  void* scratch = nullptr;
+  if ((rc = static_scratch_address(&scratch))) return rc;
+  return bd_decode_attn(q, k, v, out, scaling, scratch, kStaticScratchBytes, stream);
 }
 
 int bd_decode_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,

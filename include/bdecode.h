@@ -71,6 +71,19 @@ int bd_decode_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v,
                    const bd_tensor* out, float scaling, void* workspace,
                    size_t workspace_bytes, bd_stream_t stream);
 
+/* bd_decode_attn without a caller workspace: no counterpart in the reference. For
+ * callers that cannot allocate device memory for us (a serving runtime that reserves
+ * all HBM for its KV pages at start-up, or a plain C / FFI host that only owns q, k, v
+ * and out), the split partials go to a fixed 4 MiB device array inside the library,
+ * which every GPU that loads the library keeps until the process exits. Calls needing
+ * more split scratch than that are rejected with BD_ERR_UNSUPPORTED (use
+ * bd_decode_attn then); nothing is allocated. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress): make it before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU (other streams, other
+ * host threads) race; serialise them. Every byte a call reads is written by that call. */
+int bd_decode_attn_noalloc(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v,
+                           const bd_tensor* out, float scaling, bd_stream_t stream);
+
 /* Per-shard partials for split-KV across GPUs: m,l [B,Hq] f32 (running max of
  * scaling*q.k and softmax denominator), o [B,Hq,D] f32 (un-normalised
  * numerator). An empty shard yields m=-inf, l=0, o=0. Combine the shards of

@@ -1,0 +1,79 @@
+"""bd_decode_attn_noalloc: decode attention for callers that cannot allocate device memory.
+
+A serving runtime that has reserved all of HBM for its KV pages, or a plain C / FFI host
+holding only the q/k/v/out buffers, cannot hand the engine a workspace. This entry point
+keeps its split partials in a fixed device array inside the library instead. The test
+calls it through the C ABI twice in a row (the array keeps the previous call's contents)
+and compares each result with bd_decode_attn given a normal workspace.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from bytes_b200 import _native as N
+
+pytestmark = pytest.mark.gpu
+
+
+def _call_with_workspace(lib, q3, k, v, out):
+    dq, dk, dv, do = N.desc(q3), N.desc(k), N.desc(v), N.desc(out)
+    f = lib.bd_decode_attn_workspace
+    f.restype = ctypes.c_size_t
+    nws = f(ctypes.byref(dq), ctypes.byref(dk))
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=q3.device)
+    rc = lib.bd_decode_attn(ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(do),
+                            ctypes.c_float(1.0), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(nws),
+                            N.stream_of(q3))
+    assert rc == 0, lib.bd_last_error()
+
+
+def _call_noalloc(lib, q3, k, v, out):
+    dq, dk, dv, do = N.desc(q3), N.desc(k), N.desc(v), N.desc(out)
+    rc = lib.bd_decode_attn_noalloc(ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(do),
+                                    ctypes.c_float(1.0), N.stream_of(q3))
+    assert rc == 0, lib.bd_last_error()
+
+
+def test_noalloc_matches_workspace_entry_point_twice(cuda):
+    lib = N.lib()
+    lib.bd_decode_attn.restype = ctypes.c_int
+    lib.bd_decode_attn_noalloc.restype = ctypes.c_int
+    g = torch.Generator().manual_seed(77)
+    # two different problems in a row: the second must not see the first one's partials
+    for (B, Hq, Hk, S) in ((1, 28, 4, 8192), (2, 8, 2, 3000)):
+        q3 = torch.randn(B, Hq, 128, generator=g).bfloat16().to(cuda)
+        k = torch.randn(B, Hk, S, 128, generator=g).bfloat16().to(cuda)
+        v = torch.randn(B, Hk, S, 128, generator=g).bfloat16().to(cuda)
+        ref = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=cuda)
+        out = torch.empty_like(ref)
+        _call_with_workspace(lib, q3, k, v, ref)
+        _call_noalloc(lib, q3, k, v, out)
+        torch.cuda.synchronize()
+        d = (out.float() - ref.float()).abs()
+        assert torch.isfinite(out.float()).all()
+        assert d.max().item() <= 2e-2 and d.mean().item() <= 1e-3
+
+
+def test_noalloc_rejects_oversized_scratch_on_host():
+    lib = N.lib()
+    lib.bd_decode_attn_noalloc.restype = ctypes.c_int
+
+    def fake(shape, dt, ptr=0x100000):
+        d = N.BdTensor()
+        d.data, d.dtype, d.ndim = ptr, dt, len(shape)
+        s = 1
+        for i in range(len(shape) - 1, -1, -1):
+            d.shape[i], d.stride[i] = shape[i], s
+            s *= shape[i]
+        return d
+
+    # 4096 query rows split many ways need far more than the 4 MiB static scratch
+    q = fake((64, 64, 128), N.BD_BF16)
+    k = fake((64, 1, 1 << 20, 128), N.BD_BF16)
+    out = fake((64, 64, 128), N.BD_BF16)
+    rc = lib.bd_decode_attn_noalloc(ctypes.byref(q), ctypes.byref(k), ctypes.byref(k), ctypes.byref(out),
+                                    ctypes.c_float(1.0), ctypes.c_void_p(0))
+    if rc == 0:
+        pytest.skip("plan needed no split scratch on this device")
+    assert rc == 7 and b"static scratch" in lib.bd_last_error()
