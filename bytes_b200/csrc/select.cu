@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
     const int64_t off = int64_t(b) * p.i_sb + int64_t(hq) * p.i_sh + r;
     return p.idx64 ? reinterpret_cast<const int64_t*>(p.idx)[off] : int64_t(reinterpret_cast<const int32_t*>(p.idx)[off]);
   };
-  constexpr int WPL = CPL * ELT / 4;  // 32-bit words per lane per row (2, 4 or 8)
+  constexpr int WPL = CPL * ELT / 4;  // 32-bit words per lane per row (1, 2, 4 or 8)
   // all four 8-lane row groups of a warp iterate together (the shuffles below need every
   // lane of the warp); a group whose row is past the end is predicated off
   for (int rw = r_begin + warp * 4; rw < r_end; rw += 16) {
@@ -290,7 +290,10 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
     if (ok) {
       const uint8_t* kr = kb_ + t * p.k_ss * ELT;
       const uint8_t* vr = vb_ + t * p.v_ss * ELT;
-      if (WPL == 2) {
+      if (WPL == 1) {
+        kw[0] = __ldg(reinterpret_cast<const uint32_t*>(kr));
+        vw[0] = __ldg(reinterpret_cast<const uint32_t*>(vr));
+      } else if (WPL == 2) {
         const uint2 a = __ldg(reinterpret_cast<const uint2*>(kr)), c = __ldg(reinterpret_cast<const uint2*>(vr));
         kw[0] = a.x; kw[1] = a.y; vw[0] = c.x; vw[1] = c.y;
       } else {
@@ -573,7 +576,7 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
   const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
   const int64_t Hk = k->shape[1], S = k->shape[2], kb = idx->shape[2];
   if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
-  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (D != 32 && D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 32, 64 or 128");
   for (int i = 0; i < 4; ++i)
     if (k->shape[i] != v->shape[i]) return fail(BD_ERR_SHAPE, "k and v shapes differ");
   if (k->shape[0] != B || k->shape[3] != D || idx->shape[0] != B || idx->shape[1] != Hq)
@@ -606,9 +609,12 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
   if (D == 128) {
     if (fp8) gather_attn_kernel<128, true><<<grid, 128, 0, st>>>(p);
     else gather_attn_kernel<128, false><<<grid, 128, 0, st>>>(p);
-  } else {
+  } else if (D == 64) {
     if (fp8) gather_attn_kernel<64, true><<<grid, 128, 0, st>>>(p);
     else gather_attn_kernel<64, false><<<grid, 128, 0, st>>>(p);
+  } else {
+    if (fp8) gather_attn_kernel<32, true><<<grid, 128, 0, st>>>(p);
+    else gather_attn_kernel<32, false><<<grid, 128, 0, st>>>(p);
   }
   if ((rc = cuda_check(cudaGetLastError(), "gather_attn_kernel launch"))) return rc;
   return launch_combine(part, int(B), int(Hq), int(D), out, st);
@@ -660,7 +666,7 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
   const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
   const int64_t Hk = kmin->shape[1], np = kmin->shape[2];
   if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
-  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (D != 32 && D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 32, 64 or 128");
   for (int i = 0; i < 4; ++i)
     if (kmin->shape[i] != kmax->shape[i] || kmin->stride[i] != kmax->stride[i])
       return fail(BD_ERR_SHAPE, "kmin and kmax must have the same shape and layout");
@@ -679,8 +685,12 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
     quest_bounds_kernel<128><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
         kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
         static_cast<float*>(bounds->data));
-  else
+  else if (D == 64)
     quest_bounds_kernel<64><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
+        kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
+        static_cast<float*>(bounds->data));
+  else
+    quest_bounds_kernel<32><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
         kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
         static_cast<float*>(bounds->data));
   return cuda_check(cudaGetLastError(), "quest_bounds_kernel launch");
