@@ -119,6 +119,16 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return d;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization
+// attribute may start before its predecessor in the stream has finished;
+// griddep_wait() blocks until that predecessor grid has completed and its writes are
+// visible (it returns at once when there is no programmatic predecessor), and
+// griddep_launch_dependents() lets the next such kernel start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 template <typename T> __device__ __forceinline__ float to_f32(T x);
 template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
 template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }

@@ -46,6 +46,10 @@ struct DenseParams {
   // direct output when n_splits == 1 and final
   void* out; int out_dtype; int64_t o_sb, o_sh;
   int direct;
+  // 1: launched as a programmatic dependent of the kernel before it in the stream, which
+  // it does not read from; it waits for that kernel only before exiting, so a kernel
+  // that waits on this one also sees the earlier kernel's writes.
+  int pdl;
 };
 
 template <typename T>
@@ -72,6 +76,7 @@ __device__ __forceinline__ void store_out(void* base, int dt, int64_t off, float
 template <int D, int NT, bool FP8>
 __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const DenseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  if (p.pdl) griddep_launch_dependents();
   constexpr int ELT = FP8 ? 1 : 2;
   constexpr int ROWB = D * ELT;
   constexpr int PITCH = ROWB + 16;
@@ -356,6 +361,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
       }
     }
   }
+  if (p.pdl) griddep_wait();
 }
 
 // Merge per-split partials. mode 0: final output O/L; mode 1: export (m, l, O) per (b,hq).
@@ -370,6 +376,7 @@ struct CombineParams {
 };
 
 __global__ void lse_combine_kernel(const CombineParams p) {
+  griddep_wait();  // partials of a programmatic predecessor (no-op after a plain launch)
   extern __shared__ float wsm[];  // [n] weights
   const int row = blockIdx.x;
   __shared__ float sM, sL;
@@ -455,6 +462,7 @@ int launch_dense(const DenseParams& p, const Plan& pl, cudaStream_t st) {
     attr_set[dev & 63] = true;
   }
   dim3 grid(pl.n_splits, p.Hk * pl.head_chunks, p.B);
+  if (p.pdl) return launch_programmatic(kern, grid, dim3(kWarps * 32), smem, st, p, "dense_decode_kernel launch");
   kern<<<grid, kWarps * 32, smem, st>>>(p);
   return cuda_check(cudaGetLastError(), "dense_decode_kernel launch");
 }
@@ -513,7 +521,7 @@ int dense_split_count(int64_t B, int64_t Hq, int64_t Hk, int64_t S, int64_t D, i
 }
 
 int launch_dense_partials(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
-                          const Partials& part, int split_offset, int nsplit_here, cudaStream_t st) {
+                          const Partials& part, int split_offset, int nsplit_here, cudaStream_t st, bool pdl) {
   int rc;
   if ((rc = validate(q, k, v))) return rc;
   Plan pl;
@@ -529,16 +537,20 @@ int launch_dense_partials(const bd_tensor* q, const bd_tensor* k, const bd_tenso
   p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
   p.split_offset = split_offset; p.split_stride = part.nsplit;
   p.direct = 0;
+  p.pdl = pdl ? 1 : 0;
   return dispatch_dense(p, pl, st);
 }
 
-int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st) {
+int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st, bool pdl) {
   CombineParams c{};
   c.m = part.m; c.l = part.l; c.o = part.o;
   c.rows = B * Hq; c.n = part.nsplit; c.D = D; c.Hq = Hq; c.ms_rows = 1;
   c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
   c.mode = 0;
   if (c.rows == 0) return BD_OK;
+  if (pdl)
+    return launch_programmatic(lse_combine_kernel, dim3(c.rows), dim3(128), size_t(c.n) * sizeof(float), st, c,
+                               "lse_combine_kernel launch");
   lse_combine_kernel<<<c.rows, 128, size_t(c.n) * sizeof(float), st>>>(c);
   return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
 }

@@ -29,10 +29,32 @@ inline size_t partials_bytes(size_t rows, int nsplit, int D) {
 // offset `split_offset` of `part`. Returns the number of splits it will use via
 // dense_split_count (call it first to size the buffer).
 int dense_split_count(int64_t B, int64_t Hq, int64_t Hk, int64_t S, int64_t D, int target_ctas);
+// pdl: launch as a programmatic dependent of the previous kernel in the stream (which
+// must not write what this pass reads); the pass waits for that kernel before it exits.
 int launch_dense_partials(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
-                          const Partials& part, int split_offset, int nsplit_here, cudaStream_t st);
+                          const Partials& part, int split_offset, int nsplit_here, cudaStream_t st,
+                          bool pdl = false);
 
-// Final merge of all splits in `part` into out [B,Hq,D] (bf16/f16/f32).
-int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st);
+// Final merge of all splits in `part` into out [B,Hq,D] (bf16/f16/f32). pdl: launch as a
+// programmatic dependent; the kernel waits for its predecessor before reading partials.
+int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st,
+                   bool pdl = false);
+
+// Launch `kern` with the programmatic stream serialization attribute.
+template <typename Params>
+int launch_programmatic(void (*kern)(Params), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                        const Params& prm, const char* what) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kern, prm), what);
+}
 
 }  // namespace bd

@@ -16,19 +16,26 @@
 //    The scale folds into Q' = q*s (f16, HMUL2 per warp per group), so the contraction
 //    runs on the tensor cores over raw codes: S^T[16 tok x 8 heads] += codes . Q'^T
 //    (mma.sync m16n8k16 f16 -> f32); the per-(head, group) bias sum_c q_c m_c is one
-//    more MMA with the group's minima as the only non-zero A row.
+//    more MMA with the group's minima in every A row, so each lane reads its heads' bias
+//    straight from its own accumulators.
 //  * Codes become MMA operands in registers with no shared-memory staging of unpacked
-//    data: a 2-bit (4-bit) field masked into the low mantissa bits of an f16 is the
-//    exact subnormal code*2^-24, so one shift and one AND per word give two operands;
-//    the 2^24 factor is applied to the fp32 accumulators. Register pairs along the
-//    contraction dim come from one PRMT of two words.
+//    data: a 2-bit (4-bit) field masked into the low byte of an f16 is the exact
+//    subnormal code * 2^(pos-24). One byte-select PRMT of two packed words puts the
+//    right byte of each into the two halves of an operand register and one AND keeps
+//    the field, so every register (two codes) costs two ALU ops. The field position
+//    depends only on the accumulator row a lane owns, so 2^(24-pos) is a per-lane
+//    constant applied to the fp32 accumulators.
 //  * Values: O^T[16 ch x 8 heads] += codes^T[16 ch x 16 tok] . P'^T[16 tok x 8], with the
 //    per-token scale folded into P' = P*s_v (one version per 32-channel group); the
 //    minima contribute sum_t P_t m_t per (group, head), again one MMA per row block.
 //  * Row/token permutations are chosen so every shared-memory read is conflict-free
 //    and the movmatrix transpose of P lands directly in the PV operand layout.
 //  * The bf16 residual window runs through the dense split kernel into the same
-//    partial buffer; a log-sum-exp combine produces the output.
+//    partial buffer; a log-sum-exp combine produces the output. Both are launched as
+//    programmatic dependents, so the residual CTAs fill the SMs this grid's tail frees
+//    and the combine is resident before its inputs are complete.
+//  * Splits are balanced to one wave of 4 CTAs per SM (split s owns tiles
+//    [s*T/n, (s+1)*T/n)), so no SM carries a second round.
 #include "common.cuh"
 #include "decode_shared.cuh"
 
@@ -43,7 +50,7 @@ constexpr int kTile = 128;  // tokens per tile
 constexpr int kStagesK = 3;
 constexpr float kLog2eK = 1.4426950408889634f;
 constexpr float kLn2K = 0.6931471805599453f;
-constexpr float kSub = 16777216.f;  // 2^24: f16 subnormal code c has value c * 2^-24
+constexpr int kRedPitch = 132;  // floats per head row of the epilogue buffer (padded: no bank conflicts)
 
 template <int BITS>
 struct KL {
@@ -74,7 +81,8 @@ struct KiviParams {
   const __half* vs; int64_t vs_sb, vs_sh, vs_st;
   const __half* vm; int64_t vm_sb, vm_sh, vm_st;
   int B, Hq, Hk, G, Sq;
-  int head_chunks, tiles_per_split;
+  int head_chunks;
+  int nsplit, ntiles;  // split s owns tiles [s*ntiles/nsplit, (s+1)*ntiles/nsplit)
   float scale_log2;
   float* part_m; float* part_l; float* part_o; int split_stride;
 };
@@ -97,20 +105,46 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
   using L = KL<BITS>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* tsm = smem + kStagesK * L::STAGE;  // transposed key scale / min of the current tile
+  // the residual-window kernel queued behind this one reads nothing this grid writes
+  griddep_launch_dependents();
   const int split = blockIdx.x;
   const int hk = blockIdx.y / p.head_chunks;
   const int chunk = blockIdx.y % p.head_chunks;
   const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
-  const int t_begin = split * p.tiles_per_split * kTile;
-  const int t_end = min(p.Sq, t_begin + p.tiles_per_split * kTile);
-  const int ntiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
+  const int tile0 = int(int64_t(split) * p.ntiles / p.nsplit);
+  const int ntiles = int(int64_t(split + 1) * p.ntiles / p.nsplit) - tile0;
+  const int t_begin = tile0 * kTile;
+  const int t_end = min(p.Sq, t_begin + ntiles * kTile);
   const int h0 = chunk * 8;
   const int nheads = min(8, p.G - h0);
   // QK accumulator row g <-> token rho (row g+8 <-> rho+8) inside a 16-token row block;
   // chosen so that the movmatrix transpose of P is the PV operand for tokens tq+4u.
   const int rho = (g >> 1) + 4 * (g & 1);
+  // Byte-select PRMT selectors: byte x of the first word -> result byte 0 and byte x of
+  // the second word -> result byte 2 (bytes 1 and 3 are masked off afterwards).
+  //  keys:   word = 16 (8) tokens of one channel; row rho takes token rho's byte
+  //  values: word = 16 (8) channels of one token; row g takes channel g's byte
+  uint32_t selK0, selK1, mskK, selV0, selV1, mskV;
+  float subK, subV;  // 2^(24 - field position): undoes the subnormal encoding per row
+  if (BITS == 2) {
+    selK0 = uint32_t(rho >> 2) | (uint32_t(4 + (rho >> 2)) << 8);        // tokens 0..7 (low half)
+    selK1 = uint32_t(2 + (rho >> 2)) | (uint32_t(6 + (rho >> 2)) << 8);  // tokens 8..15 (high half)
+    mskK = 0x00030003u << (2 * (rho & 3));
+    subK = __int_as_float((127 + 24 - 2 * (rho & 3)) << 23);
+    selV0 = uint32_t(g >> 2) | (uint32_t(4 + (g >> 2)) << 8);            // channel g (low half)
+    selV1 = uint32_t(2 + (g >> 2)) | (uint32_t(6 + (g >> 2)) << 8);      // channel g+8 (high half)
+    mskV = 0x00030003u << (2 * (g & 3));
+    subV = __int_as_float((127 + 24 - 2 * (g & 3)) << 23);
+  } else {
+    selK0 = selK1 = uint32_t(rho >> 1) | (uint32_t(4 + (rho >> 1)) << 8);
+    mskK = 0x000F000Fu << (4 * (rho & 1));
+    subK = __int_as_float((127 + 24 - 4 * (rho & 1)) << 23);
+    selV0 = selV1 = uint32_t(g >> 1) | (uint32_t(4 + (g >> 1)) << 8);
+    mskV = 0x000F000Fu << (4 * (g & 1));
+    subV = __int_as_float((127 + 24 - 4 * (g & 1)) << 23);
+  }
 
   const uint32_t* kq_base = p.kq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh;
   const __half* ks_base = p.ks + int64_t(b) * p.ks_sb + int64_t(hk) * p.ks_sh;
@@ -148,40 +182,58 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     }
   }
 
-  const int words_end = (t_end + L::FPI - 1) / L::FPI;  // first word index past the split
-  const int groups_end = (t_end + 31) / 32;
+  const float kmulK = subK * score_mul;  // accumulator -> log2-domain score, per lane
+
+  // Global -> shared copy assignment of this thread, fixed over the split's tiles.
+  constexpr int NCH = L::KQ_WORDS / 4;  // 16-byte key chunks per channel row (2 or 4)
+  constexpr int NVC = L::VQ_WORDS / 4;  // 16-byte value chunks per token row (2 or 4)
+  const int k_row = threadIdx.x / NCH, k_ck = threadIdx.x % NCH;
+  const int v_row = threadIdx.x / NVC, v_ck = threadIdx.x % NVC;
+  const uint32_t* k_src = kq_base + int64_t(k_row) * p.kq_sc + t_begin / L::FPI + k_ck * 4;
+  const uint32_t* v_src = vq_base + int64_t(t_begin + v_row) * p.vq_st + v_ck * 4;
+  const __half* ks_src = ks_base + int64_t(threadIdx.x) * p.ks_sc + t_begin / 32;
+  const __half* km_src = km_base + int64_t(threadIdx.x) * p.km_sc + t_begin / 32;
+  const __half* vs_src = vs_base + int64_t(t_begin + threadIdx.x) * p.vs_st;
+  const __half* vm_src = vm_base + int64_t(t_begin + threadIdx.x) * p.vm_st;
+  const int64_t k_pass = int64_t(128 / NCH) * p.kq_sc;  // channel rows per pass of the CTA
+  const int64_t v_pass = int64_t(128 / NVC) * p.vq_st;
+  const uint32_t k_dst = k_row * L::KQ_PITCH + k_ck * 16;
+  const uint32_t v_dst = L::OFF_VQ + v_row * L::VQ_PITCH + v_ck * 16;
   auto load_tile = [&](int tile, int stage) {
     const int t0 = t_begin + tile * kTile;
     const uint32_t sbase = smem_u32(smem + stage * L::STAGE);
-    constexpr int NCH = L::KQ_WORDS / 4;  // 16-byte chunks per channel row
-    for (int c = threadIdx.x; c < 128 * NCH; c += kWarpsK * 32) {
-      const int row = c / NCH, ck = c % NCH;
-      const int w0 = t0 / L::FPI + ck * 4;
-      const int valid = max(0, min(4, words_end - w0));
-      const uint32_t* src = kq_base + int64_t(row) * p.kq_sc + (valid ? w0 : 0);
-      cp_async16(sbase + row * L::KQ_PITCH + ck * 16, src, valid * 4);
-    }
-    {
-      const int row = threadIdx.x;  // 128 threads == 128 channels
-      const int gr0 = t0 / 32;
-      const int valid = max(0, min(4, groups_end - gr0));
-      cp_async8(sbase + L::OFF_KS + row * 8, ks_base + int64_t(row) * p.ks_sc + (valid ? gr0 : 0), valid * 2);
-      cp_async8(sbase + L::OFF_KM + row * 8, km_base + int64_t(row) * p.km_sc + (valid ? gr0 : 0), valid * 2);
-    }
-    constexpr int NVC = L::VQ_WORDS / 4;
-    for (int c = threadIdx.x; c < kTile * NVC; c += kWarpsK * 32) {
-      const int r = c / NVC, ck = c % NVC;
-      const int t = t0 + r;
-      const bool ok = t < t_end;
-      cp_async16(sbase + L::OFF_VQ + r * L::VQ_PITCH + ck * 16, vq_base + int64_t(ok ? t : 0) * p.vq_st + ck * 4,
-                 ok ? 16 : 0);
-    }
-    {
-      const int r = threadIdx.x;  // 128 threads == 128 tokens
-      const int t = t0 + r;
-      const bool ok = t < t_end;
-      cp_async8(sbase + L::OFF_VS + r * 8, vs_base + int64_t(ok ? t : 0) * p.vs_st, ok ? 8 : 0);
-      cp_async8(sbase + L::OFF_VM + r * 8, vm_base + int64_t(ok ? t : 0) * p.vm_st, ok ? 8 : 0);
+    const int64_t vt = int64_t(tile) * kTile;
+    if (t0 + kTile <= t_end) {
+#pragma unroll
+      for (int i = 0; i < NCH; ++i)
+        cp_async16(sbase + k_dst + i * (128 / NCH) * L::KQ_PITCH, k_src + i * k_pass + tile * L::KQ_WORDS, 16);
+      cp_async8(sbase + L::OFF_KS + threadIdx.x * 8, ks_src + tile * 4, 8);
+      cp_async8(sbase + L::OFF_KM + threadIdx.x * 8, km_src + tile * 4, 8);
+#pragma unroll
+      for (int i = 0; i < NVC; ++i)
+        cp_async16(sbase + v_dst + i * (128 / NVC) * L::VQ_PITCH, v_src + i * v_pass + vt * p.vq_st, 16);
+      cp_async8(sbase + L::OFF_VS + threadIdx.x * 8, vs_src + vt * p.vs_st, 8);
+      cp_async8(sbase + L::OFF_VM + threadIdx.x * 8, vm_src + vt * p.vm_st, 8);
+    } else {
+      // last, partial tile of the sequence: zero-fill past t_end (src-size 0 reads nothing)
+      const int words_left = (t_end - t0 + L::FPI - 1) / L::FPI - k_ck * 4;
+      const int kv = max(0, min(4, words_left));
+#pragma unroll
+      for (int i = 0; i < NCH; ++i)
+        cp_async16(sbase + k_dst + i * (128 / NCH) * L::KQ_PITCH,
+                   kv ? k_src + i * k_pass + tile * L::KQ_WORDS : k_src, kv * 4);
+      const int gv = max(0, min(4, (t_end - t0 + 31) / 32));
+      cp_async8(sbase + L::OFF_KS + threadIdx.x * 8, ks_src + (gv ? tile * 4 : 0), gv * 2);
+      cp_async8(sbase + L::OFF_KM + threadIdx.x * 8, km_src + (gv ? tile * 4 : 0), gv * 2);
+#pragma unroll
+      for (int i = 0; i < NVC; ++i) {
+        const bool ok = t0 + v_row + i * (128 / NVC) < t_end;
+        cp_async16(sbase + v_dst + i * (128 / NVC) * L::VQ_PITCH, ok ? v_src + i * v_pass + vt * p.vq_st : v_src,
+                   ok ? 16 : 0);
+      }
+      const bool ok = t0 + int(threadIdx.x) < t_end;
+      cp_async8(sbase + L::OFF_VS + threadIdx.x * 8, ok ? vs_src + vt * p.vs_st : vs_base, ok ? 8 : 0);
+      cp_async8(sbase + L::OFF_VM + threadIdx.x * 8, ok ? vm_src + vt * p.vm_st : vm_base, ok ? 8 : 0);
     }
   };
 
@@ -220,9 +272,10 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
     if (tb >= t_end) continue;
 
-    // ---- Q' = q * s_k (f16) and bias = sum_c q_c m_c (one MMA chain, minima in A row 0)
+    // ---- Q' = q * s_k (f16) and bias = sum_c q_c m_c. The bias MMA carries the group's
+    // minima in every A row, so every accumulator row holds the bias of its two heads.
     uint32_t qb[8][2];
-    float bb0, bb1;
+    float bias[2];
     {
       const uint8_t* tsr = tsm + warp * 256;         // scales of group `warp`
       const uint8_t* tmr = tsm + (4 + warp) * 256;   // minima of group `warp`
@@ -232,78 +285,106 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
         const int c0 = 16 * j + 2 * tq;
         qb[j][0] = h2u(__hmul2(u2h(qh[j][0]), u2h(lds_u32(tsr + c0 * 2))));
         qb[j][1] = h2u(__hmul2(u2h(qh[j][1]), u2h(lds_u32(tsr + (c0 + 8) * 2))));
-        const uint32_t m01 = g == 0 ? lds_u32(tmr + c0 * 2) : 0u;
-        const uint32_t m89 = g == 0 ? lds_u32(tmr + (c0 + 8) * 2) : 0u;
-        mma_f16(bacc, m01, 0u, m89, 0u, qh[j][0], qh[j][1]);
+        const uint32_t m01 = lds_u32(tmr + c0 * 2);
+        const uint32_t m89 = lds_u32(tmr + (c0 + 8) * 2);
+        mma_f16(bacc, m01, m01, m89, m89, qh[j][0], qh[j][1]);
       }
-      bb0 = __shfl_sync(0xffffffffu, bacc[0], tq);
-      bb1 = __shfl_sync(0xffffffffu, bacc[1], tq);
+      bias[0] = bacc[0] * score_mul;
+      bias[1] = bacc[1] * score_mul;
     }
 
-    // ---- S^T (scaled by 2^-24) for the warp's two 16-token row blocks
+    // ---- S^T (each row scaled by 2^(pos-24)) for the warp's two 16-token row blocks
     float s[2][4];
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) s[rb][0] = s[rb][1] = s[rb][2] = s[rb][3] = 0.f;
+    const uint8_t* kst = st + (2 * tq) * L::KQ_PITCH + warp * (BITS == 2 ? 8 : 16);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      uint32_t U[2][4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int c = 16 * j + 2 * tq + (e & 1) + (e >> 1) * 8;
-        if (BITS == 2) {
-          const uint2 w2 = *reinterpret_cast<const uint2*>(st + c * L::KQ_PITCH + warp * 8);
-          U[0][e] = (w2.x >> (2 * rho)) & 0x00030003u;
-          U[1][e] = (w2.y >> (2 * rho)) & 0x00030003u;
-        } else {
-          const uint4 w4 = *reinterpret_cast<const uint4*>(st + c * L::KQ_PITCH + warp * 16);
-          const uint32_t sel = rho < 4 ? 0x5410u : 0x7632u;
-          const int sh = 4 * (rho & 3);
-          U[0][e] = (prmt(w4.x, w4.y, sel) >> sh) & 0x000F000Fu;
-          U[1][e] = (prmt(w4.z, w4.w, sel) >> sh) & 0x000F000Fu;
-        }
+      // channels c0, c0+1 (k = 2tq, 2tq+1) and c0+8, c0+9 (k = 2tq+8, 2tq+9)
+      const uint8_t* kr = kst + 16 * j * L::KQ_PITCH;
+      if (BITS == 2) {
+        // .x = tokens 0..15 (row block 0), .y = tokens 16..31 (row block 1)
+        const uint2 wa = *reinterpret_cast<const uint2*>(kr);
+        const uint2 wb = *reinterpret_cast<const uint2*>(kr + L::KQ_PITCH);
+        const uint2 wc = *reinterpret_cast<const uint2*>(kr + 8 * L::KQ_PITCH);
+        const uint2 wd = *reinterpret_cast<const uint2*>(kr + 9 * L::KQ_PITCH);
+        mma_f16(s[0], prmt(wa.x, wb.x, selK0) & mskK, prmt(wa.x, wb.x, selK1) & mskK,
+                prmt(wc.x, wd.x, selK0) & mskK, prmt(wc.x, wd.x, selK1) & mskK, qb[j][0], qb[j][1]);
+        mma_f16(s[1], prmt(wa.y, wb.y, selK0) & mskK, prmt(wa.y, wb.y, selK1) & mskK,
+                prmt(wc.y, wd.y, selK0) & mskK, prmt(wc.y, wd.y, selK1) & mskK, qb[j][0], qb[j][1]);
+      } else {
+        // .x/.y = tokens 0..7 / 8..15 (row block 0), .z/.w = tokens 16..23 / 24..31
+        const uint4 wa = *reinterpret_cast<const uint4*>(kr);
+        const uint4 wb = *reinterpret_cast<const uint4*>(kr + L::KQ_PITCH);
+        const uint4 wc = *reinterpret_cast<const uint4*>(kr + 8 * L::KQ_PITCH);
+        const uint4 wd = *reinterpret_cast<const uint4*>(kr + 9 * L::KQ_PITCH);
+        mma_f16(s[0], prmt(wa.x, wb.x, selK0) & mskK, prmt(wa.y, wb.y, selK0) & mskK,
+                prmt(wc.x, wd.x, selK0) & mskK, prmt(wc.y, wd.y, selK0) & mskK, qb[j][0], qb[j][1]);
+        mma_f16(s[1], prmt(wa.z, wb.z, selK0) & mskK, prmt(wa.w, wb.w, selK0) & mskK,
+                prmt(wc.z, wd.z, selK0) & mskK, prmt(wc.w, wd.w, selK0) & mskK, qb[j][0], qb[j][1]);
       }
-#pragma unroll
-      for (int rb = 0; rb < 2; ++rb)
-        mma_f16(s[rb], prmt(U[rb][0], U[rb][1], 0x5410u), prmt(U[rb][0], U[rb][1], 0x7632u),
-                prmt(U[rb][2], U[rb][3], 0x5410u), prmt(U[rb][2], U[rb][3], 0x7632u), qb[j][0], qb[j][1]);
     }
 
     // ---- online softmax over the 32 tokens (exp2 domain)
     float pv[2][4];
     {
-      const float bbj[2] = {bb0, bb1};
+      float x[2][4];  // [head j][rb0 row, rb0 row+8, rb1 row, rb1 row+8]
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float x[4];
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int rb = 0; rb < 2; ++rb) {
+          x[j][2 * rb] = fmaf(s[rb][j], kmulK, bias[j]);
+          x[j][2 * rb + 1] = fmaf(s[rb][2 + j], kmulK, bias[j]);
+        }
+      if (tb + 32 > t_end) {  // warp-uniform: only the sequence's last group is partial
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
           const int tr = tb + 16 * rb + rho;
-          x[2 * rb] = tr < t_end ? fmaf(s[rb][j], kSub, bbj[j]) * score_mul : -INFINITY;
-          x[2 * rb + 1] = tr + 8 < t_end ? fmaf(s[rb][2 + j], kSub, bbj[j]) * score_mul : -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            if (tr >= t_end) x[j][2 * rb] = -INFINITY;
+            if (tr + 8 >= t_end) x[j][2 * rb + 1] = -INFINITY;
+          }
         }
-        float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      }
+      float mnew[2], muse[2];
+      bool grow = false;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float mx = fmaxf(fmaxf(x[j][0], x[j][1]), fmaxf(x[j][2], x[j][3]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mnew = fmaxf(mrow[j], mx);
-        const float muse = mnew == -INFINITY ? 0.f : mnew;
-        const float alpha = exp2f(mrow[j] - muse);
-        mrow[j] = mnew;
+        mnew[j] = fmaxf(mrow[j], mx);
+        muse[j] = mnew[j] == -INFINITY ? 0.f : mnew[j];
+        grow |= mnew[j] > mrow[j];
+      }
+      // rescale the running sums only when some head's maximum grew (alpha == 1 otherwise)
+      if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float alpha = exp2f(mrow[j] - muse[j]);
+          lrow[j] *= alpha;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            o[mt][j] *= alpha;
+            o[mt][2 + j] *= alpha;
+          }
+          cacc[j] *= alpha;
+          cacc[2 + j] *= alpha;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        mrow[j] = mnew[j];
         float acc = 0.f;
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
-          pv[rb][j] = exp2f(x[2 * rb] - muse);
-          pv[rb][2 + j] = exp2f(x[2 * rb + 1] - muse);
+          pv[rb][j] = exp2f(x[j][2 * rb] - muse[j]);
+          pv[rb][2 + j] = exp2f(x[j][2 * rb + 1] - muse[j]);
           acc += pv[rb][j] + pv[rb][2 + j];
         }
-        lrow[j] = lrow[j] * alpha + acc;
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          o[mt][j] *= alpha;
-          o[mt][2 + j] *= alpha;
-        }
-        cacc[j] *= alpha;
-        cacc[2 + j] *= alpha;
+        lrow[j] += acc;
       }
     }
 
@@ -326,19 +407,18 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
         }
       }
       {
-        // value minima: A rows = groups (g < 4), k = tokens tq, tq+4 | tq+8, tq+12
+        // value minima: A rows = groups (rows g < 4), k = tokens tq, tq+4 | tq+8, tq+12
         const uint32_t pt0 = movmatrix_trans(hp0), pt1 = movmatrix_trans(hp1);
-        uint32_t a0 = 0u, a2 = 0u;
-        if (g < 4) {
-          const uint8_t* vmr = st + L::OFF_VM + 2 * g;
-          a0 = lds_u16(vmr + (tl + tq) * 8) | (lds_u16(vmr + (tl + tq + 4) * 8) << 16);
-          a2 = lds_u16(vmr + (tl + tq + 8) * 8) | (lds_u16(vmr + (tl + tq + 12) * 8) << 16);
-        }
+        const uint8_t* vmr = st + L::OFF_VM + 2 * (g & 3);
+        const uint32_t keep = g < 4 ? 0xffffffffu : 0u;
+        const uint32_t a0 = (lds_u16(vmr + (tl + tq) * 8) | (lds_u16(vmr + (tl + tq + 4) * 8) << 16)) & keep;
+        const uint32_t a2 = (lds_u16(vmr + (tl + tq + 8) * 8) | (lds_u16(vmr + (tl + tq + 12) * 8) << 16)) & keep;
         mma_f16(cacc, a0, 0u, a2, 0u, pt0, pt1);
       }
-      // value codes of tokens tl + tq + 4u, u = 0..3
+      // value codes of tokens tl + tq + 4u, u = 0..3; A row g = channel 16mt+g, row g+8 =
+      // channel 16mt+8+g; k pairs = tokens (tq, tq+4) and (tq+8, tq+12)
       if (BITS == 2) {
-        uint32_t W[4][8];
+        uint32_t W[4][8];  // [u][word]: word mt holds channels 16mt..16mt+15
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const uint8_t* row = st + L::OFF_VQ + (tl + tq + 4 * u) * L::VQ_PITCH;
@@ -348,19 +428,14 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
           W[u][4] = hi.x; W[u][5] = hi.y; W[u][6] = hi.z; W[u][7] = hi.w;
         }
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          uint32_t Uu[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) Uu[u] = (W[u][mt] >> (2 * g)) & 0x00030003u;
-          mma_f16(o[mt], prmt(Uu[0], Uu[1], 0x5410u), prmt(Uu[0], Uu[1], 0x7632u), prmt(Uu[2], Uu[3], 0x5410u),
-                  prmt(Uu[2], Uu[3], 0x7632u), pb[mt >> 1][0], pb[mt >> 1][1]);
-        }
+        for (int mt = 0; mt < 8; ++mt)
+          mma_f16(o[mt], prmt(W[0][mt], W[1][mt], selV0) & mskV, prmt(W[0][mt], W[1][mt], selV1) & mskV,
+                  prmt(W[2][mt], W[3][mt], selV0) & mskV, prmt(W[2][mt], W[3][mt], selV1) & mskV,
+                  pb[mt >> 1][0], pb[mt >> 1][1]);
       } else {
-        const bool hiw = g >= 4;
-        const int sh = 4 * (g & 3);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          uint32_t W[4][8];
+          uint32_t W[4][8];  // [u][word]: word i holds channels 64*half + 8i .. +7
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const uint8_t* row = st + L::OFF_VQ + (tl + tq + 4 * u) * L::VQ_PITCH + half * 32;
@@ -372,14 +447,10 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
 #pragma unroll
           for (int ml = 0; ml < 4; ++ml) {
             const int mt = 4 * half + ml;
-            uint32_t Uu[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const uint32_t w = hiw ? W[u][2 * ml + 1] : W[u][2 * ml];
-              Uu[u] = (w >> sh) & 0x000F000Fu;
-            }
-            mma_f16(o[mt], prmt(Uu[0], Uu[1], 0x5410u), prmt(Uu[0], Uu[1], 0x7632u),
-                    prmt(Uu[2], Uu[3], 0x5410u), prmt(Uu[2], Uu[3], 0x7632u), pb[mt >> 1][0], pb[mt >> 1][1]);
+            mma_f16(o[mt], prmt(W[0][2 * ml], W[1][2 * ml], selV0) & mskV,
+                    prmt(W[0][2 * ml + 1], W[1][2 * ml + 1], selV0) & mskV,
+                    prmt(W[2][2 * ml], W[3][2 * ml], selV0) & mskV,
+                    prmt(W[2][2 * ml + 1], W[3][2 * ml + 1], selV0) & mskV, pb[mt >> 1][0], pb[mt >> 1][1]);
           }
         }
       }
@@ -406,7 +477,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
   __syncthreads();
   float* red_m = reinterpret_cast<float*>(smem);  // [4][8]
   float* red_l = red_m + kWarpsK * 8;             // [4][8]
-  float* red_o = red_l + kWarpsK * 8;             // [4][8][128]
+  float* red_o = red_l + kWarpsK * 8;             // [4][8][kRedPitch]
   if (g == 0) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -424,11 +495,9 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     const float f = (M == -INFINITY) ? 0.f : exp2f(mrow[j] - M);
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
-      int ca, cb;
-      if (BITS == 2) { ca = 16 * mt + g; cb = ca + 8; }
-      else { ca = 16 * mt + (g < 4 ? g : g + 4); cb = ca + 4; }
-      red_o[(warp * 8 + h) * 128 + ca] = fmaf(o[mt][j], kSub, corr[mt >> 1][j]) * f;
-      red_o[(warp * 8 + h) * 128 + cb] = fmaf(o[mt][2 + j], kSub, corr[mt >> 1][j]) * f;
+      const int ca = 16 * mt + g;  // A row g; row g+8 is channel ca + 8
+      red_o[(warp * 8 + h) * kRedPitch + ca] = fmaf(o[mt][j], subV, corr[mt >> 1][j]) * f;
+      red_o[(warp * 8 + h) * kRedPitch + ca + 8] = fmaf(o[mt][2 + j], subV, corr[mt >> 1][j]) * f;
     }
   }
   __syncthreads();
@@ -442,7 +511,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     for (int w = 0; w < kWarpsK; ++w) {
       const float f = (M == -INFINITY) ? 0.f : exp2f(red_m[w * 8 + h] - M);
       Lsum += red_l[w * 8 + h] * f;
-      O += red_o[(w * 8 + h) * 128 + c];
+      O += red_o[(w * 8 + h) * kRedPitch + c];
     }
     const int hq = hk * p.G + h0 + h;
     const int64_t pi = (int64_t(b) * p.Hq + hq) * p.split_stride + split;
@@ -457,7 +526,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
 template <int BITS>
 int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
   using L = KL<BITS>;
-  const size_t smem = std::max<size_t>(size_t(kStagesK) * L::STAGE + L::T_BYTES, (2 * 4 * 8 + 4 * 8 * 128) * sizeof(float));
+  const size_t smem = std::max<size_t>(size_t(kStagesK) * L::STAGE + L::T_BYTES, (2 * 4 * 8 + 4 * 8 * kRedPitch) * sizeof(float));
   auto kern = kivi_decode_kernel<BITS>;
   static bool attr[64] = {false};
   int dev = 0;
@@ -474,7 +543,7 @@ int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
 }
 
 struct KiviPlan {
-  int n_kivi, tiles_per_split, n_res, head_chunks;
+  int n_kivi, ntiles, n_res, head_chunks;
 };
 
 int kivi_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t Sq, int64_t R, KiviPlan* pl) {
@@ -485,9 +554,8 @@ int kivi_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t Sq, int64_t R, KiviPlan
   const int64_t slots = 4LL * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
-  const int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;
-  pl->n_kivi = ntiles > 0 ? int((ntiles + tps - 1) / tps) : 0;
-  pl->tiles_per_split = int(tps);
+  pl->n_kivi = ntiles > 0 ? int(splits) : 0;
+  pl->ntiles = int(ntiles);
   pl->n_res = R > 0 ? std::max(1, dense_split_count(B, Hq, Hk, R, 128, int(pairs))) : 0;
   return BD_OK;
 }
@@ -685,17 +753,20 @@ int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd
     kp.vs = static_cast<const __half*>(V_scale->data); kp.vs_sb = V_scale->stride[0]; kp.vs_sh = V_scale->stride[1]; kp.vs_st = V_scale->stride[2];
     kp.vm = static_cast<const __half*>(V_mn->data); kp.vm_sb = V_mn->stride[0]; kp.vm_sh = V_mn->stride[1]; kp.vm_st = V_mn->stride[2];
     kp.B = int(B); kp.Hq = int(Hq); kp.Hk = int(Hk); kp.G = int(Hq / Hk); kp.Sq = int(Sq);
-    kp.head_chunks = pl.head_chunks; kp.tiles_per_split = pl.tiles_per_split;
+    kp.head_chunks = pl.head_chunks; kp.nsplit = pl.n_kivi; kp.ntiles = pl.ntiles;
     kp.scale_log2 = scaling * kLog2eK;
     kp.part_m = part.m; kp.part_l = part.l; kp.part_o = part.o; kp.split_stride = ntot;
     rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, st) : launch_kivi<4>(kp, pl.n_kivi, st);
     if (rc) return rc;
   }
   if (pl.n_res > 0 && (stages & 2)) {
-    if ((rc = launch_dense_partials(Q, K_residual, V_residual, scaling, part, pl.n_kivi, pl.n_res, st))) return rc;
+    // programmatic dependent of the KIVI pass when that ran just before it
+    const bool pdl = pl.n_kivi > 0 && (stages & 1);
+    if ((rc = launch_dense_partials(Q, K_residual, V_residual, scaling, part, pl.n_kivi, pl.n_res, st, pdl)))
+      return rc;
   }
   if (!(stages & 4)) return BD_OK;
-  return launch_combine(part, int(B), int(Hq), 128, out, st);
+  return launch_combine(part, int(B), int(Hq), 128, out, st, (stages & 3) != 0);
 }
 
 int bd_kivi_pack_last_dim(const bd_tensor* x, int group_size, int bits, const bd_tensor* code,
