@@ -51,12 +51,33 @@ def lib():
             raise RuntimeError(
                 f"bytes_b200 native library not found at {LIB_PATH}; build it with "
                 "`python -m bytes_b200.build` (nvcc, sm_100a). There is no CPU fallback.")
-        L = ctypes.CDLL(LIB_PATH)
+        # RTLD_GLOBAL: the torch glue module resolves its bd_* symbols against this copy
+        L = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
         L.bd_last_error.restype = ctypes.c_char_p
         L.bd_status_name.restype = ctypes.c_char_p
         L.bd_abi_version.restype = ctypes.c_int
         _lib = L
     return _lib
+
+
+GLUE_PATH = os.path.join(_PKG, "lib", "glue", "bd_glue.so")
+_glue = None
+
+
+def glue():
+    """The compiled torch glue module (csrc/torch_glue.cpp); raises if it is absent."""
+    global _glue
+    if _glue is None:
+        lib()
+        if not os.path.exists(GLUE_PATH):
+            raise RuntimeError(f"bytes_b200 glue module not found at {GLUE_PATH}; build it with "
+                               "`python -m bytes_b200.build`.")
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("bd_glue", GLUE_PATH)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        _glue = mod
+    return _glue
 
 
 def fn(name, restype=ctypes.c_int):

@@ -68,8 +68,17 @@ def _ptr(buf):
     return VP(buf.data_ptr()) if buf is not None else VP(0)
 
 
+# status codes after which a call is retried with re-laid-out copies of its inputs
+_RELAYOUT = (4, 5)  # BD_ERR_STRIDE, BD_ERR_ALIGN
+
+
 def decode_attn(q3, k, v, scaling, out):
     """q3 [B,Hq,D], k/v [B,Hk,S,D] bf16|fp8 -> writes out [B,Hq,D]."""
+    rc = N.glue().decode_attn(q3, k, v, out, float(scaling))
+    if rc == 0:
+        return out
+    if rc not in _RELAYOUT:
+        N.check(rc, "bd_decode_attn")
     N.require_cuda(q3, k, v, out)
     k = rows_aligned(k)
     v = rows_aligned(v)
@@ -119,6 +128,12 @@ def lse_combine(m, l, o, out_dtype=torch.bfloat16):
 
 
 def kivi_decode(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, bits, group_size, scaling, out, stages=7):
+    rc = N.glue().kivi_decode(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, int(bits), int(group_size), float(scaling), out,
+                              int(stages))
+    if rc == 0:
+        return out
+    if rc not in _RELAYOUT:
+        N.check(rc, "bd_kivi_decode_attn")
     N.require_cuda(Q3, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, out)
     Kq, Vq = rows_aligned(Kq, 16), rows_aligned(Vq, 16)
     Ks, Km, Vs, Vm = (rows_aligned(t, 8) for t in (Ks, Km, Vs, Vm))

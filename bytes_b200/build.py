@@ -2,12 +2,15 @@
 
 Every ``bytes_b200/csrc/*.cu`` compiles to an object (in parallel, skipped when
 its sources are unchanged) and links into one shared library exporting the
-``extern "C"`` entry points declared in ``include/bdecode.h``.
+``extern "C"`` entry points declared in ``include/bdecode.h``. Then the torch glue
+module ``bytes_b200/lib/glue/bd_glue.so`` (``csrc/torch_glue.cpp``: descriptors
+filled in C++ for the per-token decode calls) is compiled against the installed torch.
 
     python -m bytes_b200.build [--verbose-ptxas]
 """
 import argparse
 import concurrent.futures as cf
+import ctypes
 import hashlib
 import os
 import subprocess
@@ -18,6 +21,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "lib", "obj")
 LIB = os.path.join(PKG, "lib", "libbdecode.so")
+GLUE_DIR = os.path.join(PKG, "lib", "glue")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
@@ -66,9 +70,20 @@ def build(ptxas_verbose=False, quiet=False):
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s\n%s" % (r.stdout, r.stderr))
+    build_glue()
     if not quiet:
         print("built", LIB)
     return LIB
+
+
+def build_glue():
+    """Compile (when changed) and import the torch glue module against libbdecode.so."""
+    from torch.utils import cpp_extension
+    ctypes.CDLL(LIB, mode=ctypes.RTLD_GLOBAL)  # the glue resolves bd_* against it
+    os.makedirs(GLUE_DIR, exist_ok=True)
+    return cpp_extension.load(name="bd_glue", sources=[os.path.join(CSRC, "torch_glue.cpp")],
+                              extra_include_paths=[os.path.join(ROOT, "include")], extra_cflags=["-O2"],
+                              build_directory=GLUE_DIR, with_cuda=True, verbose=False)
 
 
 if __name__ == "__main__":
