@@ -51,6 +51,7 @@ constexpr int kStagesK = 3;
 constexpr float kLog2eK = 1.4426950408889634f;
 constexpr float kLn2K = 0.6931471805599453f;
 constexpr int kRedPitch = 132;  // floats per head row of the epilogue buffer (padded: no bank conflicts)
+constexpr int kKChunk = 4;      // tiles per key scale/min chunk
 
 template <int BITS>
 struct KL {
@@ -60,16 +61,21 @@ struct KL {
   static constexpr int VQ_WORDS = 128 / FPI;            // words per token (D = 128)
   static constexpr int VQ_PITCH = BITS == 2 ? 32 : 80;
   static constexpr int KQ_BYTES = 128 * KQ_PITCH;
-  static constexpr int KS_BYTES = 128 * 8;  // 4 groups x f16 per channel
   static constexpr int VQ_BYTES = kTile * VQ_PITCH;
   static constexpr int VS_BYTES = kTile * 8;  // 4 groups x f16 per token
-  static constexpr int OFF_KS = KQ_BYTES;
-  static constexpr int OFF_KM = OFF_KS + KS_BYTES;
-  static constexpr int OFF_VQ = OFF_KM + KS_BYTES;
+  static constexpr int OFF_VQ = KQ_BYTES;
   static constexpr int OFF_VS = OFF_VQ + VQ_BYTES;
   static constexpr int OFF_VM = OFF_VS + VS_BYTES;
   static constexpr int STAGE = OFF_VM + VS_BYTES;
+  // Key scales/minima arrive per chunk of kKChunk tiles (16 groups = 32 contiguous bytes
+  // of each channel row), double-buffered: [2 buffers][scale, min][128 ch][16 groups] f16.
+  // A warp's copy instruction then covers 8 channel rows instead of 32.
+  static constexpr int KC_ROW = 4 * kKChunk * 2;  // bytes per channel row of one chunk
+  static constexpr int KC_BYTES = 2 * 128 * KC_ROW;
+  static constexpr int OFF_KC = kStagesK * STAGE;
   static constexpr int T_BYTES = 2 * 4 * 128 * 2;  // transposed key scale/min [2][4 groups][128 ch] f16
+  static constexpr int OFF_T = OFF_KC + 2 * KC_BYTES;
+  static constexpr int SMEM = OFF_T + T_BYTES;
 };
 
 struct KiviParams {
@@ -104,7 +110,7 @@ template <int BITS>
 __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const KiviParams p) {
   using L = KL<BITS>;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* tsm = smem + kStagesK * L::STAGE;  // transposed key scale / min of the current tile
+  uint8_t* tsm = smem + L::OFF_T;  // transposed key scale / min of the current tile
   // the residual-window kernel queued behind this one reads nothing this grid writes
   griddep_launch_dependents();
   const int split = blockIdx.x;
@@ -191,8 +197,13 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
   const int v_row = threadIdx.x / NVC, v_ck = threadIdx.x % NVC;
   const uint32_t* k_src = kq_base + int64_t(k_row) * p.kq_sc + t_begin / L::FPI + k_ck * 4;
   const uint32_t* v_src = vq_base + int64_t(t_begin + v_row) * p.vq_st + v_ck * 4;
-  const __half* ks_src = ks_base + int64_t(threadIdx.x) * p.ks_sc + t_begin / 32;
-  const __half* km_src = km_base + int64_t(threadIdx.x) * p.km_sc + t_begin / 32;
+  // key scale/min chunks: thread = (channel row kc_row + 32i, 8-byte piece kc_piece)
+  const int kc_row = threadIdx.x >> 2, kc_piece = threadIdx.x & 3;
+  const __half* ks_src = ks_base + int64_t(kc_row) * p.ks_sc + t_begin / 32 + 4 * kc_piece;
+  const __half* km_src = km_base + int64_t(kc_row) * p.km_sc + t_begin / 32 + 4 * kc_piece;
+  const int64_t ks_pass = 32 * p.ks_sc, km_pass = 32 * p.km_sc;
+  const int groups_end = (t_end + 31) / 32;  // first group index past the split
+  const uint32_t kc_dst = smem_u32(smem + L::OFF_KC) + kc_row * L::KC_ROW + kc_piece * 8;
   const __half* vs_src = vs_base + int64_t(t_begin + threadIdx.x) * p.vs_st;
   const __half* vm_src = vm_base + int64_t(t_begin + threadIdx.x) * p.vm_st;
   const int64_t k_pass = int64_t(128 / NCH) * p.kq_sc;  // channel rows per pass of the CTA
@@ -203,12 +214,21 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     const int t0 = t_begin + tile * kTile;
     const uint32_t sbase = smem_u32(smem + stage * L::STAGE);
     const int64_t vt = int64_t(tile) * kTile;
+    if (tile % kKChunk == 0) {
+      // key scale/min of tiles [tile, tile + kKChunk): 16 groups per channel row
+      const uint32_t dst = kc_dst + ((tile / kKChunk) & 1) * L::KC_BYTES;
+      const int goff = tile * 4 + 4 * kc_piece;  // first group of this piece, relative to t_begin
+      const int gv = max(0, min(4, groups_end - (t_begin / 32 + goff)));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        cp_async8(dst + i * 32 * L::KC_ROW, gv ? ks_src + i * ks_pass + tile * 4 : ks_base, gv * 2);
+        cp_async8(dst + 128 * L::KC_ROW + i * 32 * L::KC_ROW, gv ? km_src + i * km_pass + tile * 4 : km_base, gv * 2);
+      }
+    }
     if (t0 + kTile <= t_end) {
 #pragma unroll
       for (int i = 0; i < NCH; ++i)
         cp_async16(sbase + k_dst + i * (128 / NCH) * L::KQ_PITCH, k_src + i * k_pass + tile * L::KQ_WORDS, 16);
-      cp_async8(sbase + L::OFF_KS + threadIdx.x * 8, ks_src + tile * 4, 8);
-      cp_async8(sbase + L::OFF_KM + threadIdx.x * 8, km_src + tile * 4, 8);
 #pragma unroll
       for (int i = 0; i < NVC; ++i)
         cp_async16(sbase + v_dst + i * (128 / NVC) * L::VQ_PITCH, v_src + i * v_pass + vt * p.vq_st, 16);
@@ -222,9 +242,6 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
       for (int i = 0; i < NCH; ++i)
         cp_async16(sbase + k_dst + i * (128 / NCH) * L::KQ_PITCH,
                    kv ? k_src + i * k_pass + tile * L::KQ_WORDS : k_src, kv * 4);
-      const int gv = max(0, min(4, (t_end - t0 + 31) / 32));
-      cp_async8(sbase + L::OFF_KS + threadIdx.x * 8, ks_src + (gv ? tile * 4 : 0), gv * 2);
-      cp_async8(sbase + L::OFF_KM + threadIdx.x * 8, km_src + (gv ? tile * 4 : 0), gv * 2);
 #pragma unroll
       for (int i = 0; i < NVC; ++i) {
         const bool ok = t0 + v_row + i * (128 / NVC) < t_end;
@@ -260,8 +277,10 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     const uint8_t* st = smem + (it % kStagesK) * L::STAGE;
     {
       // transpose key scale / min of this tile to [group][channel] (one channel per thread)
-      const uint2 s4 = *reinterpret_cast<const uint2*>(st + L::OFF_KS + threadIdx.x * 8);
-      const uint2 m4 = *reinterpret_cast<const uint2*>(st + L::OFF_KM + threadIdx.x * 8);
+      const uint8_t* kc = smem + L::OFF_KC + ((it / kKChunk) & 1) * L::KC_BYTES + threadIdx.x * L::KC_ROW +
+                          (it % kKChunk) * 8;
+      const uint2 s4 = *reinterpret_cast<const uint2*>(kc);
+      const uint2 m4 = *reinterpret_cast<const uint2*>(kc + 128 * L::KC_ROW);
       uint16_t* ts = reinterpret_cast<uint16_t*>(tsm);
       ts[0 * 128 + threadIdx.x] = uint16_t(s4.x); ts[1 * 128 + threadIdx.x] = uint16_t(s4.x >> 16);
       ts[2 * 128 + threadIdx.x] = uint16_t(s4.y); ts[3 * 128 + threadIdx.x] = uint16_t(s4.y >> 16);
@@ -526,7 +545,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
 template <int BITS>
 int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
   using L = KL<BITS>;
-  const size_t smem = std::max<size_t>(size_t(kStagesK) * L::STAGE + L::T_BYTES, (2 * 4 * 8 + 4 * 8 * kRedPitch) * sizeof(float));
+  const size_t smem = std::max<size_t>(L::SMEM, (2 * 4 * 8 + 4 * 8 * kRedPitch) * sizeof(float));
   auto kern = kivi_decode_kernel<BITS>;
   static bool attr[64] = {false};
   int dev = 0;
