@@ -240,39 +240,42 @@ def run_reference(args, rank):
 
 
 # ----------------------------------------------------------------------------- extras
-def extras(dev, peak):
-    """Other decode paths at their configuration shapes (rank 0, single GPU)."""
-    from bytes_b200 import attention_kernels as ak, sparse_attention as sa, _ops
-    import gc
-    out = {}
-    g = torch.Generator(device=dev).manual_seed(7)
+def _rot(make, n):
+    return [make() for _ in range(n)]
 
-    def rot(make, n):
-        return [make() for _ in range(n)]
 
-    # c0: bf16 dense decode, B=1, 28/4 heads, S=8192, q pre-scaled by 1/sqrt(D)
+def path_c0(dev, peak, g):
+    """c0: bf16 dense decode, B=1, 28/4 heads, S=8192, q pre-scaled by 1/sqrt(D)."""
+    from bytes_b200 import attention_kernels as ak
     D = 128
-    sets = rot(lambda: ((torch.randn(1, 28, 1, D, device=dev, generator=g) / math.sqrt(D)).bfloat16(),
-                        torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16(),
-                        torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16()), 16)
+    sets = _rot(lambda: ((torch.randn(1, 28, 1, D, device=dev, generator=g) / math.sqrt(D)).bfloat16(),
+                         torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16(),
+                         torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16()), 16)
     gr = graph_of([lambda s=s: ak.decode_attn_bf16(*s) for s in sets])
     us = time_graph(gr, 20) / (20 * len(sets))
     b = nbytes(*sets[0][1:])
-    out["c0_bf16_decode"] = {"us": round(us, 2), "GBps": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 3)}
-    del sets, gr
+    return {"c0_bf16_decode": {"us": round(us, 2), "GBps": round(b / us / 1e3, 1),
+                               "frac": round(b / us / 1e3 / peak, 3)}}
 
-    # bf16 decode at 32K (c1 head shapes)
-    sets = rot(lambda: (torch.randn(8, 28, 1, D, device=dev, generator=g).bfloat16(),
-                        torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16(),
-                        torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16()), 2)
+
+def path_bf16_32k(dev, peak, g):
+    """bf16 dense decode at 32K context with the c1 head shapes (B=8, 28/4)."""
+    from bytes_b200 import attention_kernels as ak
+    D = 128
+    sets = _rot(lambda: (torch.randn(8, 28, 1, D, device=dev, generator=g).bfloat16(),
+                         torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16(),
+                         torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16()), 2)
     gr = graph_of([lambda s=s: ak.decode_attn_bf16(*s) for s in sets])
     us = time_graph(gr, 10) / (10 * len(sets))
     b = nbytes(*sets[0][1:])
-    out["bf16_decode_32k_B8"] = {"us": round(us, 2), "GBps": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 3)}
-    del sets, gr
+    return {"bf16_decode_32k_B8": {"us": round(us, 2), "GBps": round(b / us / 1e3, 1),
+                                   "frac": round(b / us / 1e3 / peak, 3)}}
 
-    # c2: PQ-LUT keys (16 x 8-dim subspaces, 256 centroids) + int8 V with f16 per-token scale
-    B, Hq, Hk, S, M, K = 4, 32, 8, 32768, 16, 256
+
+def path_c2(dev, peak, g):
+    """c2: PQ-LUT keys (16 x 8-dim subspaces, 256 centroids) + int8 V with f16 per-token scale."""
+    from bytes_b200 import attention_kernels as ak
+    B, Hq, Hk, S, M, K, D = 4, 32, 8, 32768, 16, 256, 128
 
     def mk2():
         lut = torch.randn(B, Hq, M, K, device=dev, generator=g) * 0.3
@@ -280,16 +283,19 @@ def extras(dev, peak):
         v8 = torch.randint(-127, 128, (B, Hk, S, D), device=dev, generator=g, dtype=torch.int32).to(torch.int8)
         vs = (torch.rand(B, Hk, S, device=dev, generator=g) * 0.02).half()
         return lut, codes, v8, vs
-    sets = rot(mk2, 3)
+    sets = _rot(mk2, 3)
     gr = graph_of([lambda s=s: ak.decode_attn_pq_lut_int8v(*s) for s in sets])
     us = time_graph(gr, 10) / (10 * len(sets))
     b = nbytes(*sets[0]) + M * K * 8 * 2 * Hk  # + per-head fp16 codebooks of the configuration
-    out["c2_pq_lut_int8v"] = {"us": round(us, 2), "GBps": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 3)}
-    del sets, gr
-    gc.collect()
+    return {"c2_pq_lut_int8v": {"us": round(us, 2), "GBps": round(b / us / 1e3, 1),
+                                "frac": round(b / us / 1e3 / peak, 3)}}
 
-    # c3: Quest top-64 pages + gather, and exact token top-k k=1024, B=16, 32/8, S=32768
-    B, Hq, Hk, S, kb, page = 16, 32, 8, 32768, 1024, 16
+
+def path_c3(dev, peak, g):
+    """c3: Quest top-64 pages + gather, exact token top-k k=1024 (B=16, 32/8, S=32768), top-k alone."""
+    from bytes_b200 import attention_kernels as ak, sparse_attention as sa, _ops
+    out = {}
+    B, Hq, Hk, S, kb, page, D = 16, 32, 8, 32768, 1024, 16, 128
     q = torch.randn(B, Hq, 1, D, device=dev, generator=g).bfloat16()
     k = torch.randn(B, Hk, S, D, device=dev, generator=g).bfloat16()
     v = torch.randn(B, Hk, S, D, device=dev, generator=g).bfloat16()
@@ -317,18 +323,32 @@ def extras(dev, peak):
     gr = graph_of([exact_step])
     us = time_graph(gr, 10) / 10
     kscan = nbytes(k)
-    scores = torch.empty(B, Hq, S, device=dev)
-    out["c3_exact_topk_decode"] = {"us": round(us, 2), "bytes_MB": round((kscan + 2 * scores.numel() * 4 + gathered) / 1e6, 1),
-                                   "frac": round((kscan + 2 * scores.numel() * 4 + gathered) / us / 1e3 / peak, 3)}
+    nscore = B * Hq * S
+    out["c3_exact_topk_decode"] = {"us": round(us, 2), "bytes_MB": round((kscan + 2 * nscore * 4 + gathered) / 1e6, 1),
+                                   "frac": round((kscan + 2 * nscore * 4 + gathered) / us / 1e3 / peak, 3)}
     s_ = ak.sparse_score_scalar(q, k, sc, score_bits=16)
     gr = graph_of([lambda: _ops.topk(s_, kb, sorted=False, want_values=False, idx_dtype=torch.int32)])
     us_tk = time_graph(gr, 20) / 20
     gr2 = graph_of([lambda: s_.topk(kb, dim=-1)])
     us_torch = time_graph(gr2, 20) / 20
     out["topk_select"] = {"rows": B * Hq, "n": S, "k": kb, "us": round(us_tk, 2), "torch_topk_us": round(us_torch, 2)}
-    del q, k, v, kmin, kmax, s_, gr, gr2
-    gc.collect()
-    torch.cuda.empty_cache()
+    return out
+
+
+PATHS = {"c0": path_c0, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3}
+
+
+def extras(dev, peak, only=None):
+    """Other decode paths at their configuration shapes (rank 0, single GPU)."""
+    import gc
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+    for name, fn in PATHS.items():
+        if only is not None and name != only:
+            continue
+        out.update(fn(dev, peak, g))
+        gc.collect()
+        torch.cuda.empty_cache()
     return out
 
 
@@ -340,6 +360,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--path", choices=sorted(PATHS), help="time only this secondary path and print its numbers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -368,6 +389,9 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peak, peak_kind = _peaks()
+    if args.path:
+        print(json.dumps(extras(dev, peak, only=args.path)), flush=True)
+        return
     c = CFG1
     sets = [kivi_inputs(dev, 1000 + rank * NBUF + i) for i in range(NBUF)]
     step_bytes = nbytes(*sets[0][1:])

@@ -375,12 +375,23 @@ struct CombineParams {
   int ms_rows;          // 1: partials laid out [rows][n]; 0: [n][rows]
 };
 
-__global__ void lse_combine_kernel(const CombineParams p) {
+constexpr int kCombThreads = 256;
+
+// One CTA per output row. Warp 0 turns the split maxima into weights; then thread
+// (slice, c4) accumulates channels 4*c4..4*c4+3 over splits slice, slice+ns, ... with
+// 16-byte loads (one warp reads a whole 512-byte partial row at D = 128), and the ns
+// slice sums meet in shared memory. VEC4 needs D % 4 == 0 and 16-byte aligned partial
+// rows; otherwise one channel per thread.
+template <bool VEC4>
+__global__ void __launch_bounds__(kCombThreads) lse_combine_kernel(const CombineParams p) {
   griddep_wait();  // partials of a programmatic predecessor (no-op after a plain launch)
-  extern __shared__ float wsm[];  // [n] weights
+  extern __shared__ __align__(16) float wsm[];  // [n4] weights, then [ns][D] slice sums
   const int row = blockIdx.x;
   __shared__ float sM, sL;
   auto midx = [&](int i) -> int64_t { return p.ms_rows ? int64_t(row) * p.n + i : int64_t(i) * p.m_s0 + row; };
+  auto orow = [&](int i) -> int64_t {
+    return p.ms_rows ? (int64_t(row) * p.n + i) * p.D : int64_t(i) * p.o_s0 + int64_t(row) * p.D;
+  };
   if (threadIdx.x < 32) {
     float M = -INFINITY;
     for (int i = threadIdx.x; i < p.n; i += 32) M = fmaxf(M, p.m[midx(i)]);
@@ -395,13 +406,33 @@ __global__ void lse_combine_kernel(const CombineParams p) {
     if (threadIdx.x == 0) { sM = M; sL = L; }
   }
   __syncthreads();
-  const int b = row / p.Hq, h = row % p.Hq;
-  for (int c = threadIdx.x; c < p.D; c += blockDim.x) {
-    float O = 0.f;
-    for (int i = 0; i < p.n; ++i) {
-      const int64_t oi = p.ms_rows ? (int64_t(row) * p.n + i) * p.D + c : int64_t(i) * p.o_s0 + int64_t(row) * p.D + c;
-      O += p.o[oi] * wsm[i];
+  float* red = wsm + ((p.n + 3) & ~3);
+  const int per = VEC4 ? p.D / 4 : p.D;  // threads per slice
+  const int ns = kCombThreads / per;     // split slices (>= 1: D <= kCombThreads * (VEC4 ? 4 : 1))
+  const int ci = threadIdx.x % per, sl = threadIdx.x / per;
+  if (sl < ns) {
+    if (VEC4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int i = sl; i < p.n; i += ns) {
+        const float4 v = *reinterpret_cast<const float4*>(p.o + orow(i) + 4 * ci);
+        const float w = wsm[i];
+        acc.x = fmaf(v.x, w, acc.x); acc.y = fmaf(v.y, w, acc.y);
+        acc.z = fmaf(v.z, w, acc.z); acc.w = fmaf(v.w, w, acc.w);
+      }
+      reinterpret_cast<float4*>(red)[sl * per + ci] = acc;
+    } else {
+      float acc = 0.f;
+#pragma unroll 4
+      for (int i = sl; i < p.n; i += ns) acc = fmaf(p.o[orow(i) + ci], wsm[i], acc);
+      red[sl * per + ci] = acc;
     }
+  }
+  __syncthreads();
+  const int b = row / p.Hq, h = row % p.Hq;
+  for (int c = threadIdx.x; c < p.D; c += kCombThreads) {
+    float O = 0.f;
+    for (int q = 0; q < ns; ++q) O += red[q * p.D + c];
     if (p.mode == 0) {
       store_out(p.out, p.out_dtype, int64_t(b) * p.o_sb + int64_t(h) * p.o_sh + c, O / sL);
     } else {
@@ -409,6 +440,27 @@ __global__ void lse_combine_kernel(const CombineParams p) {
       if (c == 0) { p.em[row] = sM; p.el[row] = sL; }
     }
   }
+}
+
+// Launches the combine for c.rows rows (plain, or as a programmatic dependent).
+int launch_combine_kernel(const CombineParams& c, cudaStream_t st, bool pdl) {
+  if (c.rows == 0) return BD_OK;
+  if (c.D <= 0 || c.D > kCombThreads * 4) return fail(BD_ERR_UNSUPPORTED, "combine supports head_dim up to 1024");
+  const bool vec4 = c.D % 4 == 0 && (reinterpret_cast<uintptr_t>(c.o) & 15) == 0 && (c.ms_rows || c.o_s0 % 4 == 0) &&
+                    c.D / 4 <= kCombThreads;
+  const int per = vec4 ? c.D / 4 : c.D;
+  if (per > kCombThreads) return fail(BD_ERR_UNSUPPORTED, "combine: head_dim not a multiple of 4 above 256");
+  const int ns = kCombThreads / per;
+  const size_t smem = (size_t((c.n + 3) & ~3) + size_t(ns) * c.D) * sizeof(float);
+  auto kern = vec4 ? lse_combine_kernel<true> : lse_combine_kernel<false>;
+  if (smem > 48 * 1024) {
+    const int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                              "cudaFuncSetAttribute(combine)");
+    if (rc) return rc;
+  }
+  if (pdl) return launch_programmatic(kern, dim3(c.rows), dim3(kCombThreads), smem, st, c, "lse_combine_kernel launch");
+  kern<<<c.rows, kCombThreads, smem, st>>>(c);
+  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
 }
 
 struct Plan {
@@ -547,12 +599,7 @@ int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* 
   c.rows = B * Hq; c.n = part.nsplit; c.D = D; c.Hq = Hq; c.ms_rows = 1;
   c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
   c.mode = 0;
-  if (c.rows == 0) return BD_OK;
-  if (pdl)
-    return launch_programmatic(lse_combine_kernel, dim3(c.rows), dim3(128), size_t(c.n) * sizeof(float), st, c,
-                               "lse_combine_kernel launch");
-  lse_combine_kernel<<<c.rows, 128, size_t(c.n) * sizeof(float), st>>>(c);
-  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+  return launch_combine_kernel(c, st, pdl);
 }
 
 // ---- static scratch for bd_decode_attn_noalloc --------------------------------------
@@ -631,8 +678,7 @@ int bd_decode_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, c
   c.rows = int(rows); c.n = pl.n_splits; c.D = pl.D; c.Hq = p.Hq; c.ms_rows = 1;
   c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
   c.mode = 0;
-  lse_combine_kernel<<<int(rows), pl.D, pl.n_splits * sizeof(float), st>>>(c);
-  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+  return launch_combine_kernel(c, st, false);
 }
 
 // Variant of bd_decode_attn for callers that cannot hand us a workspace: its split
@@ -694,8 +740,7 @@ int bd_decode_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tens
   c.rows = int(rows); c.n = pl.n_splits; c.D = int(D); c.Hq = int(Hq); c.ms_rows = 1;
   c.mode = 1;
   c.em = static_cast<float*>(m->data); c.el = static_cast<float*>(l->data); c.eo = static_cast<float*>(o->data);
-  lse_combine_kernel<<<int(rows), int(D), pl.n_splits * sizeof(float), st>>>(c);
-  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+  return launch_combine_kernel(c, st, false);
 }
 
 int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o, const bd_tensor* out,
@@ -724,8 +769,7 @@ int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o, c
   c.m_s0 = m->stride[0]; c.o_s0 = o->stride[0]; c.ms_rows = 0;
   c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
   c.mode = 0;
-  lse_combine_kernel<<<c.rows, 128, size_t(n) * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(c);
-  return cuda_check(cudaGetLastError(), "lse_combine_kernel launch");
+  return launch_combine_kernel(c, reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 }  // extern "C"
