@@ -34,7 +34,7 @@ namespace {
 
 constexpr int kPW = 8;              // warps per CTA
 constexpr int kPRows = 16 * kPW;    // tokens per tile
-constexpr int kPStages = 3;
+constexpr int kPStages = 2;  // 2 stages: the LUT chunk plus two tiles fit twice per SM
 constexpr int kHC = 4;              // query heads per CTA
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kLn2P = 0.6931471805599453f;
@@ -53,7 +53,7 @@ struct PqParams {
   const float* vcent; int64_t vc_sm, vc_sk, vc_sd; int Mv, Kv, dsv;
   const int32_t* btab; int64_t bt_sb, bt_ss; const int32_t* clens; int bsz;
   int B, Hq, Hk, G, S, M, K, D;
-  int head_chunks, tiles_per_split, n_splits;
+  int head_chunks, ntiles, n_splits;  // split s owns tiles [s*ntiles/n_splits, (s+1)*ntiles/n_splits)
   float* scores_out; int64_t so_sb, so_sh;  // V_NONE mode
   float* part_m; float* part_l; float* part_o;
 };
@@ -89,7 +89,7 @@ __device__ __forceinline__ float ld16f(const uint16_t* p, int64_t off, int dt) {
 }
 
 template <int VK, bool PAGED, bool OUTL, int D>
-__global__ void __launch_bounds__(kPW * 32, 1) pq_decode_kernel(const PqParams p) {
+__global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int KSTEPS = D / 16;
   const PqSmem L = pq_smem(VK, p.M, p.K, OUTL ? p.C : 0, D, p.Mv);
@@ -106,18 +106,32 @@ __global__ void __launch_bounds__(kPW * 32, 1) pq_decode_kernel(const PqParams p
   const int h0 = chunk * kHC;
   const int nheads = min(kHC, p.G - h0);
   const int S_b = PAGED ? min(p.S, p.clens[b]) : p.S;
-  const int t_begin = split * p.tiles_per_split * kPRows;
-  const int t_end = min(S_b, t_begin + p.tiles_per_split * kPRows);
+  const int tile0 = int(int64_t(split) * p.ntiles / p.n_splits);
+  const int t_begin = tile0 * kPRows;
+  const int t_end = min(S_b, int(int64_t(split + 1) * p.ntiles / p.n_splits) * kPRows);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kPRows - 1) / kPRows : 0;
 
-  // ---- LUT of the chunk's heads -> smem [M][K][4]
-  for (int i = threadIdx.x; i < p.M * p.K * kHC; i += kPW * 32) {
-    const int h = i % kHC, r = i / kHC;
-    const int c = r % p.K, j = r / p.K;
-    float x = 0.f;
-    if (h < nheads)
-      x = p.lut[int64_t(b) * p.l_sb + int64_t(hk * p.G + h0 + h) * p.l_sh + int64_t(j) * p.l_sm + int64_t(c) * p.l_sk];
-    lut_s[i] = x;
+  // ---- LUT of the chunk's heads -> smem [M][K][4]; rows of a head are read four
+  // entries at a time when they are contiguous and 16-byte aligned
+  {
+    const int MK = p.M * p.K;
+    const bool vec = p.l_sk == 1 && p.l_sm == p.K && (p.K & 3) == 0 && (p.l_sh & 3) == 0 && (p.l_sb & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.lut) & 15) == 0;
+    for (int h = 0; h < kHC; ++h) {
+      const float* src = p.lut + int64_t(b) * p.l_sb + int64_t(hk * p.G + h0 + min(h, nheads - 1)) * p.l_sh;
+      if (vec) {
+        for (int i = threadIdx.x; i < MK / 4; i += kPW * 32) {
+          const float4 x = h < nheads ? reinterpret_cast<const float4*>(src)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+          float* d = lut_s + (4 * i) * kHC + h;
+          d[0] = x.x; d[kHC] = x.y; d[2 * kHC] = x.z; d[3 * kHC] = x.w;
+        }
+      } else {
+        for (int i = threadIdx.x; i < MK; i += kPW * 32) {
+          const int c = i % p.K, j = i / p.K;
+          lut_s[i * kHC + h] = h < nheads ? src[int64_t(j) * p.l_sm + int64_t(c) * p.l_sk] : 0.f;
+        }
+      }
+    }
   }
   // outlier query of the lane's head pair (tq & 1): heads 2hp, 2hp+1
   const int hp = tq & 1;
@@ -257,10 +271,27 @@ __global__ void __launch_bounds__(kPW * 32, 1) pq_decode_kernel(const PqParams p
     {
       const uint8_t* ca = st + (r0 + g) * L.codes_pitch;
       const uint8_t* cb = st + (r0 + g + 8) * L.codes_pitch;
-      for (int j = jlo; j < jhi; ++j) {
-        const float2 a = *reinterpret_cast<const float2*>(lut_s + (j * p.K + ca[j]) * kHC + 2 * hp);
-        const float2 c = *reinterpret_cast<const float2*>(lut_s + (j * p.K + cb[j]) * kHC + 2 * hp);
-        sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
+      const float* lj = lut_s + jlo * p.K * kHC + 2 * hp;  // LUT rows of subspace j, stepped per j
+      const int jstep = p.K * kHC;
+      if (p.M == 16) {
+        // the lane's 8 subspaces of both tokens as one 8-byte load each
+        const uint2 wa = *reinterpret_cast<const uint2*>(ca + jlo), wb = *reinterpret_cast<const uint2*>(cb + jlo);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t xa = ((j < 4 ? wa.x : wa.y) >> (8 * (j & 3))) & 0xffu;
+          const uint32_t xb = ((j < 4 ? wb.x : wb.y) >> (8 * (j & 3))) & 0xffu;
+          const float2 a = *reinterpret_cast<const float2*>(lj + xa * kHC);
+          const float2 c = *reinterpret_cast<const float2*>(lj + xb * kHC);
+          sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
+          lj += jstep;
+        }
+      } else {
+        for (int j = jlo; j < jhi; ++j) {
+          const float2 a = *reinterpret_cast<const float2*>(lj + ca[j] * kHC);
+          const float2 c = *reinterpret_cast<const float2*>(lj + cb[j] * kHC);
+          sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
+          lj += jstep;
+        }
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
@@ -610,13 +641,14 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
   const int head_chunks = int((Hq / Hk + kHC - 1) / kHC);
   const int64_t ntiles = (S + kPRows - 1) / kPRows;
   const int64_t pairs = B * Hk * head_chunks;
-  const int64_t slots = num_sms();
+  // resident CTAs per SM from the shared-memory footprint (227 KB usable per SM)
+  const size_t cta_smem = std::max(size_t(Ls.lut_bytes) + size_t(kPStages) * Ls.stage + Ls.recon_bytes,
+                                   (2 * kPW * 8 + size_t(kPW) * kHC * size_t(D)) * sizeof(float)) + 1024;
+  const int64_t per_sm = std::max<int64_t>(1, std::min<int64_t>(2, int64_t(227 * 1024) / int64_t(cta_smem)));
+  const int64_t slots = per_sm * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / pairs;
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
-  const int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;
-  splits = ntiles > 0 ? (ntiles + tps - 1) / tps : 1;
   const size_t need = scores_only ? 0 : partials_bytes(size_t(B * Hq), int(splits), int(D));
-  (void)Ls;
   if (ws_query) { *ws_query = need; return BD_OK; }
   if (!out_or_scores) return fail(BD_ERR_NULL, "output descriptor is NULL");
   if (!scores_only && (!workspace || workspace_bytes < need))
@@ -656,7 +688,7 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
   }
   p.B = int(B); p.Hq = int(Hq); p.Hk = int(Hk); p.G = int(Hq / Hk); p.S = int(S); p.M = int(M); p.K = int(K);
   p.D = int(D);
-  p.head_chunks = head_chunks; p.tiles_per_split = int(tps); p.n_splits = int(splits);
+  p.head_chunks = head_chunks; p.ntiles = int(ntiles); p.n_splits = int(splits);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (B * Hq == 0) return BD_OK;
   if (scores_only) {
