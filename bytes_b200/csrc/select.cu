@@ -448,6 +448,81 @@ __global__ void __launch_bounds__(kQPages) quest_bounds_kernel(const void* q, in
   }
 }
 
+// Tensor-core form of the same bound for a bf16 query. Since max_pd >= min_pd,
+//   max(q_d*min_pd, q_d*max_pd) = q+_d*max_pd + q-_d*min_pd   (q+ = max(q,0), q- = min(q,0)),
+// so the bounds of a page tile are one GEMM: [max_p | min_p] (pages x 2D, bf16) times
+// [q+ ; q-] (2D x heads, bf16, exact), fp32 accumulate -- mma.sync m16n8k16, 16 pages per
+// warp, 8 heads per CTA. The page rows stream through a padded shared-memory tile
+// (conflict-free ldmatrix); bytes per page and KV head: 4*D.
+constexpr int kQmPages = 64;  // pages per CTA (4 warps x 16)
+
+struct QuestMmaParams {
+  const __nv_bfloat16* q; int64_t q_sb, q_sh;
+  const __nv_bfloat16* kmin; const __nv_bfloat16* kmax; int64_t m_sb, m_sh, m_sp;
+  int Hq, Hk, G, head_chunks, np, force_from;
+  float scaling;
+  float* bounds;
+};
+
+template <int D>
+__global__ void __launch_bounds__(128) quest_bounds_mma_kernel(const QuestMmaParams p) {
+  constexpr int ROWB = 4 * D;        // [max | min] bf16 bytes per page
+  constexpr int PITCH = ROWB + 16;   // padded row
+  constexpr int CH = ROWB / 16;      // 16-byte chunks per page
+  constexpr int KSTEPS = 2 * D / 16;
+  __shared__ __align__(16) uint8_t sm[kQmPages * PITCH];
+  const int b = blockIdx.z, hk = blockIdx.y / p.head_chunks, chunk = blockIdx.y % p.head_chunks;
+  const int p0 = blockIdx.x * kQmPages;
+  const int npg = min(kQmPages, p.np - p0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int64_t mbase = int64_t(b) * p.m_sb + int64_t(hk) * p.m_sh;
+  for (int c = threadIdx.x; c < kQmPages * CH; c += 128) {
+    const int r = c / CH, cc = c % CH;
+    const bool ok = r < npg;
+    const __nv_bfloat16* src = (cc < CH / 2 ? p.kmax : p.kmin) + mbase + int64_t(ok ? p0 + r : 0) * p.m_sp +
+                               (cc % (CH / 2)) * 8;
+    cp_async16(smem_u32(sm + r * PITCH + cc * 16), src, ok ? 16 : 0);
+  }
+  cp_async_commit();
+  // B fragments: head n = g of this chunk; k < D -> q+ (max rows), k >= D -> q- (min rows)
+  const int h = chunk * 8 + g;
+  const bool hv = h < p.G;
+  const __nv_bfloat16* qr = p.q + int64_t(b) * p.q_sb + int64_t(hk * p.G + (hv ? h : 0)) * p.q_sh;
+  uint32_t bq[KSTEPS][2];
+#pragma unroll
+  for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int k = kk * 16 + 8 * e + 2 * tq;
+      const int ch = k < D ? k : k - D;
+      uint32_t w = hv ? *reinterpret_cast<const uint32_t*>(qr + ch) : 0u;
+      __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&w);
+      const __nv_bfloat162 z = __float2bfloat162_rn(0.f);
+      x = k < D ? __hmax2(x, z) : __hmin2(x, z);
+      bq[kk][e] = *reinterpret_cast<uint32_t*>(&x);
+    }
+  cp_async_wait<0>();
+  __syncthreads();
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t arow = smem_u32(sm + (warp * 16 + (lane & 15)) * PITCH + (lane >> 4) * 16);
+#pragma unroll
+  for (int kk = 0; kk < KSTEPS; ++kk) {
+    uint32_t a0, a1, a2, a3;
+    ldmatrix_x4(a0, a1, a2, a3, arow + kk * 32);
+    mma_bf16(acc, a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
+  }
+  // acc: (page 16w+g, heads 2tq, 2tq+1), (page 16w+g+8, heads 2tq, 2tq+1)
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int pg = p0 + warp * 16 + g + (e >> 1) * 8;
+    const int hh = chunk * 8 + 2 * tq + (e & 1);
+    if (pg < p.np && hh < p.G) {
+      const float v = pg >= p.force_from ? INFINITY : acc[e] * p.scaling;
+      p.bounds[(int64_t(b) * p.Hq + hk * p.G + hh) * p.np + pg] = v;
+    }
+  }
+}
+
 __global__ void quest_expand_kernel(const int64_t* pidx, int npick, int page, int S, int rows, void* out, int out64,
                                     int64_t o_rs) {
   const int row = blockIdx.y;
@@ -677,10 +752,24 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
   if (q->stride[2] != 1) return fail(BD_ERR_STRIDE, "q innermost dim must be contiguous");
   if ((rc = check_rows_aligned(kmin, "kmin")) || (rc = check_rows_aligned(kmax, "kmax"))) return rc;
   if (B * Hq * np == 0) return BD_OK;
-  dim3 grid(unsigned((np + kQPages - 1) / kQPages), unsigned(Hk), unsigned(B));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   auto* mn = static_cast<const __nv_bfloat16*>(kmin->data);
   auto* mx = static_cast<const __nv_bfloat16*>(kmax->data);
+  // bf16 query with 4-byte aligned channel pairs: tensor-core bounds
+  if (q->dtype == BD_BF16 && (reinterpret_cast<uintptr_t>(q->data) & 3) == 0 && (q->stride[0] % 2) == 0 &&
+      (q->stride[1] % 2) == 0) {
+    QuestMmaParams p{};
+    p.q = static_cast<const __nv_bfloat16*>(q->data); p.q_sb = q->stride[0]; p.q_sh = q->stride[1];
+    p.kmin = mn; p.kmax = mx; p.m_sb = kmin->stride[0]; p.m_sh = kmin->stride[1]; p.m_sp = kmin->stride[2];
+    p.Hq = int(Hq); p.Hk = int(Hk); p.G = int(Hq / Hk); p.head_chunks = (p.G + 7) / 8; p.np = int(np);
+    p.force_from = force_from_page; p.scaling = scaling; p.bounds = static_cast<float*>(bounds->data);
+    dim3 gm(unsigned((np + kQmPages - 1) / kQmPages), unsigned(Hk * p.head_chunks), unsigned(B));
+    if (D == 128) quest_bounds_mma_kernel<128><<<gm, 128, 0, st>>>(p);
+    else if (D == 64) quest_bounds_mma_kernel<64><<<gm, 128, 0, st>>>(p);
+    else quest_bounds_mma_kernel<32><<<gm, 128, 0, st>>>(p);
+    return cuda_check(cudaGetLastError(), "quest_bounds_mma_kernel launch");
+  }
+  dim3 grid(unsigned((np + kQPages - 1) / kQPages), unsigned(Hk), unsigned(B));
   if (D == 128)
     quest_bounds_kernel<128><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
         kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
