@@ -335,7 +335,20 @@ def path_c3(dev, peak, g):
     return out
 
 
-PATHS = {"c0": path_c0, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3}
+def path_topk(dev, peak, g):
+    """Top-k select alone: 512 rows x 32768 fp32 scores (c3's B*Hq rows), k = 1024, vs torch.topk."""
+    from bytes_b200 import _ops
+    rows, n, kb = 16 * 32, 32768, 1024
+    s_ = torch.randn(rows, n, device=dev, generator=g)
+    gr = graph_of([lambda: _ops.topk(s_, kb, sorted=False, want_values=False, idx_dtype=torch.int32)])
+    us_tk = time_graph(gr, 20) / 20
+    gr2 = graph_of([lambda: s_.topk(kb, dim=-1)])
+    us_torch = time_graph(gr2, 20) / 20
+    return {"topk_alone": {"rows": rows, "n": n, "k": kb, "us": round(us_tk, 2), "torch_topk_us": round(us_torch, 2),
+                           "GBps": round(rows * n * 4 / us_tk / 1e3, 1)}}
+
+
+PATHS = {"c0": path_c0, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3, "topk": path_topk}
 
 
 def extras(dev, peak, only=None):

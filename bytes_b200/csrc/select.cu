@@ -68,6 +68,322 @@ __device__ __forceinline__ int warp_base_scan(int v, int* red, int* total) {
   return base;
 }
 
+// Block-wide exclusive scan of one int per thread (1024 threads); red[] holds 33 ints.
+__device__ __forceinline__ int block_excl_scan(int v, int* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int x = red[lane];
+    int wi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    red[lane] = wi - x;
+  }
+  __syncthreads();
+  const int r = red[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// In a digit histogram of nb bins, find the digit holding the `remaining`-th largest key
+// (digits scanned from nb-1 down) and the number of keys in higher digits. Thread t
+// owns the bins nb-1-t*per .. nb-per-t*per. Results in *s_digit, *s_above.
+__device__ __forceinline__ void find_digit(const int* hist, int nb, int remaining, int* red, int* s_digit,
+                                           int* s_above) {
+  const int per = nb > kTkThreads ? nb / kTkThreads : 1;
+  const int d0 = nb - 1 - int(threadIdx.x) * per;
+  int sum = 0;
+  if (d0 >= 0)
+    for (int j = 0; j < per; ++j) sum += hist[d0 - j];
+  const int excl = block_excl_scan(sum, red);
+  if (d0 >= 0 && excl < remaining && excl + sum >= remaining) {
+    int acc = excl;
+    for (int j = 0; j < per; ++j) {
+      const int c = hist[d0 - j];
+      if (acc + c >= remaining) { *s_digit = d0 - j; *s_above = acc; break; }
+      acc += c;
+    }
+  }
+  __syncthreads();
+}
+
+constexpr int kCandMax = 2048;  // candidates of the first 12-bit digit kept for the remaining digits
+constexpr int kWarpCand = kCandMax / kTkWarps;  // candidate slots per warp
+
+// Top-k for a row held in shared memory with 16-byte aligned float4 access (n % 4 == 0).
+// One load pass builds a 12-bit histogram (bits 31..20 of the key); one filter pass copies
+// the keys of the threshold digit (a few hundred for real-valued scores) with their
+// indices; the remaining 20 bits (12 + 8) are resolved on those candidates only, or on the
+// whole row if they overflow kCandMax. Selection and ordering rules as topk_kernel.
+__global__ void __launch_bounds__(kTkThreads, 1) topk_fast_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int red[33];
+  __shared__ int s_digit, s_above, s_overflow;
+  __shared__ int s_wcnt[kTkWarps];
+  const int n = p.n, k = min(p.k, p.n), n4 = p.n >> 2;
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* src = p.scores + int64_t(row / p.rows_per_b) * p.b_stride + int64_t(row % p.rows_per_b) * p.row_stride;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
+  uint4* keys4 = reinterpret_cast<uint4*>(smem);
+  int* hist = reinterpret_cast<int*>(smem + size_t(n) * 4);  // [4096]
+  uint32_t* ck = reinterpret_cast<uint32_t*>(hist + 4096);     // [kCandMax], kWarpCand per warp
+  if (k <= 0) return;
+
+  // ---- load, keys to shared memory, 12-bit histogram
+  if (threadIdx.x == 0) s_overflow = 0;
+  for (int i = threadIdx.x; i < 4096; i += kTkThreads) hist[i] = 0;
+  __syncthreads();
+  {
+    // eight 16-byte loads in flight per thread before any of them is consumed
+    constexpr int U = 8;
+    const float4* src4 = reinterpret_cast<const float4*>(src);
+    for (int c0 = 0; c0 < n4; c0 += U * kTkThreads) {
+      float4 x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = c0 + u * kTkThreads + threadIdx.x;
+        x[u] = i < n4 ? src4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = c0 + u * kTkThreads + threadIdx.x;
+        if (i < n4) {
+          const uint4 kk = make_uint4(f2key(x[u].x), f2key(x[u].y), f2key(x[u].z), f2key(x[u].w));
+          keys4[i] = kk;
+          atomicAdd(&hist[kk.x >> 20], 1); atomicAdd(&hist[kk.y >> 20], 1);
+          atomicAdd(&hist[kk.z >> 20], 1); atomicAdd(&hist[kk.w >> 20], 1);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const bool take_all = k >= n;
+  uint32_t prefix = 0, mask = 0;
+  int remaining = k, eq_total = 0;
+  if (!take_all) {
+    find_digit(hist, 4096, remaining, red, &s_digit, &s_above);
+    prefix = uint32_t(s_digit) << 20;
+    mask = 0xfff00000u;
+    remaining -= s_above;
+    // ---- candidates: keys whose top 12 bits equal the threshold digit, appended to a
+    // per-warp buffer of kWarpCand slots (no shared counter); any overflow sends the
+    // remaining digits to the whole row
+    {
+      const unsigned lt = (1u << lane) - 1u;
+      uint32_t* wck = ck + warp * kWarpCand;
+      int wcnt = 0;  // warp-uniform
+      for (int i0 = 0; i0 < n4; i0 += kTkThreads) {  // warp-uniform trip count
+        const int i = i0 + threadIdx.x;
+        const uint4 kk = i < n4 ? keys4[i] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t kv[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool m = i < n4 && (kv[e] & mask) == prefix;
+          const unsigned bm = __ballot_sync(0xffffffffu, m);
+          const int pos = wcnt + __popc(bm & lt);
+          if (m && pos < kWarpCand) wck[pos] = kv[e];
+          wcnt += __popc(bm);
+        }
+      }
+      if (lane == 0) {
+        s_wcnt[warp] = wcnt;
+        if (wcnt > kWarpCand) s_overflow = 1;
+      }
+    }
+    __syncthreads();
+    const bool in_cand = s_overflow == 0;
+    // ---- remaining digits: bits 19..8 (12 bits), then 7..0 (8 bits)
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+      const int shift = pass == 0 ? 8 : 0, nb = pass == 0 ? 4096 : 256;
+      for (int i = threadIdx.x; i < nb; i += kTkThreads) hist[i] = 0;
+      __syncthreads();
+      if (in_cand) {
+        for (int j = threadIdx.x; j < kCandMax; j += kTkThreads) {
+          if (j % kWarpCand >= s_wcnt[j / kWarpCand]) continue;
+          const uint32_t kk = ck[j];
+          if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & uint32_t(nb - 1)], 1);
+        }
+      } else {
+        for (int j = threadIdx.x; j < n; j += kTkThreads) {
+          const uint32_t kk = keys[j];
+          if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & uint32_t(nb - 1)], 1);
+        }
+      }
+      __syncthreads();
+      find_digit(hist, nb, remaining, red, &s_digit, &s_above);
+      prefix |= uint32_t(s_digit) << shift;
+      mask |= uint32_t(nb - 1) << shift;
+      remaining -= s_above;
+    }
+    eq_total = hist[s_digit];  // keys equal to the full threshold (last digit's bin)
+  }
+  // threshold T = prefix; keep all keys > T and the `remaining` lowest-index keys == T.
+  const uint32_t T = prefix;
+  const int keep_eq = remaining;
+  const unsigned lt = (1u << lane) - 1u;
+  uint32_t* wk = reinterpret_cast<uint32_t*>(ck + kCandMax);
+  const int kpow = p.sorted ? (k <= 1 ? 1 : 1 << (32 - __clz(k - 1))) : 0;
+  int* wi = reinterpret_cast<int*>(wk + kpow);
+  const int seg4 = (n4 + kTkWarps - 1) / kTkWarps;  // uint4 per warp segment
+  const int s0 = min(n4, warp * seg4), s1 = min(n4, s0 + seg4);
+  auto emit = [&](int o, uint32_t key, int ix) {
+    if (p.sorted) {
+      wk[o] = key;
+      wi[o] = ix;
+    } else {
+      if (p.vals) p.vals[int64_t(row) * p.v_rs + o] = key2f(key);
+      if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + o] = ix;
+      else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + o] = ix;
+    }
+  };
+  if (take_all || keep_eq == eq_total) {
+    // every key >= T is selected (exactly k of them): one count pass, one write pass
+    int cnt = 0;
+    for (int i = s0 + lane; i < s1; i += 32) {
+      const uint4 x = keys4[i];
+      cnt += (x.x >= T) + (x.y >= T) + (x.z >= T) + (x.w >= T);
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    int tot;
+    int pos = warp_base_scan(cnt, red, &tot);
+    for (int i0 = s0; i0 < s1; i0 += 32) {  // warp-uniform trip count
+      const int i = i0 + lane;
+      const uint4 x = i < s1 ? keys4[i] : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t kv[4] = {x.x, x.y, x.z, x.w};
+      bool sel[4];
+      unsigned bal[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sel[e] = i < s1 && kv[e] >= T;
+        bal[e] = __ballot_sync(0xffffffffu, sel[e]);
+      }
+      if ((bal[0] | bal[1] | bal[2] | bal[3]) == 0u) continue;
+      int o = pos + __popc(bal[0] & lt) + __popc(bal[1] & lt) + __popc(bal[2] & lt) + __popc(bal[3] & lt);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (sel[e]) emit(o++, kv[e], 4 * i + e);
+      pos += __popc(bal[0]) + __popc(bal[1]) + __popc(bal[2]) + __popc(bal[3]);
+    }
+  } else {
+
+  // ---- general case (ties at T trimmed by index): ranks of the equal keys in index
+  // order; warp w walks a contiguous segment, 4 keys per lane per step
+  auto load4 = [&](int i, uint32_t* kv) {
+    const uint4 x = i < s1 ? keys4[i] : make_uint4(0u, 0u, 0u, 0u);
+    kv[0] = x.x; kv[1] = x.y; kv[2] = x.z; kv[3] = x.w;
+  };
+  int eq_cnt = 0;
+  if (!take_all)
+    for (int i0 = s0; i0 < s1; i0 += 32) {
+      const int i = i0 + lane;
+      uint32_t kv[4];
+      load4(i, kv);
+      int c = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c += (i < s1 && kv[e] == T);
+      eq_cnt += __reduce_add_sync(0xffffffffu, c);
+    }
+  int eq_total;
+  const int eq_base = warp_base_scan(eq_cnt, red, &eq_total);
+  // selection flags of a step: sel bit e of lane; returns the lane's selected count
+  auto step_sel = [&](int i, const uint32_t* kv, int& eq_run, int* sel) {
+    int eqf[4], eq_own = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { eqf[e] = (i < s1 && kv[e] == T); eq_own += eqf[e]; }
+    // equal keys before this lane in the step: inclusive scan of eq_own over lanes
+    int incl = eq_own;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int rank = eq_run + incl - eq_own;
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      sel[e] = i < s1 && (take_all || kv[e] > T || (eqf[e] && rank < keep_eq));
+      rank += eqf[e];
+      cnt += sel[e];
+    }
+    eq_run += __shfl_sync(0xffffffffu, incl, 31);
+    return cnt;
+  };
+  int sel_cnt = 0;
+  {
+    int eq_run = eq_base;
+    for (int i0 = s0; i0 < s1; i0 += 32) {
+      const int i = i0 + lane;
+      uint32_t kv[4];
+      int sel[4];
+      load4(i, kv);
+      sel_cnt += __reduce_add_sync(0xffffffffu, step_sel(i, kv, eq_run, sel));
+    }
+  }
+  int sel_total;
+  const int sel_base = warp_base_scan(sel_cnt, red, &sel_total);
+  {
+    int eq_run = eq_base, pos = sel_base;
+    for (int i0 = s0; i0 < s1; i0 += 32) {
+      const int i = i0 + lane;
+      uint32_t kv[4];
+      int sel[4];
+      load4(i, kv);
+      const int c = step_sel(i, kv, eq_run, sel);
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int o = pos + incl - c;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (sel[e]) emit(o++, kv[e], 4 * i + e);
+      pos += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  }  // general case
+  if (!p.sorted) return;
+  __syncthreads();
+  // ---- bitonic sort of kpow (key desc, index asc); padding sorts last
+  for (int i = k + threadIdx.x; i < kpow; i += kTkThreads) { wk[i] = 0u; wi[i] = 0x7fffffff; }
+  __syncthreads();
+  for (int size = 2; size <= kpow; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int t = threadIdx.x; t < kpow / 2; t += kTkThreads) {
+        const int lo = 2 * t - (t & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc_block = ((lo & size) == 0);
+        const uint32_t ka = wk[lo], kb = wk[hi];
+        const int ia = wi[lo], ib = wi[hi];
+        const bool a_first = (ka > kb) || (ka == kb && ia < ib);
+        if (a_first != desc_block) {
+          wk[lo] = kb; wk[hi] = ka;
+          wi[lo] = ib; wi[hi] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int o = threadIdx.x; o < k; o += kTkThreads) {
+    if (p.vals) p.vals[int64_t(row) * p.v_rs + o] = key2f(wk[o]);
+    if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + o] = wi[o];
+    else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + o] = wi[o];
+  }
+}
+
 template <bool SMEM_ROW>
 __global__ void __launch_bounds__(kTkThreads, 1) topk_kernel(const TopkParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -551,6 +867,23 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
   const size_t smem = (in_smem ? size_t(n) * 4 : 0) + wbytes;
   if (smem > 220 * 1024) return fail(BD_ERR_UNSUPPORTED, "top-k: sorted output of this many elements does not fit");
   int rc;
+  const size_t fast_smem = size_t(n) * 4 + 4096 * 4 + size_t(kCandMax) * 4 + wbytes;
+  const bool aligned = (reinterpret_cast<uintptr_t>(scores) & 15) == 0 && row_stride % 4 == 0 &&
+                       (rows_per_b >= rows || b_stride % 4 == 0);
+  if (in_smem && n % 4 == 0 && n > 0 && aligned && fast_smem <= 220 * 1024) {
+    static bool attr_f[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_f[dev & 63]) {
+      if ((rc = cuda_check(cudaFuncSetAttribute(topk_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                220 * 1024),
+                           "cudaFuncSetAttribute(topk_fast)")))
+        return rc;
+      attr_f[dev & 63] = true;
+    }
+    topk_fast_kernel<<<rows, kTkThreads, fast_smem, st>>>(p);
+    return cuda_check(cudaGetLastError(), "topk_fast_kernel launch");
+  }
   if (in_smem) {
     static bool attr[64] = {false};
     int dev = 0;

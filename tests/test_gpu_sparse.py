@@ -101,6 +101,16 @@ def test_topk_random_rows(cuda, n, k):
     _topk_check(s, k, False)
 
 
+@pytest.mark.parametrize("sorted_", [True, False])
+def test_topk_threshold_bucket_overflow(cuda, sorted_):
+    # three distinct values over 32768 keys: the threshold's first digit holds ~11K keys,
+    # more than the candidate buffer, so the remaining digits are resolved on the whole row
+    g = gen(5)
+    s = torch.randint(0, 3, (4, 32768), generator=g).float()
+    for k in ((1000, 4000) if sorted_ else (1000, 20000)):  # sorted output must fit shared memory
+        _topk_check(s, k, sorted_)
+
+
 def test_topk_3d_rows(cuda):
     g = gen(3)
     s = torch.randn(2, 8, 3000, generator=g)
