@@ -911,6 +911,15 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
 }
 
 }  // namespace
+
+// Index-list splits of the gather-attention: enough 4-warp CTAs for ~8 per SM (random
+// row gathers need many rows in flight), at least 64 index entries per split.
+int gather_splits(int64_t rows, int64_t kb) {
+  const int64_t target = 8LL * num_sms();
+  const int64_t want = std::max<int64_t>(1, (target + std::max<int64_t>(rows, 1) - 1) / std::max<int64_t>(rows, 1));
+  return int(std::max<int64_t>(1, std::min<int64_t>(want, (kb + 63) / 64)));
+}
+
 }  // namespace bd
 
 extern "C" {
@@ -963,10 +972,7 @@ size_t bd_sparse_gather_attn_workspace(const bd_tensor* q, const bd_tensor* idx)
   using namespace bd;
   if (check_tensor(q, "q", 3) || check_tensor(idx, "idx", 3)) return 0;
   const int64_t rows = q->shape[0] * q->shape[1];
-  const int64_t kb = idx->shape[2];
-  const int64_t want = std::max<int64_t>(1, (2LL * num_sms() * 1) / std::max<int64_t>(rows, 1));
-  const int64_t nsplit = std::max<int64_t>(1, std::min<int64_t>(want, (kb + 63) / 64));
-  return partials_bytes(size_t(rows), int(nsplit), int(q->shape[2]));
+  return partials_bytes(size_t(rows), gather_splits(rows, idx->shape[2]), int(q->shape[2]));
 }
 
 int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
@@ -996,8 +1002,7 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
   if ((rc = check_rows_aligned(k, "k")) || (rc = check_rows_aligned(v, "v"))) return rc;
   if (B * Hq == 0) return BD_OK;
   const int64_t rows = B * Hq;
-  const int64_t want = std::max<int64_t>(1, (2LL * num_sms()) / rows);
-  const int nsplit = int(std::max<int64_t>(1, std::min<int64_t>(want, (kb + 63) / 64)));
+  const int nsplit = gather_splits(rows, kb);
   const size_t need = partials_bytes(size_t(rows), nsplit, int(D));
   if (!workspace || workspace_bytes < need) return fail(BD_ERR_WORKSPACE, "need " + std::to_string(need) + " workspace bytes");
   Partials part = carve_partials(workspace, size_t(rows), nsplit, int(D));
