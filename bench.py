@@ -58,6 +58,14 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+def _host_cores():
+    """Cores this process may run on (its CPU affinity), for the host-side baselines."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def _profile_traffic(name):
     """bytes per launch from a committed ncu summary line 'traffic_bytes_per_launch: N'."""
     path = os.path.join(ROOT, "profiles", name)
@@ -209,7 +217,7 @@ def run_reference(args, rank):
     """--impl reference: the CPU restatement of the reference path, timed on host cores."""
     if rank != 0:
         return None
-    cores = os.cpu_count() or 1
+    cores = _host_cores()
     torch.set_num_threads(cores)
     inp = cpu_inputs()
     # size the per-step sample so the whole run stays within ~2 minutes
@@ -380,6 +388,15 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        # host-core work on rank 0 only; the other ranks exit at once (no process group, so
+        # nothing spins on a core the CPU sample needs)
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
     dist = None
     if world > 1:
         import datetime
@@ -387,15 +404,6 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-
-    if args.impl == "reference":
-        line = run_reference(args, rank)
-        if line is not None:
-            print(json.dumps(line), flush=True)
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
 
     from bytes_b200 import kivi as kv
     from bytes_b200 import _ops
@@ -472,7 +480,7 @@ def main():
     if rank == 0 and world == 1:
         if not args.no_extras:
             extra = extras(dev, peak)
-        cores = os.cpu_count() or 1
+        cores = _host_cores()
         torch.set_num_threads(cores)
         inp = cpu_inputs()
         t0 = time.perf_counter()
