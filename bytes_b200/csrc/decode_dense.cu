@@ -76,7 +76,9 @@ __device__ __forceinline__ void store_out(void* base, int dt, int64_t off, float
 template <int D, int NT, bool FP8>
 __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const DenseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  if (p.pdl) griddep_launch_dependents();
+  // a programmatic dependent queued behind this grid (the combine) may start launching;
+  // it waits for this grid before reading anything
+  griddep_launch_dependents();
   constexpr int ELT = FP8 ? 1 : 2;
   constexpr int ROWB = D * ELT;
   constexpr int PITCH = ROWB + 16;
@@ -100,6 +102,27 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
 
   const uint8_t* kbase = p.k + (int64_t(b) * p.k_sb + int64_t(hk) * p.k_sh) * ELT;
   const uint8_t* vbase = p.v + (int64_t(b) * p.v_sb + int64_t(hk) * p.v_sh) * ELT;
+
+  auto load_tile = [&](int tile, int stage) {
+    const int t0 = t_begin + tile * kRows;
+    const uint32_t ks = smem_u32(smem + stage * 2 * TILEB);
+    const uint32_t vs = ks + TILEB;
+    for (int c = threadIdx.x; c < kRows * CHUNKS; c += kWarps * 32) {
+      const int r = c / CHUNKS, cc = c % CHUNKS;
+      const int t = t0 + r;
+      const bool ok = t < t_end;
+      const int tt = ok ? t : t_begin;
+      cp_async16(ks + r * PITCH + cc * 16, kbase + int64_t(tt) * p.k_ss * ELT + cc * 16, ok ? 16 : 0);
+      cp_async16(vs + r * PITCH + cc * 16, vbase + int64_t(tt) * p.v_ss * ELT + cc * 16, ok ? 16 : 0);
+    }
+  };
+
+  // first tiles in flight before the query loads, so the two latencies overlap
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < ntiles) load_tile(s, s);
+    cp_async_commit();
+  }
 
   // ---- query fragments (B operand of QK^T), kept in registers for the whole split
   uint32_t qb[KSTEPS][NT][2];
@@ -147,20 +170,6 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
       }
   }
 
-  auto load_tile = [&](int tile, int stage) {
-    const int t0 = t_begin + tile * kRows;
-    const uint32_t ks = smem_u32(smem + stage * 2 * TILEB);
-    const uint32_t vs = ks + TILEB;
-    for (int c = threadIdx.x; c < kRows * CHUNKS; c += kWarps * 32) {
-      const int r = c / CHUNKS, cc = c % CHUNKS;
-      const int t = t0 + r;
-      const bool ok = t < t_end;
-      const int tt = ok ? t : t_begin;
-      cp_async16(ks + r * PITCH + cc * 16, kbase + int64_t(tt) * p.k_ss * ELT + cc * 16, ok ? 16 : 0);
-      cp_async16(vs + r * PITCH + cc * 16, vbase + int64_t(tt) * p.v_ss * ELT + cc * 16, ok ? 16 : 0);
-    }
-  };
-
   float o[KSTEPS][NT][4];
   float mrow[NT][2], lrow[NT][2];
 #pragma unroll
@@ -175,11 +184,6 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
     lrow[nt][0] = lrow[nt][1] = 0.f;
   }
 
-#pragma unroll
-  for (int s = 0; s < kStages - 1; ++s) {
-    if (s < ntiles) load_tile(s, s);
-    cp_async_commit();
-  }
 
   const int r0 = warp * 16;
   for (int it = 0; it < ntiles; ++it) {
@@ -678,7 +682,7 @@ int bd_decode_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, c
   c.rows = int(rows); c.n = pl.n_splits; c.D = pl.D; c.Hq = p.Hq; c.ms_rows = 1;
   c.out = out->data; c.out_dtype = out->dtype; c.o_sb = out->stride[0]; c.o_sh = out->stride[1];
   c.mode = 0;
-  return launch_combine_kernel(c, st, false);
+  return launch_combine_kernel(c, st, true);
 }
 
 // Variant of bd_decode_attn for callers that cannot hand us a workspace: its split
@@ -740,7 +744,7 @@ int bd_decode_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tens
   c.rows = int(rows); c.n = pl.n_splits; c.D = int(D); c.Hq = int(Hq); c.ms_rows = 1;
   c.mode = 1;
   c.em = static_cast<float*>(m->data); c.el = static_cast<float*>(l->data); c.eo = static_cast<float*>(o->data);
-  return launch_combine_kernel(c, st, false);
+  return launch_combine_kernel(c, st, true);
 }
 
 int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o, const bd_tensor* out,

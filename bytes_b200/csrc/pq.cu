@@ -91,6 +91,7 @@ __device__ __forceinline__ float ld16f(const uint16_t* p, int64_t off, int dt) {
 template <int VK, bool PAGED, bool OUTL, int D>
 __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_launch_dependents();  // the combine queued behind may start launching (it waits for this grid)
   constexpr int KSTEPS = D / 16;
   const PqSmem L = pq_smem(VK, p.M, p.K, OUTL ? p.C : 0, D, p.Mv);
   float* lut_s = reinterpret_cast<float*>(smem);
@@ -699,7 +700,7 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
   Partials part = carve_partials(workspace, size_t(B * Hq), int(splits), int(D));
   p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
   if ((rc = dispatch_pq(p, vk, paged, outl, st))) return rc;
-  return launch_combine(part, int(B), int(Hq), int(D), out_or_scores, st);
+  return launch_combine(part, int(B), int(Hq), int(D), out_or_scores, st, true);
 }
 
 size_t bd_pq_decode_workspace(const bd_tensor* lut, const bd_tensor* k_idx, const bd_tensor* v,

@@ -561,6 +561,7 @@ struct GatherParams {
 
 template <int D, bool FP8>
 __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) {
+  griddep_launch_dependents();  // the combine queued behind may start launching (it waits for this grid)
   constexpr int CPL = D / 8;  // channels per lane (8 lanes per row)
   constexpr int ELT = FP8 ? 1 : 2;
   __shared__ float red_m[16], red_l[16];
@@ -1030,7 +1031,7 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
     else gather_attn_kernel<32, false><<<grid, 128, 0, st>>>(p);
   }
   if ((rc = cuda_check(cudaGetLastError(), "gather_attn_kernel launch"))) return rc;
-  return launch_combine(part, int(B), int(Hq), int(D), out, st);
+  return launch_combine(part, int(B), int(Hq), int(D), out, st, true);
 }
 
 int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, const bd_tensor* kmax,
