@@ -174,6 +174,19 @@ def kivi_pack(x, group_size, bits):
     return code, scale, mn
 
 
+def kivi_append(k_new, v_new, bits, group_size, token_offset, Kq, K_scale, K_mn, Vq, V_scale, V_mn):
+    """Quantize whole 32-token groups of k_new/v_new [B,Hk,Tn,D] into the caches in place."""
+    N.require_cuda(k_new, v_new, Kq, K_scale, K_mn, Vq, V_scale, V_mn)
+    k_new, v_new = inner_contig(k_new), inner_contig(v_new)
+    if v_new.dtype != k_new.dtype:
+        v_new = v_new.to(k_new.dtype)
+    ds = [N.desc(t) for t in (k_new, v_new, Kq, K_scale, K_mn, Vq, V_scale, V_mn)]
+    rc = _fn("bd_kivi_append", [P, P, I, I, ctypes.c_int64, P, P, P, P, P, P, VP])(
+        ctypes.byref(ds[0]), ctypes.byref(ds[1]), int(bits), int(group_size), int(token_offset),
+        *[ctypes.byref(d) for d in ds[2:]], N.stream_of(k_new))
+    N.check(rc, "bd_kivi_append")
+
+
 def kivi_gemv(group_size, fA, qB, scales, zeros, bits):
     N.require_cuda(fA, qB, scales, zeros)
     fA = inner_contig(fA.to(torch.float16))
@@ -295,6 +308,16 @@ def quest_page_minmax(k, page):
                                                        ctypes.byref(dmx), N.stream_of(k))
     N.check(rc, "bd_quest_page_minmax")
     return kmin, kmax
+
+
+def quest_page_minmax_into(k, page, kmin, kmax):
+    """Page min/max of k [B,H,S,D] written into the (possibly strided) views kmin/kmax."""
+    N.require_cuda(k, kmin, kmax)
+    k = inner_contig(k)
+    dk, dmn, dmx = N.desc(k), N.desc(kmin), N.desc(kmax)
+    rc = _fn("bd_quest_page_minmax", [P, I, P, P, VP])(ctypes.byref(dk), int(page), ctypes.byref(dmn),
+                                                       ctypes.byref(dmx), N.stream_of(k))
+    N.check(rc, "bd_quest_page_minmax")
 
 
 def quest_page_bounds(q3, kmin, kmax, scaling, force_from_page=None):

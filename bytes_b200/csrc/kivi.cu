@@ -666,6 +666,101 @@ __global__ void kivi_pack_kernel(const T* __restrict__ x, int nlead, int64_t l0,
   mn[row * gpr + grp] = from_f32<T>(lo);
 }
 
+// ---------------------------------------------------------------- KIVI cache append
+// Quantizes whole 32-token groups of new keys/values into existing packed caches at a
+// token offset, with the packer's arithmetic (fp32 min/max, scale = max(max-min,1e-8) /
+// (2^bits-1), round-half-even, clamp): the caches then hold exactly what packing the whole
+// sequence at once would give. Keys are quantized per channel over the group's tokens
+// (one thread per (b, hk, channel, group); a warp reads 32 consecutive channels of each
+// token), values per token over 32-channel groups (one thread per (b, hk, token, group)).
+struct AppendParams {
+  const void* k; int64_t k_sb, k_sh, k_st;  // [B,Hk,Tn,D], channels contiguous
+  const void* v; int64_t v_sb, v_sh, v_st;
+  int in_dtype;
+  int B, Hk, Tn, D;
+  int64_t t0;  // token offset of the first new token (multiple of 32)
+  uint32_t* kq; int64_t kq_sb, kq_sh, kq_sc;  // [B,Hk,D,cap/fpi]
+  __half* ks; int64_t ks_sb, ks_sh, ks_sc;    // [B,Hk,D,cap/32]
+  __half* km; int64_t km_sb, km_sh, km_sc;
+  uint32_t* vq; int64_t vq_sb, vq_sh, vq_st;  // [B,Hk,cap,D/fpi]
+  __half* vs; int64_t vs_sb, vs_sh, vs_st;    // [B,Hk,cap,D/32]
+  __half* vm; int64_t vm_sb, vm_sh, vm_st;
+};
+
+__device__ __forceinline__ float ld_in(const void* base, int dt, int64_t off) {
+  switch (dt) {
+    case BD_F16: return __half2float(reinterpret_cast<const __half*>(base)[off]);
+    case BD_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[off]);
+    default: return reinterpret_cast<const float*>(base)[off];
+  }
+}
+
+// quantize 32 values, return the packed words, scale and minimum
+template <int BITS>
+__device__ __forceinline__ void quant32(const float* v, uint32_t* words, float* sc_out, float* lo_out) {
+  float lo = v[0], hi = v[0];
+#pragma unroll
+  for (int e = 1; e < 32; ++e) { lo = fminf(lo, v[e]); hi = fmaxf(hi, v[e]); }
+  constexpr int LV = (1 << BITS) - 1;
+  constexpr int FPI = 32 / BITS;
+  const float sc = __fdiv_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), float(LV));
+#pragma unroll
+  for (int w = 0; w < 32 / FPI; ++w) words[w] = 0u;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    float qv = rintf(__fdiv_rn(__fsub_rn(v[e], lo), sc));
+    qv = fminf(fmaxf(qv, 0.f), float(LV));
+    words[e / FPI] |= uint32_t(qv) << ((e % FPI) * BITS);
+  }
+  *sc_out = sc;
+  *lo_out = lo;
+}
+
+template <int BITS>
+__global__ void kivi_append_kernel(const AppendParams p) {
+  constexpr int FPI = 32 / BITS;
+  const int ngr = p.Tn / 32;
+  const int64_t nk = int64_t(p.B) * p.Hk * ngr * p.D;  // key threads: (b, hk, group, channel)
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  float v[32];
+  uint32_t words[32 / FPI];
+  float sc, lo;
+  if (gid < nk) {
+    const int c = int(gid % p.D);
+    int64_t r = gid / p.D;
+    const int grp = int(r % ngr); r /= ngr;
+    const int hk = int(r % p.Hk), b = int(r / p.Hk);
+    const int64_t base = int64_t(b) * p.k_sb + int64_t(hk) * p.k_sh + int64_t(grp) * 32 * p.k_st + c;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = ld_in(p.k, p.in_dtype, base + int64_t(e) * p.k_st);
+    quant32<BITS>(v, words, &sc, &lo);
+    const int64_t g0 = p.t0 / 32 + grp;  // group index in the cache
+    uint32_t* kq = p.kq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh + int64_t(c) * p.kq_sc + g0 * (32 / FPI);
+#pragma unroll
+    for (int w = 0; w < 32 / FPI; ++w) kq[w] = words[w];
+    p.ks[int64_t(b) * p.ks_sb + int64_t(hk) * p.ks_sh + int64_t(c) * p.ks_sc + g0] = __float2half_rn(sc);
+    p.km[int64_t(b) * p.km_sb + int64_t(hk) * p.km_sh + int64_t(c) * p.km_sc + g0] = __float2half_rn(lo);
+    return;
+  }
+  const int64_t vid = gid - nk;  // value threads: (b, hk, token, channel group)
+  const int cg = p.D / 32;
+  if (vid >= int64_t(p.B) * p.Hk * p.Tn * cg) return;
+  const int grp = int(vid % cg);
+  int64_t r = vid / cg;
+  const int t = int(r % p.Tn); r /= p.Tn;
+  const int hk = int(r % p.Hk), b = int(r / p.Hk);
+  const int64_t base = int64_t(b) * p.v_sb + int64_t(hk) * p.v_sh + int64_t(t) * p.v_st + grp * 32;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = ld_in(p.v, p.in_dtype, base + e);
+  quant32<BITS>(v, words, &sc, &lo);
+  const int64_t tc = p.t0 + t;  // token index in the cache
+  uint32_t* vq = p.vq + int64_t(b) * p.vq_sb + int64_t(hk) * p.vq_sh + tc * p.vq_st + grp * (32 / FPI);
+#pragma unroll
+  for (int w = 0; w < 32 / FPI; ++w) vq[w] = words[w];
+  p.vs[int64_t(b) * p.vs_sb + int64_t(hk) * p.vs_sh + tc * p.vs_st + grp] = __float2half_rn(sc);
+  p.vm[int64_t(b) * p.vm_sb + int64_t(hk) * p.vm_sh + tc * p.vm_st + grp] = __float2half_rn(lo);
+}
+
 // ---------------------------------------------------------------- KIVI GEMV
 // out[b,hq,m,n] = sum_k fA[b,hq,m,k] * (code(qB[b,hk,k,n]) * sc[b,hk,k,n/gs] + zr[b,hk,k,n/gs])
 struct GemvParams {
@@ -841,6 +936,61 @@ int bd_kivi_pack_last_dim(const bd_tensor* x, int group_size, int bits, const bd
   else { BD_PACK(float, BD_F32) }
 #undef BD_PACK
   return cuda_check(cudaGetLastError(), "kivi_pack_kernel launch");
+}
+
+int bd_kivi_append(const bd_tensor* k_new, const bd_tensor* v_new, int bits, int group_size, int64_t token_offset,
+                   const bd_tensor* Kq, const bd_tensor* K_scale, const bd_tensor* K_mn, const bd_tensor* Vq,
+                   const bd_tensor* V_scale, const bd_tensor* V_mn, bd_stream_t stream) {
+  using namespace bd;
+  int rc;
+  if (bits != 2 && bits != 4) return fail(BD_ERR_VALUE, "bits must be 2 or 4");
+  if (group_size != 32) return fail(BD_ERR_UNSUPPORTED, "group_size must be 32");
+  if ((rc = check_tensor(k_new, "k_new", 4)) || (rc = check_tensor(v_new, "v_new", 4, k_new->dtype)) ||
+      (rc = check_tensor(Kq, "Kq", 4, BD_I32)) || (rc = check_tensor(K_scale, "K_scale", 4, BD_F16)) ||
+      (rc = check_tensor(K_mn, "K_mn", 4, BD_F16)) || (rc = check_tensor(Vq, "Vq", 4, BD_I32)) ||
+      (rc = check_tensor(V_scale, "V_scale", 4, BD_F16)) || (rc = check_tensor(V_mn, "V_mn", 4, BD_F16)))
+    return rc;
+  if (k_new->dtype != BD_F16 && k_new->dtype != BD_BF16 && k_new->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "k_new/v_new must be f16, bf16 or f32");
+  const int64_t B = k_new->shape[0], Hk = k_new->shape[1], Tn = k_new->shape[2], D = k_new->shape[3];
+  const int fpi = 32 / bits;
+  for (int i = 0; i < 4; ++i)
+    if (v_new->shape[i] != k_new->shape[i]) return fail(BD_ERR_SHAPE, "k_new and v_new shapes differ");
+  if (Tn % 32 || D % 32) return fail(BD_ERR_SHAPE, "new tokens and head_dim must be multiples of 32");
+  if (token_offset < 0 || token_offset % 32) return fail(BD_ERR_VALUE, "token_offset must be a non-negative multiple of 32");
+  if ((Tn > 1 && (k_new->stride[3] != 1 || v_new->stride[3] != 1)))
+    return fail(BD_ERR_STRIDE, "k_new/v_new channels must be contiguous");
+  const int64_t end = token_offset + Tn;
+  if (Kq->shape[0] != B || Kq->shape[1] != Hk || Kq->shape[2] != D || Kq->shape[3] * fpi < end)
+    return fail(BD_ERR_SHAPE, "Kq must be [B,Hk,D,>= (offset+new)/fpi]");
+  for (const bd_tensor* t : {K_scale, K_mn})
+    if (t->shape[0] != B || t->shape[1] != Hk || t->shape[2] != D || t->shape[3] * 32 < end)
+      return fail(BD_ERR_SHAPE, "K_scale/K_mn must be [B,Hk,D,>= (offset+new)/32]");
+  if (Vq->shape[0] != B || Vq->shape[1] != Hk || Vq->shape[2] < end || Vq->shape[3] * fpi != D)
+    return fail(BD_ERR_SHAPE, "Vq must be [B,Hk,>= offset+new,D/fpi]");
+  for (const bd_tensor* t : {V_scale, V_mn})
+    if (t->shape[0] != B || t->shape[1] != Hk || t->shape[2] < end || t->shape[3] * 32 != D)
+      return fail(BD_ERR_SHAPE, "V_scale/V_mn must be [B,Hk,>= offset+new,D/32]");
+  for (const bd_tensor* t : {Kq, K_scale, K_mn, Vq, V_scale, V_mn})
+    if (t->shape[3] > 1 && t->stride[3] != 1) return fail(BD_ERR_STRIDE, "cache rows must be contiguous");
+  if (B * Hk * Tn == 0) return BD_OK;
+  AppendParams p{};
+  p.k = k_new->data; p.k_sb = k_new->stride[0]; p.k_sh = k_new->stride[1]; p.k_st = k_new->stride[2];
+  p.v = v_new->data; p.v_sb = v_new->stride[0]; p.v_sh = v_new->stride[1]; p.v_st = v_new->stride[2];
+  p.in_dtype = k_new->dtype;
+  p.B = int(B); p.Hk = int(Hk); p.Tn = int(Tn); p.D = int(D); p.t0 = token_offset;
+  p.kq = static_cast<uint32_t*>(Kq->data); p.kq_sb = Kq->stride[0]; p.kq_sh = Kq->stride[1]; p.kq_sc = Kq->stride[2];
+  p.ks = static_cast<__half*>(K_scale->data); p.ks_sb = K_scale->stride[0]; p.ks_sh = K_scale->stride[1]; p.ks_sc = K_scale->stride[2];
+  p.km = static_cast<__half*>(K_mn->data); p.km_sb = K_mn->stride[0]; p.km_sh = K_mn->stride[1]; p.km_sc = K_mn->stride[2];
+  p.vq = static_cast<uint32_t*>(Vq->data); p.vq_sb = Vq->stride[0]; p.vq_sh = Vq->stride[1]; p.vq_st = Vq->stride[2];
+  p.vs = static_cast<__half*>(V_scale->data); p.vs_sb = V_scale->stride[0]; p.vs_sh = V_scale->stride[1]; p.vs_st = V_scale->stride[2];
+  p.vm = static_cast<__half*>(V_mn->data); p.vm_sb = V_mn->stride[0]; p.vm_sh = V_mn->stride[1]; p.vm_st = V_mn->stride[2];
+  const int64_t total = B * Hk * (Tn / 32) * D + B * Hk * Tn * (D / 32);
+  const unsigned blocks = unsigned((total + 127) / 128);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (bits == 2) kivi_append_kernel<2><<<blocks, 128, 0, st>>>(p);
+  else kivi_append_kernel<4><<<blocks, 128, 0, st>>>(p);
+  return cuda_check(cudaGetLastError(), "kivi_append_kernel launch");
 }
 
 int bd_kivi_gemv_outer(int group_size, const bd_tensor* fA, const bd_tensor* qB, const bd_tensor* scales,

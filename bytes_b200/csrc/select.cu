@@ -682,7 +682,8 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
 // ------------------------------------------------------------------ Quest
 template <typename T>
 __global__ void quest_minmax_kernel(const T* __restrict__ k, int64_t s_b, int64_t s_h, int64_t s_s, int Hk, int S,
-                                    int D, int page, int np, T* __restrict__ kmin, T* __restrict__ kmax) {
+                                    int D, int page, int np, T* __restrict__ kmin, T* __restrict__ kmax,
+                                    int64_t m_sb, int64_t m_sh, int64_t m_sp) {
   const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, h, page, d)
   const int64_t total = int64_t(gridDim.y) * Hk * np * D;
   (void)total;
@@ -699,7 +700,7 @@ __global__ void quest_minmax_kernel(const T* __restrict__ k, int64_t s_b, int64_
     lo = fminf(lo, x);
     hi = fmaxf(hi, x);
   }
-  const int64_t o = ((int64_t(b) * Hk + h) * np + pg) * D + d;
+  const int64_t o = int64_t(b) * m_sb + int64_t(h) * m_sh + int64_t(pg) * m_sp + d;
   kmin[o] = from_f32<T>(lo);
   kmax[o] = from_f32<T>(hi);
 }
@@ -1045,11 +1046,12 @@ int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, co
   if (k->dtype != BD_BF16 && k->dtype != BD_F16 && k->dtype != BD_F32) return fail(BD_ERR_DTYPE, "k must be bf16/f16/f32");
   const int64_t B = k->shape[0], H = k->shape[1], S = k->shape[2], D = k->shape[3];
   const int64_t np = (S + page - 1) / page;
+  for (int i = 0; i < 4; ++i)
+    if (kmin->stride[i] != kmax->stride[i]) return fail(BD_ERR_STRIDE, "kmin and kmax must share a layout");
   for (const bd_tensor* t : {kmin, kmax}) {
     if (t->shape[0] != B || t->shape[1] != H || t->shape[2] != np || t->shape[3] != D)
       return fail(BD_ERR_SHAPE, "kmin/kmax must be [B,H,ceil(S/page),D]");
-    if (t->stride[3] != 1 || t->stride[2] != D || t->stride[1] != np * D || (B > 1 && t->stride[0] != H * np * D))
-      return fail(BD_ERR_STRIDE, "kmin/kmax must be contiguous");
+    if (D > 1 && t->stride[3] != 1) return fail(BD_ERR_STRIDE, "kmin/kmax channels must be contiguous");
   }
   if (B * H * np * D == 0) return BD_OK;
   const int64_t per_b = H * np * D;
@@ -1058,15 +1060,15 @@ int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, co
   if (k->dtype == BD_BF16)
     quest_minmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(k->data), k->stride[0],
         k->stride[1], k->stride[2], int(H), int(S), int(D), page, int(np), static_cast<__nv_bfloat16*>(kmin->data),
-        static_cast<__nv_bfloat16*>(kmax->data));
+        static_cast<__nv_bfloat16*>(kmax->data), kmin->stride[0], kmin->stride[1], kmin->stride[2]);
   else if (k->dtype == BD_F16)
     quest_minmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(k->data), k->stride[0], k->stride[1],
         k->stride[2], int(H), int(S), int(D), page, int(np), static_cast<__half*>(kmin->data),
-        static_cast<__half*>(kmax->data));
+        static_cast<__half*>(kmax->data), kmin->stride[0], kmin->stride[1], kmin->stride[2]);
   else
     quest_minmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(k->data), k->stride[0], k->stride[1],
         k->stride[2], int(H), int(S), int(D), page, int(np), static_cast<float*>(kmin->data),
-        static_cast<float*>(kmax->data));
+        static_cast<float*>(kmax->data), kmin->stride[0], kmin->stride[1], kmin->stride[2]);
   return cuda_check(cudaGetLastError(), "quest_minmax_kernel launch");
 }
 

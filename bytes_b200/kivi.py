@@ -37,6 +37,22 @@ def kivi_decode_attn(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_resi
     return out.unsqueeze(2)
 
 
+def kivi_append(k_new, v_new, bits, token_offset, Kq, K_scale, K_mn, Vq, V_scale, V_mn, group_size=32):
+    """Streaming cache write: quantize whole 32-token groups of new keys and values into
+    the packed caches in place, starting at token ``token_offset`` (a multiple of 32).
+
+    k_new, v_new [B,H_k,Tn,D] (Tn a multiple of 32); Kq int32 [B,H_k,D,cap*bits/32],
+    K_scale/K_mn f16 [B,H_k,D,cap/32], Vq int32 [B,H_k,cap,D*bits/32], V_scale/V_mn f16
+    [B,H_k,cap,D/32]. After any sequence of appends the caches hold exactly what
+    ``triton_quantize_and_pack_along_last_dim`` of the whole sequence gives (keys passed
+    transposed, as benchmarks/kivi_latency.py:123,127 does), so a serving loop flushes
+    the oldest 32 tokens of the bf16 residual window once it exceeds R and keeps decoding
+    with kivi_decode_attn. The reference has no incremental form; it packs whole tensors
+    and keeps the newest R tokens exact (KIVIQuantizer, src/quantization.py:468-501).
+    """
+    _ops.kivi_append(k_new, v_new, bits, group_size, token_offset, Kq, K_scale, K_mn, Vq, V_scale, V_mn)
+
+
 def triton_quantize_and_pack_along_last_dim(data, group_size, bit):
     """Group-wise asymmetric quantize + pack along the last dim (KIVI packer contract).
 

@@ -74,6 +74,22 @@ def quest_page_metadata(k, page):
     return _ops.quest_page_minmax(k, page)
 
 
+def quest_page_metadata_update(k, kmin, kmax, page, first_page, last_page):
+    """Refresh pages [first_page, last_page) of an existing metadata cache in place.
+
+    k [B,H_k,S,D] is the key cache holding S valid tokens; kmin/kmax [B,H_k,>=last_page,D].
+    A serving loop calls this for the page the new token fell into (its min/max grows
+    until the page fills) -- the cache-side maintenance the reference recomputes from
+    scratch on every call (benchmarks/sparse_attention.py:334-341).
+    """
+    S = k.shape[2]
+    t0, t1 = first_page * page, min(S, last_page * page)
+    if first_page < 0 or last_page * page - page >= S or t0 >= t1:
+        raise ValueError("page range must cover valid tokens")
+    _ops.quest_page_minmax_into(k[:, :, t0:t1], page, kmin[:, :, first_page:last_page],
+                                kmax[:, :, first_page:last_page])
+
+
 def quest_select_decode(q, kmin, kmax, S, kb, page, scaling):
     """Quest selection from per-KV-head metadata: q [B,H_q,1,D] -> idx [B,H_q,npick*page]."""
     return _ops.quest_select(q[:, :, 0, :], kmin, kmax, S, kb, page, scaling)

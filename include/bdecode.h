@@ -4,9 +4,10 @@
  * Every entry point takes plain device pointers wrapped in `bd_tensor`
  * descriptors (data pointer, dtype code, shape and element strides — the same
  * information a DLPack DLTensor carries), a few scalars and a CUDA stream. No
- * entry point allocates device memory: scratch space comes from the caller as
- * (workspace, workspace_bytes), sized by the matching *_workspace() query, so
- * every launch is CUDA-graph capturable. Nothing synchronises the stream.
+ * entry point allocates device memory. Scratch space comes from the caller as
+ * (workspace, workspace_bytes), sized by the matching *_workspace() query, so those
+ * launches can be captured in CUDA graphs; bd_decode_attn_noalloc (below) instead
+ * uses a fixed array inside the library. Nothing synchronises the stream.
  *
  * Return value: 0 (BD_OK) or a BD_ERR_* code; bd_last_error() gives the
  * message for the calling thread's last failure. Inputs are validated on the
@@ -137,6 +138,23 @@ int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd
 int bd_kivi_pack_last_dim(const bd_tensor* x, int group_size, int bits, const bd_tensor* code,
                           const bd_tensor* scale, const bd_tensor* mn, bd_stream_t stream);
 
+/* Streaming KIVI cache write: quantizes whole 32-token groups of new keys and values
+ * into existing packed caches, starting at token `token_offset` (a multiple of 32).
+ * Keys go per channel over each group's tokens, values per token over 32-channel
+ * groups, with bd_kivi_pack_last_dim's arithmetic, so after any sequence of appends the
+ * caches equal packing the whole sequence at once. k_new, v_new [B,Hk,Tn,D]
+ * f16/bf16/f32 (Tn, D multiples of 32, channels contiguous); Kq int32 [B,Hk,D,>=end/fpi],
+ * K_scale/K_mn f16 [B,Hk,D,>=end/32], Vq int32 [B,Hk,>=end,D/fpi], V_scale/V_mn f16
+ * [B,Hk,>=end,D/32] with end = token_offset + Tn (fpi = 32/bits); cache rows contiguous,
+ * other strides free. This is the step before the decode path: a serving loop flushes
+ * the oldest 32 tokens of the bf16 residual window once it exceeds R.
+ * ref: the reference packs whole tensors (external KIVI packer, benchmarks/kivi_latency.py:123)
+ *      and keeps the newest R tokens exact (KIVIQuantizer, src/quantization.py:468-501);
+ *      it has no incremental append. */
+int bd_kivi_append(const bd_tensor* k_new, const bd_tensor* v_new, int bits, int group_size, int64_t token_offset,
+                   const bd_tensor* Kq, const bd_tensor* K_scale, const bd_tensor* K_mn, const bd_tensor* Vq,
+                   const bd_tensor* V_scale, const bd_tensor* V_mn, bd_stream_t stream);
+
 /* out[b,hq,m,n] = sum_k fA[b,hq,m,k] * (code(qB)[b,hq/G,k,n]*scales + zeros), f16.
  * fA f16 [B,Hq,M,K]; qB int32 [B,Hk,K,N*bits/32]; scales,zeros f16
  * [B,Hk,K,N/group_size]; out f16 [B,Hq,M,N].
@@ -186,7 +204,9 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
 
 /* Quest page metadata: elementwise min / max of each page of `page` tokens
  * (a ragged last page covers the real tokens only). k [B,H,S,D]; kmin, kmax
- * [B,H,ceil(S/page),D] in k's dtype.
+ * [B,H,ceil(S/page),D] in k's dtype, channels contiguous, other strides free -- so a
+ * serving loop refreshes pages [p0, p1) of a metadata cache by passing the views
+ * k[:, :, p0*page : min(S, p1*page)] and kmin/kmax[:, :, p0:p1].
  * ref: _quest_select  benchmarks/sparse_attention.py:334-341 */
 int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, const bd_tensor* kmax,
                          bd_stream_t stream);

@@ -90,6 +90,28 @@ def test_kivi_rejects_bad_bits_on_host():
     assert rc == 7
 
 
+def test_kivi_append_rejects_bad_requests_on_host():
+    lib = N.lib()
+    f = lib.bd_kivi_append
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int64] + [ctypes.c_void_p] * 7
+    kn = _fake((1, 1, 32, 128), N.BD_F16)
+    Kq = _fake((1, 1, 128, 8), N.BD_I32)    # capacity 128 tokens at 2 bits
+    Ks = _fake((1, 1, 128, 4), N.BD_F16)
+    Vq = _fake((1, 1, 128, 8), N.BD_I32)
+    Vs = _fake((1, 1, 128, 4), N.BD_F16)
+
+    def call(k, bits, off, kq=Kq):
+        return f(ctypes.addressof(k), ctypes.addressof(k), bits, 32, off, ctypes.addressof(kq), ctypes.addressof(Ks),
+                 ctypes.addressof(Ks), ctypes.addressof(Vq), ctypes.addressof(Vs), ctypes.addressof(Vs), None)
+
+    assert call(kn, 3, 0) == 9                                   # bits
+    assert call(kn, 2, 16) == 9                                  # offset inside a group
+    assert call(_fake((1, 1, 48, 128), N.BD_F16), 2, 0) == 3     # partial group
+    assert call(kn, 2, 128) == 3                                 # past the key capacity
+    assert call(_fake((1, 1, 32, 128), N.BD_I8), 2, 0) == 2      # dtype
+
+
 def test_python_layer_refuses_cpu_tensors():
     from bytes_b200 import attention_kernels as ak
     q = torch.randn(1, 4, 1, 128).bfloat16()
