@@ -39,8 +39,13 @@
 #include "common.cuh"
 #include "decode_shared.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
+#include <cstring>
+#include <mutex>
 
 namespace bd {
 namespace {
@@ -53,11 +58,14 @@ constexpr float kLn2K = 0.6931471805599453f;
 constexpr int kRedPitch = 132;  // floats per head row of the epilogue buffer (padded: no bank conflicts)
 constexpr int kKChunk = 4;      // tiles per key scale/min chunk
 
-template <int BITS>
+// Shared-memory layout. TMA (2-bit only): the key tile lands unpadded with the 32-byte
+// swizzle (16-byte chunk c of row r at chunk c ^ ((r >> 2) & 1)), which keeps the
+// per-lane key reads conflict-free; the cp.async form pads rows to 48 bytes instead.
+template <int BITS, bool TMA = false>
 struct KL {
   static constexpr int FPI = 32 / BITS;
   static constexpr int KQ_WORDS = kTile / FPI;          // words per channel per tile
-  static constexpr int KQ_PITCH = BITS == 2 ? 48 : 80;  // smem bytes per channel row (padded)
+  static constexpr int KQ_PITCH = TMA ? 32 : (BITS == 2 ? 48 : 80);  // smem bytes per channel row
   static constexpr int VQ_WORDS = 128 / FPI;            // words per token (D = 128)
   static constexpr int VQ_PITCH = BITS == 2 ? 32 : 80;
   static constexpr int KQ_BYTES = 128 * KQ_PITCH;
@@ -75,7 +83,10 @@ struct KL {
   static constexpr int OFF_KC = kStagesK * STAGE;
   static constexpr int T_BYTES = 2 * 4 * 128 * 2;  // transposed key scale/min [2][4 groups][128 ch] f16
   static constexpr int OFF_T = OFF_KC + 2 * KC_BYTES;
-  static constexpr int SMEM = OFF_T + T_BYTES;
+  static constexpr int OFF_BAR = OFF_T + T_BYTES;  // TMA: one mbarrier per stage
+  static constexpr int SMEM = OFF_BAR + kStagesK * 8;
+  static constexpr uint32_t TMA_BYTES = 128 * 32 + kTile * 32 + 2 * kTile * 8;  // K, V codes, V scale, V min
+  static_assert(!TMA || (BITS == 2 && STAGE % 1024 == 0), "TMA stages hold the 2-bit tile at 1024-byte alignment");
 };
 
 struct KiviParams {
@@ -106,11 +117,29 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 __device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-template <int BITS>
-__global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const KiviParams p) {
-  using L = KL<BITS>;
-  extern __shared__ __align__(128) uint8_t smem[];
+// TMA waits that ran past their iteration limit (the kernel then carries on with
+// whatever landed; a non-zero count means a result of that launch is wrong)
+__device__ unsigned int g_kivi_tma_timeouts = 0;
+
+template <int BITS, bool TMA>
+__global__ void __launch_bounds__(kWarpsK * 32, 4)
+    kivi_decode_kernel(const KiviParams p, const __grid_constant__ CUtensorMap tm_kq,
+                       const __grid_constant__ CUtensorMap tm_vq, const __grid_constant__ CUtensorMap tm_vs,
+                       const __grid_constant__ CUtensorMap tm_vm) {
+  using L = KL<BITS, TMA>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // TMA destinations must sit on the swizzle atom: align the working base by hand (the
+  // launch adds 1 KB); every shared-memory access below goes through `smem`
+  uint8_t* smem = TMA ? smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : smem_raw;
   uint8_t* tsm = smem + L::OFF_T;  // transposed key scale / min of the current tile
+  const uint32_t bar0 = smem_u32(smem + L::OFF_BAR);
+  if (TMA) {
+    if (threadIdx.x == 0) {
+      for (int s = 0; s < kStagesK; ++s) mbar_init(bar0 + 8 * s, 1);
+      mbar_fence_init();
+    }
+    __syncthreads();
+  }
   // the residual-window kernel queued behind this one reads nothing this grid writes
   griddep_launch_dependents();
   const int split = blockIdx.x;
@@ -225,7 +254,17 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
         cp_async8(dst + 128 * L::KC_ROW + i * 32 * L::KC_ROW, gv ? km_src + i * km_pass + tile * 4 : km_base, gv * 2);
       }
     }
-    if (t0 + kTile <= t_end) {
+    if (TMA) {
+      // one thread moves the whole tile; rows past the sequence end arrive as zeros
+      if (threadIdx.x == 0) {
+        const uint32_t bar = bar0 + 8 * stage;
+        mbar_arrive_expect_tx(bar, L::TMA_BYTES);
+        tma_load_4d(sbase, &tm_kq, t0 / L::FPI, 0, hk, b, bar);
+        tma_load_4d(sbase + L::OFF_VQ, &tm_vq, 0, t0, hk, b, bar);
+        tma_load_4d(sbase + L::OFF_VS, &tm_vs, 0, t0 / 2, hk, b, bar);
+        tma_load_4d(sbase + L::OFF_VM, &tm_vm, 0, t0 / 2, hk, b, bar);
+      }
+    } else if (t0 + kTile <= t_end) {
 #pragma unroll
       for (int i = 0; i < NCH; ++i)
         cp_async16(sbase + k_dst + i * (128 / NCH) * L::KQ_PITCH, k_src + i * k_pass + tile * L::KQ_WORDS, 16);
@@ -267,7 +306,9 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
   }
 
   for (int it = 0; it < ntiles; ++it) {
-    cp_async_wait<kStagesK - 2>();
+    cp_async_wait<kStagesK - 2>();  // key scale/min chunks (and, without TMA, the tile)
+    if (TMA && !mbar_wait(bar0 + 8 * (it % kStagesK), (it / kStagesK) & 1) && threadIdx.x == 0)
+      atomicAdd(&g_kivi_tma_timeouts, 1u);
     __syncthreads();
     {
       const int nxt = it + kStagesK - 1;
@@ -316,7 +357,9 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
     float s[2][4];
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) s[rb][0] = s[rb][1] = s[rb][2] = s[rb][3] = 0.f;
-    const uint8_t* kst = st + (2 * tq) * L::KQ_PITCH + warp * (BITS == 2 ? 8 : 16);
+    // rows 2tq + {0, 1, 8, 9} (+16j) share the 32-byte swizzle bit (row >> 2) & 1 = tq >> 1
+    const uint8_t* kst = st + (2 * tq) * L::KQ_PITCH +
+                         (TMA ? ((((warp >> 1) ^ (tq >> 1)) << 4) + (warp & 1) * 8) : warp * (BITS == 2 ? 8 : 16));
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       // channels c0, c0+1 (k = 2tq, 2tq+1) and c0+8, c0+9 (k = 2tq+8, 2tq+9)
@@ -542,11 +585,106 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4) kivi_decode_kernel(const Kivi
   }
 }
 
-template <int BITS>
-int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
-  using L = KL<BITS>;
-  const size_t smem = std::max<size_t>(L::SMEM, (2 * 4 * 8 + 4 * 8 * kRedPitch) * sizeof(float));
-  auto kern = kivi_decode_kernel<BITS>;
+// ---- TMA tensor maps (host). Encoded through the driver entry point fetched from the
+// runtime (no link against libcuda) and cached per cache-tensor geometry, so a decode loop
+// over the same caches encodes once.
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn tensor_map_encoder() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(f);
+  });
+  return fn;
+}
+
+bool encode4d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, const cuuint64_t dims[4],
+              const cuuint64_t strides[3], const cuuint32_t box[4], CUtensorMapSwizzle sw) {
+  const EncodeFn enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(m, dt, 4, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct TmaKey {
+  const void* kq; const void* vq; const void* vs; const void* vm;
+  int64_t W, Sq, Hk, B, kq_sc, kq_sh, kq_sb, vq_st, vq_sh, vq_sb, vs_sh, vs_sb, vm_sh, vm_sb;
+  int dev;
+};
+struct TmaEntry {
+  TmaKey key;
+  CUtensorMap m[4];
+  bool used;
+};
+std::mutex g_tma_mu;
+TmaEntry g_tma[16];
+int g_tma_next = 0;
+
+// The 2-bit TMA form needs 16-byte aligned bases and strides (bytes) and dense 8-byte rows
+// of value scales/minima (read as 16-byte rows of two tokens). W = words per key row.
+bool kivi_tma_maps(const KiviParams& kp, int64_t W, CUtensorMap out[4]) {
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  // bytes stride of a dim, or a harmless 16-byte multiple when the dim has one entry
+  auto st = [](int64_t elems, int esz, int64_t size, int64_t fallback) -> int64_t {
+    return size > 1 ? elems * esz : fallback;
+  };
+  const int64_t Hk = kp.Hk, B = kp.B, Sq = kp.Sq;
+  const int64_t s_kc = kp.kq_sc * 4, s_kh = st(kp.kq_sh, 4, Hk, s_kc * 128), s_kb = st(kp.kq_sb, 4, B, s_kh * Hk);
+  const int64_t s_vt = kp.vq_st * 4, s_vh = st(kp.vq_sh, 4, Hk, s_vt * Sq), s_vb = st(kp.vq_sb, 4, B, s_vh * Hk);
+  const int64_t s_sh = st(kp.vs_sh, 2, Hk, Sq * 8), s_sb = st(kp.vs_sb, 2, B, s_sh * Hk);
+  const int64_t s_mh = st(kp.vm_sh, 2, Hk, Sq * 8), s_mb = st(kp.vm_sb, 2, B, s_mh * Hk);
+  for (int64_t x : {s_kc, s_kh, s_kb, s_vt, s_vh, s_vb, s_sh, s_sb, s_mh, s_mb})
+    if (x <= 0 || x % 16 || x >= (int64_t(1) << 40)) return false;
+  if (!a16(kp.kq) || !a16(kp.vq) || !a16(kp.vs) || !a16(kp.vm) || kp.vs_st != 4 || kp.vm_st != 4 || (Sq & 1))
+    return false;
+  TmaKey key{};
+  key.kq = kp.kq; key.vq = kp.vq; key.vs = kp.vs; key.vm = kp.vm;
+  key.W = W; key.Sq = Sq; key.Hk = Hk; key.B = B;
+  key.kq_sc = s_kc; key.kq_sh = s_kh; key.kq_sb = s_kb; key.vq_st = s_vt; key.vq_sh = s_vh; key.vq_sb = s_vb;
+  key.vs_sh = s_sh; key.vs_sb = s_sb; key.vm_sh = s_mh; key.vm_sb = s_mb;
+  cudaGetDevice(&key.dev);
+  std::lock_guard<std::mutex> lock(g_tma_mu);
+  for (const TmaEntry& e : g_tma)
+    if (e.used && std::memcmp(&e.key, &key, sizeof key) == 0) {
+      std::memcpy(out, e.m, sizeof e.m);
+      return true;
+    }
+  CUtensorMap m[4];
+  const cuuint64_t dk[4] = {cuuint64_t(W), 128, cuuint64_t(Hk), cuuint64_t(B)};
+  const cuuint64_t sk[3] = {cuuint64_t(s_kc), cuuint64_t(s_kh), cuuint64_t(s_kb)};
+  const cuuint32_t bk[4] = {8, 128, 1, 1};
+  const cuuint64_t dv[4] = {8, cuuint64_t(Sq), cuuint64_t(Hk), cuuint64_t(B)};
+  const cuuint64_t sv[3] = {cuuint64_t(s_vt), cuuint64_t(s_vh), cuuint64_t(s_vb)};
+  const cuuint32_t bv[4] = {8, uint32_t(kTile), 1, 1};
+  const cuuint64_t ds[4] = {8, cuuint64_t(Sq / 2), cuuint64_t(Hk), cuuint64_t(B)};
+  const cuuint64_t ss[3] = {16, cuuint64_t(s_sh), cuuint64_t(s_sb)};
+  const cuuint64_t sm[3] = {16, cuuint64_t(s_mh), cuuint64_t(s_mb)};
+  const cuuint32_t bs[4] = {8, uint32_t(kTile / 2), 1, 1};
+  if (!encode4d(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, kp.kq, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_32B) ||
+      !encode4d(&m[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, kp.vq, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode4d(&m[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kp.vs, ds, ss, bs, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode4d(&m[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kp.vm, ds, sm, bs, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return false;
+  TmaEntry& e = g_tma[g_tma_next];
+  g_tma_next = (g_tma_next + 1) % 16;
+  e.key = key;
+  std::memcpy(e.m, m, sizeof m);
+  e.used = true;
+  std::memcpy(out, m, sizeof m);
+  return true;
+}
+
+template <int BITS, bool TMA>
+int launch_kivi_as(const KiviParams& kp, int n_splits, const CUtensorMap* maps, cudaStream_t st) {
+  using L = KL<BITS, TMA>;
+  const size_t smem = std::max<size_t>(L::SMEM, (2 * 4 * 8 + 4 * 8 * kRedPitch) * sizeof(float)) + (TMA ? 1024 : 0);
+  auto kern = kivi_decode_kernel<BITS, TMA>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -557,8 +695,18 @@ int launch_kivi(const KiviParams& kp, int n_splits, cudaStream_t st) {
     attr[dev & 63] = true;
   }
   dim3 grid(n_splits, kp.Hk * kp.head_chunks, kp.B);
-  kern<<<grid, kWarpsK * 32, smem, st>>>(kp);
+  kern<<<grid, kWarpsK * 32, smem, st>>>(kp, maps[0], maps[1], maps[2], maps[3]);
   return cuda_check(cudaGetLastError(), "kivi_decode_kernel launch");
+}
+
+// W = words per key row (Kq's last dim). 2-bit caches whose geometry TMA can address take
+// the TMA form; everything else the cp.async form.
+template <int BITS>
+int launch_kivi(const KiviParams& kp, int n_splits, int64_t W, cudaStream_t st) {
+  alignas(64) CUtensorMap maps[4];
+  std::memset(maps, 0, sizeof maps);
+  if (BITS == 2 && kivi_tma_maps(kp, W, maps)) return launch_kivi_as<2, true>(kp, n_splits, maps, st);
+  return launch_kivi_as<BITS, false>(kp, n_splits, maps, st);
 }
 
 struct KiviPlan {
@@ -870,7 +1018,7 @@ int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd
     kp.head_chunks = pl.head_chunks; kp.nsplit = pl.n_kivi; kp.ntiles = pl.ntiles;
     kp.scale_log2 = scaling * kLog2eK;
     kp.part_m = part.m; kp.part_l = part.l; kp.part_o = part.o; kp.split_stride = ntot;
-    rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, st) : launch_kivi<4>(kp, pl.n_kivi, st);
+    rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, Kq->shape[3], st) : launch_kivi<4>(kp, pl.n_kivi, Kq->shape[3], st);
     if (rc) return rc;
   }
   if (pl.n_res > 0 && (stages & 2)) {
