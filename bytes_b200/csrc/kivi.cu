@@ -58,9 +58,12 @@ constexpr float kLn2K = 0.6931471805599453f;
 constexpr int kRedPitch = 132;  // floats per head row of the epilogue buffer (padded: no bank conflicts)
 constexpr int kKChunk = 4;      // tiles per key scale/min chunk
 
-// Shared-memory layout. TMA (2-bit only): the key tile lands unpadded with the 32-byte
-// swizzle (16-byte chunk c of row r at chunk c ^ ((r >> 2) & 1)), which keeps the
-// per-lane key reads conflict-free; the cp.async form pads rows to 48 bytes instead.
+// Shared-memory layout. Key tile: TMA (2-bit only) lands it unpadded with the 32-byte
+// swizzle (16-byte chunk c of row r at chunk c ^ ((r >> 2) & 1)); the cp.async form pads
+// rows to 48 / 80 bytes instead. 2-bit value tile: token t of the tile sits at row
+// (t & 7) * 16 + (t >> 3) (32-byte rows), so the four tokens that the four lane columns of
+// a warp read at once fall in four different bank groups; the 4-bit value tile keeps
+// token order in padded 80-byte rows.
 template <int BITS, bool TMA = false>
 struct KL {
   static constexpr int FPI = 32 / BITS;
@@ -81,13 +84,20 @@ struct KL {
   static constexpr int KC_ROW = 4 * kKChunk * 2;  // bytes per channel row of one chunk
   static constexpr int KC_BYTES = 2 * 128 * KC_ROW;
   static constexpr int OFF_KC = kStagesK * STAGE;
-  static constexpr int T_BYTES = 2 * 4 * 128 * 2;  // transposed key scale/min [2][4 groups][128 ch] f16
+  // Key scale/min of the current tile regrouped per lane column: [scale g0..g3, min g0..g3]
+  // x [4 columns tq, 80-byte pitch] x 32 f16 (channels 16j + 8h + 2tq + l at index 4j + 2h + l)
+  static constexpr int T_COL = 80;
+  static constexpr int T_GROUP = 4 * T_COL;
+  static constexpr int T_BYTES = 8 * T_GROUP;
   static constexpr int OFF_T = OFF_KC + 2 * KC_BYTES;
   static constexpr int OFF_BAR = OFF_T + T_BYTES;  // TMA: one mbarrier per stage
   static constexpr int SMEM = OFF_BAR + kStagesK * 8;
   static constexpr uint32_t TMA_BYTES = 128 * 32 + kTile * 32 + 2 * kTile * 8;  // K, V codes, V scale, V min
   static_assert(!TMA || (BITS == 2 && STAGE % 1024 == 0), "TMA stages hold the 2-bit tile at 1024-byte alignment");
 };
+
+// Byte offset of (token t, 16-byte chunk c) in the 2-bit value tile.
+__host__ __device__ constexpr int vq2_offset(int t, int c) { return ((t & 7) * 16 + (t >> 3)) * 32 + c * 16; }
 
 struct KiviParams {
   const void* q; int64_t q_sb, q_sh; int q_dtype;
@@ -121,6 +131,12 @@ __device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterp
 // whatever landed; a non-zero count means a result of that launch is wrong)
 __device__ unsigned int g_kivi_tma_timeouts = 0;
 
+// Headroom of the lazily rescaled softmax reference: when a tile's maximum exceeds the
+// reference, the reference moves to that maximum + kHeadroom (log2 units), so the running
+// sums are rescaled only when a score beats the last maximum by more than 2^kHeadroom and
+// every weight 2^(x - reference) stays <= 1.
+constexpr float kHeadroom = 4.f;
+
 template <int BITS, bool TMA>
 __global__ void __launch_bounds__(kWarpsK * 32, 4)
     kivi_decode_kernel(const KiviParams p, const __grid_constant__ CUtensorMap tm_kq,
@@ -131,7 +147,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
   // TMA destinations must sit on the swizzle atom: align the working base by hand (the
   // launch adds 1 KB); every shared-memory access below goes through `smem`
   uint8_t* smem = TMA ? smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : smem_raw;
-  uint8_t* tsm = smem + L::OFF_T;  // transposed key scale / min of the current tile
+  uint8_t* tsm = smem + L::OFF_T;  // key scale / min of the current tile, per lane column
   const uint32_t bar0 = smem_u32(smem + L::OFF_BAR);
   if (TMA) {
     if (threadIdx.x == 0) {
@@ -154,32 +170,34 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
   const int t_end = min(p.Sq, t_begin + ntiles * kTile);
   const int h0 = chunk * 8;
   const int nheads = min(8, p.G - h0);
-  // QK accumulator row g <-> token rho (row g+8 <-> rho+8) inside a 16-token row block;
-  // chosen so that the movmatrix transpose of P is the PV operand for tokens tq+4u.
+  // Lane roles. A 2-bit (4-bit) field masked into the low byte of an f16 half is the exact
+  // subnormal code * 2^(pos - 24); the power of two is undone on the fp32 accumulators.
+  //  2-bit: lane g owns byte g & 3 of word g >> 2 of the warp's 32-token key group, i.e.
+  //   tokens 16(g>>2) + 4(g&3) + {0,1,2,3}; QK accumulator row g (g+8) of row block rb
+  //   takes field 2rb (2rb+1) of that byte, so one byte-select PRMT of two channel words
+  //   feeds four operand registers (one AND each). On the value side m-tile pair i
+  //   (channels 32i..32i+31, one scale group) gives lane g byte g & 3 of word 2i + (g>>2):
+  //   row g (g+8) of m-tile 2i+e is channel 16(2i + (g>>2)) + 4(g&3) + 2e (+1).
+  //  4-bit: row g (g+8) of a row block is token rho (rho+8), rho = (g>>1) + 4(g&1), with
+  //   one PRMT per operand register; value row g (g+8) of m-tile mt is channel 16mt+g (+8).
   const int rho = (g >> 1) + 4 * (g & 1);
   // Byte-select PRMT selectors: byte x of the first word -> result byte 0 and byte x of
   // the second word -> result byte 2 (bytes 1 and 3 are masked off afterwards).
-  //  keys:   word = 16 (8) tokens of one channel; row rho takes token rho's byte
-  //  values: word = 16 (8) channels of one token; row g takes channel g's byte
-  uint32_t selK0, selK1, mskK, selV0, selV1, mskV;
-  float subK, subV;  // 2^(24 - field position): undoes the subnormal encoding per row
+  uint32_t selK0, selK1, mskK, selV0, mskV;
+  float subK, subV;
   if (BITS == 2) {
-    selK0 = uint32_t(rho >> 2) | (uint32_t(4 + (rho >> 2)) << 8);        // tokens 0..7 (low half)
-    selK1 = uint32_t(2 + (rho >> 2)) | (uint32_t(6 + (rho >> 2)) << 8);  // tokens 8..15 (high half)
-    mskK = 0x00030003u << (2 * (rho & 3));
-    subK = __int_as_float((127 + 24 - 2 * (rho & 3)) << 23);
-    selV0 = uint32_t(g >> 2) | (uint32_t(4 + (g >> 2)) << 8);            // channel g (low half)
-    selV1 = uint32_t(2 + (g >> 2)) | (uint32_t(6 + (g >> 2)) << 8);      // channel g+8 (high half)
-    mskV = 0x00030003u << (2 * (g & 3));
-    subV = __int_as_float((127 + 24 - 2 * (g & 3)) << 23);
+    selK0 = selK1 = selV0 = uint32_t(g & 3) | (uint32_t(4 + (g & 3)) << 8);
+    mskK = mskV = 0u;  // fields are compile-time: 0x00030003 << 2 * pos
+    subK = subV = 0.f;
   } else {
     selK0 = selK1 = uint32_t(rho >> 1) | (uint32_t(4 + (rho >> 1)) << 8);
     mskK = 0x000F000Fu << (4 * (rho & 1));
     subK = __int_as_float((127 + 24 - 4 * (rho & 1)) << 23);
-    selV0 = selV1 = uint32_t(g >> 1) | (uint32_t(4 + (g >> 1)) << 8);
+    selV0 = uint32_t(g >> 1) | (uint32_t(4 + (g >> 1)) << 8);
     mskV = 0x000F000Fu << (4 * (g & 1));
     subV = __int_as_float((127 + 24 - 4 * (g & 1)) << 23);
   }
+  (void)selK1;
 
   const uint32_t* kq_base = p.kq + int64_t(b) * p.kq_sb + int64_t(hk) * p.kq_sh;
   const __half* ks_base = p.ks + int64_t(b) * p.ks_sb + int64_t(hk) * p.ks_sh;
@@ -217,7 +235,11 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     }
   }
 
-  const float kmulK = subK * score_mul;  // accumulator -> log2-domain score, per lane
+  // accumulator -> log2-domain score: kmul[2rb + h] for row g + 8h of row block rb
+  float kmul[4];
+#pragma unroll
+  for (int f = 0; f < 4; ++f)
+    kmul[f] = BITS == 2 ? __int_as_float((127 + 24 - 2 * f) << 23) * score_mul : subK * score_mul;
 
   // Global -> shared copy assignment of this thread, fixed over the split's tiles.
   constexpr int NCH = L::KQ_WORDS / 4;  // 16-byte key chunks per channel row (2 or 4)
@@ -238,7 +260,9 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
   const int64_t k_pass = int64_t(128 / NCH) * p.kq_sc;  // channel rows per pass of the CTA
   const int64_t v_pass = int64_t(128 / NVC) * p.vq_st;
   const uint32_t k_dst = k_row * L::KQ_PITCH + k_ck * 16;
-  const uint32_t v_dst = L::OFF_VQ + v_row * L::VQ_PITCH + v_ck * 16;
+  // value rows per pass: 64 tokens (2-bit: +8 row slots of the interleaved tile) or 32
+  const uint32_t v_dst = L::OFF_VQ + (BITS == 2 ? vq2_offset(v_row, v_ck) : v_row * L::VQ_PITCH + v_ck * 16);
+  constexpr uint32_t V_PASS_BYTES = BITS == 2 ? 8 * 32 : (128 / NVC) * L::VQ_PITCH;
   auto load_tile = [&](int tile, int stage) {
     const int t0 = t_begin + tile * kTile;
     const uint32_t sbase = smem_u32(smem + stage * L::STAGE);
@@ -260,7 +284,9 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
         const uint32_t bar = bar0 + 8 * stage;
         mbar_arrive_expect_tx(bar, L::TMA_BYTES);
         tma_load_4d(sbase, &tm_kq, t0 / L::FPI, 0, hk, b, bar);
-        tma_load_4d(sbase + L::OFF_VQ, &tm_vq, 0, t0, hk, b, bar);
+        // value map dims {word, token / 8, token % 8, head, batch}: the box lands in the
+        // interleaved row order of the 2-bit value tile
+        tma_load_5d(sbase + L::OFF_VQ, &tm_vq, 0, t0 / 8, 0, hk, b, bar);
         tma_load_4d(sbase + L::OFF_VS, &tm_vs, 0, t0 / 2, hk, b, bar);
         tma_load_4d(sbase + L::OFF_VM, &tm_vm, 0, t0 / 2, hk, b, bar);
       }
@@ -270,7 +296,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
         cp_async16(sbase + k_dst + i * (128 / NCH) * L::KQ_PITCH, k_src + i * k_pass + tile * L::KQ_WORDS, 16);
 #pragma unroll
       for (int i = 0; i < NVC; ++i)
-        cp_async16(sbase + v_dst + i * (128 / NVC) * L::VQ_PITCH, v_src + i * v_pass + vt * p.vq_st, 16);
+        cp_async16(sbase + v_dst + i * V_PASS_BYTES, v_src + i * v_pass + vt * p.vq_st, 16);
       cp_async8(sbase + L::OFF_VS + threadIdx.x * 8, vs_src + vt * p.vs_st, 8);
       cp_async8(sbase + L::OFF_VM + threadIdx.x * 8, vm_src + vt * p.vm_st, 8);
     } else {
@@ -284,8 +310,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
 #pragma unroll
       for (int i = 0; i < NVC; ++i) {
         const bool ok = t0 + v_row + i * (128 / NVC) < t_end;
-        cp_async16(sbase + v_dst + i * (128 / NVC) * L::VQ_PITCH, ok ? v_src + i * v_pass + vt * p.vq_st : v_src,
-                   ok ? 16 : 0);
+        cp_async16(sbase + v_dst + i * V_PASS_BYTES, ok ? v_src + i * v_pass + vt * p.vq_st : v_src, ok ? 16 : 0);
       }
       const bool ok = t0 + int(threadIdx.x) < t_end;
       cp_async8(sbase + L::OFF_VS + threadIdx.x * 8, ok ? vs_src + vt * p.vs_st : vs_base, ok ? 8 : 0);
@@ -297,7 +322,13 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   float cacc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g<4: sum_t P_t * m_v[t][group g], heads 2tq,2tq+1
-  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  float mref[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  // this thread's slot in the per-column key scale layout (thread = channel)
+  const uint32_t t_slot = ((threadIdx.x >> 1) & 3) * L::T_COL +
+                          ((threadIdx.x >> 4) * 4 + ((threadIdx.x >> 3) & 1) * 2 + (threadIdx.x & 1)) * 2;
+  // 2-bit value reads: row block (tq + 4 warp) of the interleaved tile, word g >> 2
+  const uint32_t v_lane = (tq + 4 * warp) * 32 + 4 * (g >> 2);
 
 #pragma unroll
   for (int s = 0; s < kStagesK - 1; ++s) {
@@ -317,16 +348,20 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     }
     const uint8_t* st = smem + (it % kStagesK) * L::STAGE;
     {
-      // transpose key scale / min of this tile to [group][channel] (one channel per thread)
+      // regroup key scale / min of this tile per lane column (one channel per thread)
       const uint8_t* kc = smem + L::OFF_KC + ((it / kKChunk) & 1) * L::KC_BYTES + threadIdx.x * L::KC_ROW +
                           (it % kKChunk) * 8;
       const uint2 s4 = *reinterpret_cast<const uint2*>(kc);
       const uint2 m4 = *reinterpret_cast<const uint2*>(kc + 128 * L::KC_ROW);
-      uint16_t* ts = reinterpret_cast<uint16_t*>(tsm);
-      ts[0 * 128 + threadIdx.x] = uint16_t(s4.x); ts[1 * 128 + threadIdx.x] = uint16_t(s4.x >> 16);
-      ts[2 * 128 + threadIdx.x] = uint16_t(s4.y); ts[3 * 128 + threadIdx.x] = uint16_t(s4.y >> 16);
-      ts[4 * 128 + threadIdx.x] = uint16_t(m4.x); ts[5 * 128 + threadIdx.x] = uint16_t(m4.x >> 16);
-      ts[6 * 128 + threadIdx.x] = uint16_t(m4.y); ts[7 * 128 + threadIdx.x] = uint16_t(m4.y >> 16);
+      uint8_t* ts = tsm + t_slot;
+      *reinterpret_cast<uint16_t*>(ts + 0 * L::T_GROUP) = uint16_t(s4.x);
+      *reinterpret_cast<uint16_t*>(ts + 1 * L::T_GROUP) = uint16_t(s4.x >> 16);
+      *reinterpret_cast<uint16_t*>(ts + 2 * L::T_GROUP) = uint16_t(s4.y);
+      *reinterpret_cast<uint16_t*>(ts + 3 * L::T_GROUP) = uint16_t(s4.y >> 16);
+      *reinterpret_cast<uint16_t*>(ts + 4 * L::T_GROUP) = uint16_t(m4.x);
+      *reinterpret_cast<uint16_t*>(ts + 5 * L::T_GROUP) = uint16_t(m4.x >> 16);
+      *reinterpret_cast<uint16_t*>(ts + 6 * L::T_GROUP) = uint16_t(m4.y);
+      *reinterpret_cast<uint16_t*>(ts + 7 * L::T_GROUP) = uint16_t(m4.y >> 16);
     }
     __syncthreads();
     const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
@@ -337,17 +372,18 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     uint32_t qb[8][2];
     float bias[2];
     {
-      const uint8_t* tsr = tsm + warp * 256;         // scales of group `warp`
-      const uint8_t* tmr = tsm + (4 + warp) * 256;   // minima of group `warp`
+      const uint4* tsr = reinterpret_cast<const uint4*>(tsm + warp * L::T_GROUP + tq * L::T_COL);
+      const uint4* tmr = reinterpret_cast<const uint4*>(tsm + (4 + warp) * L::T_GROUP + tq * L::T_COL);
       float bacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c0 = 16 * j + 2 * tq;
-        qb[j][0] = h2u(__hmul2(u2h(qh[j][0]), u2h(lds_u32(tsr + c0 * 2))));
-        qb[j][1] = h2u(__hmul2(u2h(qh[j][1]), u2h(lds_u32(tsr + (c0 + 8) * 2))));
-        const uint32_t m01 = lds_u32(tmr + c0 * 2);
-        const uint32_t m89 = lds_u32(tmr + (c0 + 8) * 2);
-        mma_f16(bacc, m01, m01, m89, m89, qh[j][0], qh[j][1]);
+      for (int k = 0; k < 4; ++k) {
+        const uint4 sc = tsr[k], mn = tmr[k];  // .x/.y: j = 2k (h = 0/1), .z/.w: j = 2k+1
+        qb[2 * k][0] = h2u(__hmul2(u2h(qh[2 * k][0]), u2h(sc.x)));
+        qb[2 * k][1] = h2u(__hmul2(u2h(qh[2 * k][1]), u2h(sc.y)));
+        qb[2 * k + 1][0] = h2u(__hmul2(u2h(qh[2 * k + 1][0]), u2h(sc.z)));
+        qb[2 * k + 1][1] = h2u(__hmul2(u2h(qh[2 * k + 1][1]), u2h(sc.w)));
+        mma_f16(bacc, mn.x, mn.x, mn.y, mn.y, qh[2 * k][0], qh[2 * k][1]);
+        mma_f16(bacc, mn.z, mn.z, mn.w, mn.w, qh[2 * k + 1][0], qh[2 * k + 1][1]);
       }
       bias[0] = bacc[0] * score_mul;
       bias[1] = bacc[1] * score_mul;
@@ -365,15 +401,12 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
       // channels c0, c0+1 (k = 2tq, 2tq+1) and c0+8, c0+9 (k = 2tq+8, 2tq+9)
       const uint8_t* kr = kst + 16 * j * L::KQ_PITCH;
       if (BITS == 2) {
-        // .x = tokens 0..15 (row block 0), .y = tokens 16..31 (row block 1)
-        const uint2 wa = *reinterpret_cast<const uint2*>(kr);
-        const uint2 wb = *reinterpret_cast<const uint2*>(kr + L::KQ_PITCH);
-        const uint2 wc = *reinterpret_cast<const uint2*>(kr + 8 * L::KQ_PITCH);
-        const uint2 wd = *reinterpret_cast<const uint2*>(kr + 9 * L::KQ_PITCH);
-        mma_f16(s[0], prmt(wa.x, wb.x, selK0) & mskK, prmt(wa.x, wb.x, selK1) & mskK,
-                prmt(wc.x, wd.x, selK0) & mskK, prmt(wc.x, wd.x, selK1) & mskK, qb[j][0], qb[j][1]);
-        mma_f16(s[1], prmt(wa.y, wb.y, selK0) & mskK, prmt(wa.y, wb.y, selK1) & mskK,
-                prmt(wc.y, wd.y, selK0) & mskK, prmt(wc.y, wd.y, selK1) & mskK, qb[j][0], qb[j][1]);
+        // this lane's word (tokens 0..15 or 16..31 of the group) of the four channel rows
+        const uint8_t* kw = kr + 4 * (g >> 2);
+        const uint32_t rab = prmt(lds_u32(kw), lds_u32(kw + L::KQ_PITCH), selK0);
+        const uint32_t rcd = prmt(lds_u32(kw + 8 * L::KQ_PITCH), lds_u32(kw + 9 * L::KQ_PITCH), selK0);
+        mma_f16(s[0], rab & 0x00030003u, rab & 0x000C000Cu, rcd & 0x00030003u, rcd & 0x000C000Cu, qb[j][0], qb[j][1]);
+        mma_f16(s[1], rab & 0x00300030u, rab & 0x00C000C0u, rcd & 0x00300030u, rcd & 0x00C000C0u, qb[j][0], qb[j][1]);
       } else {
         // .x/.y = tokens 0..7 / 8..15 (row block 0), .z/.w = tokens 16..23 / 24..31
         const uint4 wa = *reinterpret_cast<const uint4*>(kr);
@@ -387,7 +420,11 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
       }
     }
 
-    // ---- online softmax over the 32 tokens (exp2 domain)
+    // group-local token of accumulator row g (+1 or +8 for row g+8) in row block rb
+    auto row_token = [&](int rb) { return BITS == 2 ? 16 * (g >> 2) + 4 * (g & 3) + 2 * rb : 16 * rb + rho; };
+    constexpr int kRowStep = BITS == 2 ? 1 : 8;
+
+    // ---- online softmax over the 32 tokens (exp2 domain, lazily rescaled reference)
     float pv[2][4];
     {
       float x[2][4];  // [head j][rb0 row, rb0 row+8, rb1 row, rb1 row+8]
@@ -395,37 +432,39 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
       for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
-          x[j][2 * rb] = fmaf(s[rb][j], kmulK, bias[j]);
-          x[j][2 * rb + 1] = fmaf(s[rb][2 + j], kmulK, bias[j]);
+          x[j][2 * rb] = fmaf(s[rb][j], kmul[2 * rb], bias[j]);
+          x[j][2 * rb + 1] = fmaf(s[rb][2 + j], kmul[2 * rb + 1], bias[j]);
         }
       if (tb + 32 > t_end) {  // warp-uniform: only the sequence's last group is partial
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
-          const int tr = tb + 16 * rb + rho;
+          const int tr = tb + row_token(rb);
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             if (tr >= t_end) x[j][2 * rb] = -INFINITY;
-            if (tr + 8 >= t_end) x[j][2 * rb + 1] = -INFINITY;
+            if (tr + kRowStep >= t_end) x[j][2 * rb + 1] = -INFINITY;
           }
         }
       }
-      float mnew[2], muse[2];
+      float mx[2];
       bool grow = false;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        float mx = fmaxf(fmaxf(x[j][0], x[j][1]), fmaxf(x[j][2], x[j][3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        mnew[j] = fmaxf(mrow[j], mx);
-        muse[j] = mnew[j] == -INFINITY ? 0.f : mnew[j];
-        grow |= mnew[j] > mrow[j];
+        float m = fmaxf(fmaxf(x[j][0], x[j][1]), fmaxf(x[j][2], x[j][3]));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        mx[j] = m;
+        grow |= m > mref[j];
       }
-      // rescale the running sums only when some head's maximum grew (alpha == 1 otherwise)
+      // move the reference only when some head's maximum passed it (rare after the first
+      // tile of a split): then alpha = 2^(old - new) rescales the running sums
       if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const float alpha = exp2f(mrow[j] - muse[j]);
+          const float mnew = mx[j] > mref[j] ? mx[j] + kHeadroom : mref[j];
+          const float alpha = mref[j] == -INFINITY ? 0.f : fast_exp2(mref[j] - mnew);
+          mref[j] = mnew;
           lrow[j] *= alpha;
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt) {
@@ -438,12 +477,12 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
       }
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        mrow[j] = mnew[j];
+        const float muse = mref[j] == -INFINITY ? 0.f : mref[j];
         float acc = 0.f;
 #pragma unroll
         for (int rb = 0; rb < 2; ++rb) {
-          pv[rb][j] = exp2f(x[j][2 * rb] - muse[j]);
-          pv[rb][2 + j] = exp2f(x[j][2 * rb + 1] - muse[j]);
+          pv[rb][j] = fast_exp2(x[j][2 * rb] - muse);
+          pv[rb][2 + j] = fast_exp2(x[j][2 * rb + 1] - muse);
           acc += pv[rb][j] + pv[rb][2 + j];
         }
         lrow[j] += acc;
@@ -451,16 +490,24 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     }
 
     // ---- P' = P * s_v per group; PV and the value-minimum term on the tensor cores
+    const int tw = 32 * warp;  // tile-local first token of the warp's group
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) {
-      const int tl = 32 * warp + 16 * rb;  // tile-local first token of the row block
       uint32_t pb[4][2];
       const uint32_t hp0 = pack_f16x2(pv[rb][0], pv[rb][1]);
       const uint32_t hp1 = pack_f16x2(pv[rb][2], pv[rb][3]);
       {
-        const uint2 vs0 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tl + rho) * 8);
-        const uint2 vs1 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tl + rho + 8) * 8);
-        const uint32_t s0w[2] = {vs0.x, vs0.y}, s1w[2] = {vs1.x, vs1.y};
+        // value scales of the tokens of rows g and g+8 (adjacent tokens in the 2-bit form)
+        const int tr = tw + row_token(rb);
+        uint32_t s0w[2], s1w[2];
+        if (BITS == 2) {
+          const uint4 vs01 = *reinterpret_cast<const uint4*>(st + L::OFF_VS + tr * 8);
+          s0w[0] = vs01.x; s0w[1] = vs01.y; s1w[0] = vs01.z; s1w[1] = vs01.w;
+        } else {
+          const uint2 vs0 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + tr * 8);
+          const uint2 vs1 = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tr + 8) * 8);
+          s0w[0] = vs0.x; s0w[1] = vs0.y; s1w[0] = vs1.x; s1w[1] = vs1.y;
+        }
 #pragma unroll
         for (int gr = 0; gr < 4; ++gr) {
           const uint32_t sel = (gr & 1) ? 0x3232u : 0x1010u;  // broadcast one f16 to both halves
@@ -468,33 +515,36 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
           pb[gr][1] = movmatrix_trans(h2u(__hmul2(u2h(hp1), u2h(prmt(s1w[gr >> 1], 0, sel)))));
         }
       }
+      // After the transpose, MMA k index kappa (0..15) of this row block is accumulator row
+      // kappa: lane tq's k pairs (2tq, 2tq+1) and (2tq+8, 2tq+9) are the tokens
+      //  2-bit: tq8 + {0, 4} and tq8 + {1, 5}, tq8 = 8tq + 2rb;
+      //  4-bit: tq + {0, 4} and tq + {8, 12} (+16rb).
+      const int kt0 = BITS == 2 ? 8 * tq + 2 * rb : 16 * rb + tq;
+      constexpr int kd1 = 4, kd2 = BITS == 2 ? 1 : 8, kd3 = BITS == 2 ? 5 : 12;
       {
-        // value minima: A rows = groups (rows g < 4), k = tokens tq, tq+4 | tq+8, tq+12
+        // value minima: A rows = groups (rows g < 4)
         const uint32_t pt0 = movmatrix_trans(hp0), pt1 = movmatrix_trans(hp1);
-        const uint8_t* vmr = st + L::OFF_VM + 2 * (g & 3);
+        const uint8_t* vmr = st + L::OFF_VM + 2 * (g & 3) + (tw + kt0) * 8;
         const uint32_t keep = g < 4 ? 0xffffffffu : 0u;
-        const uint32_t a0 = (lds_u16(vmr + (tl + tq) * 8) | (lds_u16(vmr + (tl + tq + 4) * 8) << 16)) & keep;
-        const uint32_t a2 = (lds_u16(vmr + (tl + tq + 8) * 8) | (lds_u16(vmr + (tl + tq + 12) * 8) << 16)) & keep;
+        const uint32_t a0 = (lds_u16(vmr) | (lds_u16(vmr + kd1 * 8) << 16)) & keep;
+        const uint32_t a2 = (lds_u16(vmr + kd2 * 8) | (lds_u16(vmr + kd3 * 8) << 16)) & keep;
         mma_f16(cacc, a0, 0u, a2, 0u, pt0, pt1);
       }
-      // value codes of tokens tl + tq + 4u, u = 0..3; A row g = channel 16mt+g, row g+8 =
-      // channel 16mt+8+g; k pairs = tokens (tq, tq+4) and (tq+8, tq+12)
       if (BITS == 2) {
-        uint32_t W[4][8];  // [u][word]: word mt holds channels 16mt..16mt+15
+        // tokens tw + kt0 + {0, 4, 1, 5} sit at interleaved rows (kt0 + d) * 16 + tq + 4 warp
+        const uint8_t* vt = st + L::OFF_VQ + v_lane + (2 * rb) * 512;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint8_t* row = st + L::OFF_VQ + (tl + tq + 4 * u) * L::VQ_PITCH;
-          const uint4 lo = *reinterpret_cast<const uint4*>(row);
-          const uint4 hi = *reinterpret_cast<const uint4*>(row + 16);
-          W[u][0] = lo.x; W[u][1] = lo.y; W[u][2] = lo.z; W[u][3] = lo.w;
-          W[u][4] = hi.x; W[u][5] = hi.y; W[u][6] = hi.z; W[u][7] = hi.w;
+        for (int i = 0; i < 4; ++i) {
+          // word 2i + (g >> 2) (byte offset 8i + 4(g >> 2), the latter in v_lane)
+          const uint32_t rA = prmt(lds_u32(vt + 8 * i), lds_u32(vt + 4 * 512 + 8 * i), selV0);
+          const uint32_t rC = prmt(lds_u32(vt + 1 * 512 + 8 * i), lds_u32(vt + 5 * 512 + 8 * i), selV0);
+          mma_f16(o[2 * i], rA & 0x00030003u, rA & 0x000C000Cu, rC & 0x00030003u, rC & 0x000C000Cu, pb[i][0],
+                  pb[i][1]);
+          mma_f16(o[2 * i + 1], rA & 0x00300030u, rA & 0x00C000C0u, rC & 0x00300030u, rC & 0x00C000C0u, pb[i][0],
+                  pb[i][1]);
         }
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
-          mma_f16(o[mt], prmt(W[0][mt], W[1][mt], selV0) & mskV, prmt(W[0][mt], W[1][mt], selV1) & mskV,
-                  prmt(W[2][mt], W[3][mt], selV0) & mskV, prmt(W[2][mt], W[3][mt], selV1) & mskV,
-                  pb[mt >> 1][0], pb[mt >> 1][1]);
       } else {
+        const int tl = tw + 16 * rb;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t W[4][8];  // [u][word]: word i holds channels 64*half + 8i .. +7
@@ -543,7 +593,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
   if (g == 0) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      red_m[warp * 8 + 2 * tq + j] = mrow[j];
+      red_m[warp * 8 + 2 * tq + j] = mref[j];
       red_l[warp * 8 + 2 * tq + j] = lrow[j];
     }
   }
@@ -554,12 +604,22 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kWarpsK; ++w) M = fmaxf(M, red_m[w * 8 + h]);
-    const float f = (M == -INFINITY) ? 0.f : exp2f(mrow[j] - M);
+    const float f = (M == -INFINITY) ? 0.f : fast_exp2(mref[j] - M);
+    float* ro = red_o + (warp * 8 + h) * kRedPitch;
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
-      const int ca = 16 * mt + g;  // A row g; row g+8 is channel ca + 8
-      red_o[(warp * 8 + h) * kRedPitch + ca] = fmaf(o[mt][j], subV, corr[mt >> 1][j]) * f;
-      red_o[(warp * 8 + h) * kRedPitch + ca + 8] = fmaf(o[mt][2 + j], subV, corr[mt >> 1][j]) * f;
+      if (BITS == 2) {
+        // rows g / g+8 of m-tile mt: adjacent channels ca, ca+1, field positions 2(mt&1) + {0, 1}
+        const int ca = 16 * (2 * (mt >> 1) + (g >> 2)) + 4 * (g & 3) + 2 * (mt & 1);
+        const float sv0 = __int_as_float((127 + 24 - 4 * (mt & 1)) << 23);
+        const float sv1 = __int_as_float((127 + 22 - 4 * (mt & 1)) << 23);
+        *reinterpret_cast<float2*>(ro + ca) = make_float2(fmaf(o[mt][j], sv0, corr[mt >> 1][j]) * f,
+                                                          fmaf(o[mt][2 + j], sv1, corr[mt >> 1][j]) * f);
+      } else {
+        const int ca = 16 * mt + g;  // A row g; row g+8 is channel ca + 8
+        ro[ca] = fmaf(o[mt][j], subV, corr[mt >> 1][j]) * f;
+        ro[ca + 8] = fmaf(o[mt][2 + j], subV, corr[mt >> 1][j]) * f;
+      }
     }
   }
   __syncthreads();
@@ -571,7 +631,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     float Lsum = 0.f, O = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarpsK; ++w) {
-      const float f = (M == -INFINITY) ? 0.f : exp2f(red_m[w * 8 + h] - M);
+      const float f = (M == -INFINITY) ? 0.f : fast_exp2(red_m[w * 8 + h] - M);
       Lsum += red_l[w * 8 + h] * f;
       O += red_o[(w * 8 + h) * kRedPitch + c];
     }
@@ -603,13 +663,14 @@ EncodeFn tensor_map_encoder() {
   return fn;
 }
 
-bool encode4d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, const cuuint64_t dims[4],
-              const cuuint64_t strides[3], const cuuint32_t box[4], CUtensorMapSwizzle sw) {
+// rank-R tiled map (R = 4 or 5): dims[0] is the contiguous one, strides (bytes) of dims 1..R-1
+bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
   const EncodeFn enc = tensor_map_encoder();
   if (!enc) return false;
-  const cuuint32_t es[4] = {1, 1, 1, 1};
-  return enc(m, dt, 4, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return enc(m, dt, cuuint32_t(rank), const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 struct TmaKey {
@@ -626,8 +687,10 @@ std::mutex g_tma_mu;
 TmaEntry g_tma[16];
 int g_tma_next = 0;
 
-// The 2-bit TMA form needs 16-byte aligned bases and strides (bytes) and dense 8-byte rows
-// of value scales/minima (read as 16-byte rows of two tokens). W = words per key row.
+// The 2-bit TMA form needs 16-byte aligned bases and strides (bytes), dense 32-byte value
+// rows (the value map splits the token index into token / 8 and token % 8, so the box lands
+// in the interleaved row order of the value tile) and dense 8-byte rows of value
+// scales/minima (read as 16-byte rows of two tokens). W = words per key row.
 bool kivi_tma_maps(const KiviParams& kp, int64_t W, CUtensorMap out[4]) {
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   // bytes stride of a dim, or a harmless 16-byte multiple when the dim has one entry
@@ -641,7 +704,8 @@ bool kivi_tma_maps(const KiviParams& kp, int64_t W, CUtensorMap out[4]) {
   const int64_t s_mh = st(kp.vm_sh, 2, Hk, Sq * 8), s_mb = st(kp.vm_sb, 2, B, s_mh * Hk);
   for (int64_t x : {s_kc, s_kh, s_kb, s_vt, s_vh, s_vb, s_sh, s_sb, s_mh, s_mb})
     if (x <= 0 || x % 16 || x >= (int64_t(1) << 40)) return false;
-  if (!a16(kp.kq) || !a16(kp.vq) || !a16(kp.vs) || !a16(kp.vm) || kp.vs_st != 4 || kp.vm_st != 4 || (Sq & 1))
+  if (!a16(kp.kq) || !a16(kp.vq) || !a16(kp.vs) || !a16(kp.vm) || kp.vs_st != 4 || kp.vm_st != 4 || kp.vq_st != 8 ||
+      (Sq & 7))
     return false;
   TmaKey key{};
   key.kq = kp.kq; key.vq = kp.vq; key.vs = kp.vs; key.vm = kp.vm;
@@ -659,17 +723,17 @@ bool kivi_tma_maps(const KiviParams& kp, int64_t W, CUtensorMap out[4]) {
   const cuuint64_t dk[4] = {cuuint64_t(W), 128, cuuint64_t(Hk), cuuint64_t(B)};
   const cuuint64_t sk[3] = {cuuint64_t(s_kc), cuuint64_t(s_kh), cuuint64_t(s_kb)};
   const cuuint32_t bk[4] = {8, 128, 1, 1};
-  const cuuint64_t dv[4] = {8, cuuint64_t(Sq), cuuint64_t(Hk), cuuint64_t(B)};
-  const cuuint64_t sv[3] = {cuuint64_t(s_vt), cuuint64_t(s_vh), cuuint64_t(s_vb)};
-  const cuuint32_t bv[4] = {8, uint32_t(kTile), 1, 1};
+  const cuuint64_t dv[5] = {8, cuuint64_t(Sq / 8), 8, cuuint64_t(Hk), cuuint64_t(B)};
+  const cuuint64_t sv[4] = {cuuint64_t(8 * s_vt), cuuint64_t(s_vt), cuuint64_t(s_vh), cuuint64_t(s_vb)};
+  const cuuint32_t bv[5] = {8, uint32_t(kTile / 8), 8, 1, 1};
   const cuuint64_t ds[4] = {8, cuuint64_t(Sq / 2), cuuint64_t(Hk), cuuint64_t(B)};
   const cuuint64_t ss[3] = {16, cuuint64_t(s_sh), cuuint64_t(s_sb)};
   const cuuint64_t sm[3] = {16, cuuint64_t(s_mh), cuuint64_t(s_mb)};
   const cuuint32_t bs[4] = {8, uint32_t(kTile / 2), 1, 1};
-  if (!encode4d(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, kp.kq, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_32B) ||
-      !encode4d(&m[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, kp.vq, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode4d(&m[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kp.vs, ds, ss, bs, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode4d(&m[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kp.vm, ds, sm, bs, CU_TENSOR_MAP_SWIZZLE_NONE))
+  if (!encode_map(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kp.kq, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_32B) ||
+      !encode_map(&m[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 5, kp.vq, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_map(&m[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, kp.vs, ds, ss, bs, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_map(&m[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, kp.vm, ds, sm, bs, CU_TENSOR_MAP_SWIZZLE_NONE))
     return false;
   TmaEntry& e = g_tma[g_tma_next];
   g_tma_next = (g_tma_next + 1) % 16;

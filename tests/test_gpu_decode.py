@@ -157,6 +157,29 @@ def test_kivi_decode_matches_oracle(cuda, bits, B, Hq, Hk, S, R):
     close(out, ref)
 
 
+@pytest.mark.parametrize("bits", [2, 4])
+def test_kivi_decode_padded_cache_rows(cuda, bits):
+    """Caches living inside wider buffers (row pitch > row length): the packed pass then
+    stages tiles with per-thread async copies instead of tensor-map (TMA) loads."""
+    B, Hq, Hk, S, R, D = 2, 14, 2, 1024 + 64 + 32, 32, 128
+    q, k, v, Kt, Vt, Sq = _kivi_inputs(B, Hq, Hk, S, R, D, seed=77 + bits, bits=bits)
+    Kq, Ks, Km = oracle.kivi_pack_last_dim(Kt, 32, bits)
+    Vq, Vs, Vm = oracle.kivi_pack_last_dim(Vt, 32, bits)
+    Kr, Vr = k[:, :, Sq:].contiguous(), v[:, :, Sq:].contiguous()
+    ref = oracle.kivi_decode_attn(q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, bits)
+
+    def padded(t, extra):  # same values, last-dim rows padded by `extra` elements
+        buf = torch.full(t.shape[:-1] + (t.shape[-1] + extra,), 7, dtype=t.dtype, device=cuda)
+        buf[..., :t.shape[-1]] = t.to(cuda)
+        return buf[..., :t.shape[-1]]
+
+    Kq_d, Vq_d = padded(Kq, 4), padded(Vq, 4)  # 16 extra bytes per row
+    assert Kq_d.stride(2) != Kq_d.shape[3] and Vq_d.stride(2) != Vq_d.shape[3]
+    dev = [t.to(cuda) for t in (q, Ks, Km, Kr, Vs, Vm, Vr)]
+    out = kv.kivi_decode_attn(dev[0], Kq_d, dev[1], dev[2], dev[3], Vq_d, dev[4], dev[5], dev[6], bits, 32)
+    close(out, ref)
+
+
 def test_kivi_gemv_matches_oracle(cuda):
     g = gen(13)
     bits = 2
