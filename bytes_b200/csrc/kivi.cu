@@ -52,7 +52,7 @@ namespace {
 
 constexpr int kWarpsK = 4;
 constexpr int kTile = 128;  // tokens per tile
-constexpr int kStagesK = 3;
+constexpr int kStagesK = 2;
 constexpr float kLog2eK = 1.4426950408889634f;
 constexpr float kLn2K = 0.6931471805599453f;
 constexpr int kRedPitch = 132;  // floats per head row of the epilogue buffer (padded: no bank conflicts)
@@ -85,7 +85,9 @@ struct KL {
   static constexpr int KC_BYTES = 2 * 128 * KC_ROW;
   static constexpr int OFF_KC = kStagesK * STAGE;
   // Key scale/min of the current tile regrouped per lane column: [scale g0..g3, min g0..g3]
-  // x [4 columns tq, 80-byte pitch] x 32 f16 (channels 16j + 8h + 2tq + l at index 4j + 2h + l)
+  // x [4 columns tq, 80-byte pitch] x 32 f16; channel 16j + 8h + 2tq + l sits in 16-byte
+  // unit j >> 1 at u32 slot 2h + (j & 1), half l, so one 16-byte read gives a lane the
+  // operands of k-steps j = 2k and 2k+1 in MMA register order
   static constexpr int T_COL = 80;
   static constexpr int T_GROUP = 4 * T_COL;
   static constexpr int T_BYTES = 8 * T_GROUP;
@@ -215,12 +217,25 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? g : 0)) * p.q_sh;
     float qv[8][4];
     float amax = 0.f;
+    // channel pairs (2tq, 2tq+1) are adjacent: one 32-bit load per pair for 16-bit queries
+    // whose rows start on an even element (the common case), element loads otherwise
+    const bool pairs = p.q_dtype != BD_F32 && ((qoff & 1) == 0) && ((reinterpret_cast<uintptr_t>(p.q) & 3) == 0);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        qv[j][e] = ok ? load_qk(p, qoff + 16 * j + 2 * tq + (e & 1) + (e >> 1) * 8) : 0.f;
-        amax = fmaxf(amax, fabsf(qv[j][e]));
+      for (int e = 0; e < 4; e += 2) {
+        const int64_t off = qoff + 16 * j + 2 * tq + (e >> 1) * 8;
+        float2 v = make_float2(0.f, 0.f);
+        if (ok && pairs) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(p.q) + off);
+          v = p.q_dtype == BD_BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w))
+                                   : __half22float2(*reinterpret_cast<const __half2*>(&w));
+        } else if (ok) {
+          v = make_float2(load_qk(p, off), load_qk(p, off + 1));
+        }
+        qv[j][e] = v.x;
+        qv[j][e + 1] = v.y;
+        amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
       }
     amax = warp_max(amax);
     int ex = 0;
@@ -325,8 +340,8 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
   float mref[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
   // this thread's slot in the per-column key scale layout (thread = channel)
-  const uint32_t t_slot = ((threadIdx.x >> 1) & 3) * L::T_COL +
-                          ((threadIdx.x >> 4) * 4 + ((threadIdx.x >> 3) & 1) * 2 + (threadIdx.x & 1)) * 2;
+  const uint32_t t_slot = ((threadIdx.x >> 1) & 3) * L::T_COL + (threadIdx.x >> 5) * 16 +
+                          (((threadIdx.x >> 3) & 1) * 2 + ((threadIdx.x >> 4) & 1)) * 4 + (threadIdx.x & 1) * 2;
   // 2-bit value reads: row block (tq + 4 warp) of the interleaved tile, word g >> 2
   const uint32_t v_lane = (tq + 4 * warp) * 32 + 4 * (g >> 2);
 
@@ -367,26 +382,28 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
     if (tb >= t_end) continue;
 
-    // ---- Q' = q * s_k (f16) and bias = sum_c q_c m_c. The bias MMA carries the group's
-    // minima in every A row, so every accumulator row holds the bias of its two heads.
+    // ---- Q' = q * s_k (f16) and bias = sum_c q_c m_c on the tensor cores. One 16-byte
+    // read {m(2k, h0), m(2k+1, h0), m(2k, h1), m(2k+1, h1)} is the A operand of both
+    // k-steps: with B = q of step 2k the A rows g carry step 2k, with B = q of step 2k+1 the
+    // rows g+8 carry step 2k+1, each row holding the bias of the lane's two heads.
     uint32_t qb[8][2];
     float bias[2];
     {
       const uint4* tsr = reinterpret_cast<const uint4*>(tsm + warp * L::T_GROUP + tq * L::T_COL);
       const uint4* tmr = reinterpret_cast<const uint4*>(tsm + (4 + warp) * L::T_GROUP + tq * L::T_COL);
-      float bacc[4] = {0.f, 0.f, 0.f, 0.f};
+      float be[4] = {0.f, 0.f, 0.f, 0.f}, bo[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint4 sc = tsr[k], mn = tmr[k];  // .x/.y: j = 2k (h = 0/1), .z/.w: j = 2k+1
+        const uint4 sc = tsr[k], mn = tmr[k];
         qb[2 * k][0] = h2u(__hmul2(u2h(qh[2 * k][0]), u2h(sc.x)));
-        qb[2 * k][1] = h2u(__hmul2(u2h(qh[2 * k][1]), u2h(sc.y)));
-        qb[2 * k + 1][0] = h2u(__hmul2(u2h(qh[2 * k + 1][0]), u2h(sc.z)));
+        qb[2 * k][1] = h2u(__hmul2(u2h(qh[2 * k][1]), u2h(sc.z)));
+        qb[2 * k + 1][0] = h2u(__hmul2(u2h(qh[2 * k + 1][0]), u2h(sc.y)));
         qb[2 * k + 1][1] = h2u(__hmul2(u2h(qh[2 * k + 1][1]), u2h(sc.w)));
-        mma_f16(bacc, mn.x, mn.x, mn.y, mn.y, qh[2 * k][0], qh[2 * k][1]);
-        mma_f16(bacc, mn.z, mn.z, mn.w, mn.w, qh[2 * k + 1][0], qh[2 * k + 1][1]);
+        mma_f16(be, mn.x, mn.y, mn.z, mn.w, qh[2 * k][0], qh[2 * k][1]);
+        mma_f16(bo, mn.x, mn.y, mn.z, mn.w, qh[2 * k + 1][0], qh[2 * k + 1][1]);
       }
-      bias[0] = bacc[0] * score_mul;
-      bias[1] = bacc[1] * score_mul;
+      bias[0] = (be[0] + bo[2]) * score_mul;
+      bias[1] = (be[1] + bo[3]) * score_mul;
     }
 
     // ---- S^T (each row scaled by 2^(pos-24)) for the warp's two 16-token row blocks
@@ -510,9 +527,10 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
         }
 #pragma unroll
         for (int gr = 0; gr < 4; ++gr) {
-          const uint32_t sel = (gr & 1) ? 0x3232u : 0x1010u;  // broadcast one f16 to both halves
-          pb[gr][0] = movmatrix_trans(h2u(__hmul2(u2h(hp0), u2h(prmt(s0w[gr >> 1], 0, sel)))));
-          pb[gr][1] = movmatrix_trans(h2u(__hmul2(u2h(hp1), u2h(prmt(s1w[gr >> 1], 0, sel)))));
+          const __half2 sa = (gr & 1) ? __high2half2(u2h(s0w[gr >> 1])) : __low2half2(u2h(s0w[gr >> 1]));
+          const __half2 sb = (gr & 1) ? __high2half2(u2h(s1w[gr >> 1])) : __low2half2(u2h(s1w[gr >> 1]));
+          pb[gr][0] = movmatrix_trans(h2u(__hmul2(u2h(hp0), sa)));
+          pb[gr][1] = movmatrix_trans(h2u(__hmul2(u2h(hp1), sb)));
         }
       }
       // After the transpose, MMA k index kappa (0..15) of this row block is accumulator row
@@ -623,22 +641,22 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
     }
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < nheads * 128; idx += kWarpsK * 32) {
-    const int h = idx >> 7, c = idx & 127;
-    float M = -INFINITY;
+  // thread = channel; heads in turn. The (max, sum) of each head comes from its channel-0 thread.
+  const int c = threadIdx.x;
+  const int64_t pi0 = (int64_t(b) * p.Hq + hk * p.G + h0) * p.split_stride + split;
+  for (int h = 0; h < nheads; ++h) {
+    float O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarpsK; ++w) M = fmaxf(M, red_m[w * 8 + h]);
-    float Lsum = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarpsK; ++w) {
-      const float f = (M == -INFINITY) ? 0.f : fast_exp2(red_m[w * 8 + h] - M);
-      Lsum += red_l[w * 8 + h] * f;
-      O += red_o[(w * 8 + h) * kRedPitch + c];
-    }
-    const int hq = hk * p.G + h0 + h;
-    const int64_t pi = (int64_t(b) * p.Hq + hq) * p.split_stride + split;
+    for (int w = 0; w < kWarpsK; ++w) O += red_o[(w * 8 + h) * kRedPitch + c];
+    const int64_t pi = pi0 + int64_t(h) * p.split_stride;
     p.part_o[pi * 128 + c] = O;
     if (c == 0) {
+      float M = -INFINITY, Lsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarpsK; ++w) M = fmaxf(M, red_m[w * 8 + h]);
+#pragma unroll
+      for (int w = 0; w < kWarpsK; ++w)
+        Lsum += (M == -INFINITY) ? 0.f : red_l[w * 8 + h] * fast_exp2(red_m[w * 8 + h] - M);
       p.part_m[pi] = M * kLn2K;
       p.part_l[pi] = Lsum;
     }

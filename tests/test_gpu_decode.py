@@ -143,6 +143,7 @@ def test_kivi_pack_bit_exact(cuda, bits):
     (1, 7, 1, 32 + 16, 16),       # one group + small residual
     (1, 16, 1, 1024 + 5, 5),      # G=16 (two head chunks)
     (2, 4, 4, 96, 0),             # no residual window
+    (1, 7, 1, 512 + 300, 300),    # window longer than a tile: spread over three splits
 ])
 def test_kivi_decode_matches_oracle(cuda, bits, B, Hq, Hk, S, R):
     D = 128
@@ -178,6 +179,25 @@ def test_kivi_decode_padded_cache_rows(cuda, bits):
     dev = [t.to(cuda) for t in (q, Ks, Km, Kr, Vs, Vm, Vr)]
     out = kv.kivi_decode_attn(dev[0], Kq_d, dev[1], dev[2], dev[3], Vq_d, dev[4], dev[5], dev[6], bits, 32)
     close(out, ref)
+
+
+def test_kivi_decode_unaligned_output_rows(cuda):
+    """Output rows whose pitch takes no 8-byte stores: the split slots are merged by the
+    separate combine kernel instead of the last CTA of each group."""
+    from bytes_b200 import _ops
+    bits, D = 2, 128
+    B, Hq, Hk, S, R = 2, 14, 2, 1024 + 128, 128
+    q, k, v, Kt, Vt, Sq = _kivi_inputs(B, Hq, Hk, S, R, D, seed=91, bits=bits)
+    Kq, Ks, Km = oracle.kivi_pack_last_dim(Kt, 32, bits)
+    Vq, Vs, Vm = oracle.kivi_pack_last_dim(Vt, 32, bits)
+    Kr, Vr = k[:, :, Sq:].contiguous(), v[:, :, Sq:].contiguous()
+    ref = oracle.kivi_decode_attn(q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, bits)
+    dev = [t.to(cuda) for t in (q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr)]
+    buf = torch.zeros(B, Hq, D + 2, dtype=torch.bfloat16, device=cuda)
+    out = buf[..., :D]
+    _ops.kivi_decode(dev[0][:, :, 0, :], *dev[1:], bits, 32, 1.0 / D ** 0.5, out)
+    close(out.unsqueeze(2), ref)
+    assert (buf[..., D:] == 0).all()
 
 
 def test_kivi_gemv_matches_oracle(cuda):
