@@ -50,6 +50,9 @@ struct DenseParams {
   // it does not read from; it waits for that kernel only before exiting, so a kernel
   // that waits on this one also sees the earlier kernel's writes.
   int pdl;
+  // 1 (with pdl, one split): after that wait, merge partial slots [0, split_offset) of each
+  // row with this CTA's own result and write `out`
+  int merge;
 };
 
 template <typename T>
@@ -341,6 +344,76 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
       }
     }
   __syncthreads();
+  if (p.merge) {
+    // ---- merge with the slots of the pass this grid waits for. Phase A: TPH threads per
+    // head turn the slot maxima into weights; phase B: thread = (head, 4 channels).
+    griddep_wait();
+    const int n = p.split_offset;
+    constexpr int TPH = kWarps * 32 / NH;
+    float* wts = red_o + kWarps * NH * D;  // [NH][n + 1]; slot n = this CTA
+    float* sl = wts + NH * (n + 1);        // [NH] total sums
+    {
+      const int h = threadIdx.x / TPH, part = threadIdx.x % TPH;
+      const int hq = hk * p.G + h0 + min(h, nheads - 1);
+      const int64_t row = int64_t(b) * p.Hq + hq;
+      const float* mr = p.part_m + row * p.split_stride;
+      const float* lr = p.part_l + row * p.split_stride;
+      float Mo = -INFINITY;  // this CTA's maximum (log2 units) and sum
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) Mo = fmaxf(Mo, red_m[w * NH + h]);
+      float Lo = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) Lo += Mo == -INFINITY ? 0.f : red_l[w * NH + h] * exp2f(red_m[w * NH + h] - Mo);
+      const float mo = Mo * kLn2;
+      float Mx = mo;
+      for (int s = part; s < n; s += TPH) Mx = fmaxf(Mx, __ldcg(mr + s));
+#pragma unroll
+      for (int d = 1; d < TPH; d <<= 1) Mx = fmaxf(Mx, __shfl_xor_sync(0xffffffffu, Mx, d));
+      float L = 0.f;
+      for (int s = part; s < n; s += TPH) {
+        const float w = Mx == -INFINITY ? 0.f : __expf(__ldcg(mr + s) - Mx);
+        wts[h * (n + 1) + s] = w;
+        L = fmaf(__ldcg(lr + s), w, L);
+      }
+#pragma unroll
+      for (int d = 1; d < TPH; d <<= 1) L += __shfl_xor_sync(0xffffffffu, L, d);
+      if (part == 0) {
+        const float wo = Mx == -INFINITY ? 0.f : __expf(mo - Mx);
+        wts[h * (n + 1) + n] = wo;
+        sl[h] = L + Lo * wo;
+      }
+    }
+    __syncthreads();
+    constexpr int C4 = D / 4;
+    for (int idx = threadIdx.x; idx < nheads * C4; idx += kWarps * 32) {
+      const int h = idx / C4, c = 4 * (idx % C4);
+      const int hq = hk * p.G + h0 + h;
+      const int64_t row = int64_t(b) * p.Hq + hq;
+      const float* wr = wts + h * (n + 1);
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float4 v = *reinterpret_cast<const float4*>(red_o + (w * NH + h) * D + c);
+        O.x += v.x; O.y += v.y; O.z += v.z; O.w += v.w;
+      }
+      const float wo = wr[n];
+      O.x *= wo; O.y *= wo; O.z *= wo; O.w *= wo;
+      const float* orow = p.part_o + row * p.split_stride * D + c;
+#pragma unroll 6
+      for (int s = 0; s < n; ++s) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(orow + int64_t(s) * D));
+        const float w = wr[s];
+        O.x = fmaf(v.x, w, O.x); O.y = fmaf(v.y, w, O.y); O.z = fmaf(v.z, w, O.z); O.w = fmaf(v.w, w, O.w);
+      }
+      const float inv = 1.f / sl[h];
+      const int64_t off = int64_t(b) * p.o_sb + int64_t(hq) * p.o_sh + c;
+      store_out(p.out, p.out_dtype, off, O.x * inv);
+      store_out(p.out, p.out_dtype, off + 1, O.y * inv);
+      store_out(p.out, p.out_dtype, off + 2, O.z * inv);
+      store_out(p.out, p.out_dtype, off + 3, O.w * inv);
+    }
+    return;
+  }
   for (int idx = threadIdx.x; idx < nheads * D; idx += kWarps * 32) {
     const int h = idx / D, c = idx % D;
     float M = -INFINITY;
@@ -505,17 +578,18 @@ int launch_dense(const DenseParams& p, const Plan& pl, cudaStream_t st) {
   constexpr int ELT = FP8 ? 1 : 2;
   constexpr int PITCH = D * ELT + 16;
   size_t smem = size_t(kStages) * 2 * kRows * PITCH;
-  const size_t red = (2 * kWarps * 8 * NT + size_t(kWarps) * 8 * NT * D) * sizeof(float);
+  size_t red = (2 * kWarps * 8 * NT + size_t(kWarps) * 8 * NT * D) * sizeof(float);
+  if (p.merge) red += (size_t(8 * NT) * (p.split_offset + 1) + 8 * NT) * sizeof(float);
   smem = std::max(smem, red);
   auto kern = dense_decode_kernel<D, NT, FP8>;
-  static bool attr_set[64] = {false};
+  static size_t attr_set[64] = {0};  // dynamic shared memory allowed so far, per device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
+  if (attr_set[dev & 63] < smem) {
     int rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
                         "cudaFuncSetAttribute");
     if (rc) return rc;
-    attr_set[dev & 63] = true;
+    attr_set[dev & 63] = smem;
   }
   dim3 grid(pl.n_splits, p.Hk * pl.head_chunks, p.B);
   if (p.pdl) return launch_programmatic(kern, grid, dim3(kWarps * 32), smem, st, p, "dense_decode_kernel launch");
@@ -594,6 +668,27 @@ int launch_dense_partials(const bd_tensor* q, const bd_tensor* k, const bd_tenso
   p.split_offset = split_offset; p.split_stride = part.nsplit;
   p.direct = 0;
   p.pdl = pdl ? 1 : 0;
+  return dispatch_dense(p, pl, st);
+}
+
+int launch_dense_merge(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
+                       const Partials& part, int split_offset, const bd_tensor* out, cudaStream_t st) {
+  int rc;
+  if ((rc = validate(q, k, v))) return rc;
+  Plan pl;
+  if ((rc = make_plan(q, k, &pl))) return rc;
+  if (pl.D % 4) return fail(BD_ERR_UNSUPPORTED, "merge needs head_dim % 4 == 0");
+  const int64_t S = k->shape[2];
+  pl.tiles_per_split = int(std::max<int64_t>(1, (S + kRows - 1) / kRows));
+  pl.n_splits = 1;
+  DenseParams p{};
+  fill_common(p, q, k, v, pl, scaling);
+  p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
+  p.split_offset = split_offset; p.split_stride = part.nsplit;
+  p.out = out->data; p.out_dtype = out->dtype; p.o_sb = out->stride[0]; p.o_sh = out->stride[1];
+  p.direct = 0;
+  p.pdl = 1;
+  p.merge = 1;
   return dispatch_dense(p, pl, st);
 }
 

@@ -12,12 +12,13 @@ struct Partials {
   int nsplit;  // total splits in the buffer (stride)
 };
 
+// o first, so every partial row of D floats starts on a 16-byte boundary when D % 4 == 0
 inline Partials carve_partials(void* ws, size_t rows, int nsplit, int D) {
   float* base = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
   Partials p;
-  p.m = base;
-  p.l = base + rows * nsplit;
-  p.o = base + 2 * rows * nsplit;
+  p.o = base;
+  p.m = base + rows * nsplit * size_t(D);
+  p.l = p.m + rows * nsplit;
   p.nsplit = nsplit;
   return p;
 }
@@ -34,6 +35,12 @@ int dense_split_count(int64_t B, int64_t Hq, int64_t Hk, int64_t S, int64_t D, i
 int launch_dense_partials(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
                           const Partials& part, int split_offset, int nsplit_here, cudaStream_t st,
                           bool pdl = false);
+// One dense split per (b, KV head, head chunk) over k,v, launched as a programmatic
+// dependent of the pass that fills slots [0, split_offset) of `part`: each CTA waits for
+// that pass, then merges those slots with its own result and writes `out` (no combine
+// kernel). Needs D % 4 == 0.
+int launch_dense_merge(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
+                       const Partials& part, int split_offset, const bd_tensor* out, cudaStream_t st);
 
 // Final merge of all splits in `part` into out [B,Hq,D] (bf16/f16/f32). pdl: launch as a
 // programmatic dependent; the kernel waits for its predecessor before reading partials.

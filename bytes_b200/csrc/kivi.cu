@@ -1103,6 +1103,11 @@ int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd
     rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, Kq->shape[3], st) : launch_kivi<4>(kp, pl.n_kivi, Kq->shape[3], st);
     if (rc) return rc;
   }
+  if (pl.n_res == 1 && pl.n_kivi > 0 && (stages & 7) == 7) {
+    // one window CTA per group: it waits for the packed pass and merges the group's split
+    // slots itself, so no combine kernel runs
+    return launch_dense_merge(Q, K_residual, V_residual, scaling, part, pl.n_kivi, out, st);
+  }
   if (pl.n_res > 0 && (stages & 2)) {
     // programmatic dependent of the KIVI pass when that ran just before it
     const bool pdl = pl.n_kivi > 0 && (stages & 1);
