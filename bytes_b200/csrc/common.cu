@@ -1,6 +1,8 @@
 // Host-side helpers shared by every entry point: error reporting and descriptor checks.
 #include "common.cuh"
 
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 namespace bd {
@@ -17,6 +19,33 @@ int fail(int status, const std::string& msg) {
 int cuda_check(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return BD_OK;
   return fail(BD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda)
+EncodeFn tensor_map_encoder() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(f);
+  });
+  return fn;
+}
+}  // namespace
+
+bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  const EncodeFn enc = tensor_map_encoder();
+  if (!enc || rank < 1 || rank > 5) return false;
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return enc(m, dt, cuuint32_t(rank), const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int num_sms() {

@@ -1,5 +1,6 @@
 // Shared device/host helpers for the decode-attention kernels (sm_100a).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,6 +37,11 @@ int check_tensor(const bd_tensor* t, const char* name, int ndim, int dtype = -1)
 // base pointer to be multiples of `align` bytes.
 int check_rows_aligned(const bd_tensor* t, const char* name, size_t align = 16);
 std::string shape_str(const bd_tensor* t);
+// Tiled TMA tensor map of rank 3..5 (dims[0] contiguous; strides in bytes of dims 1..rank-1),
+// encoded through the driver entry point fetched from the runtime. False if unavailable or
+// rejected.
+bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw);
 
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ float warp_max(float v) {
@@ -162,6 +168,13 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c
       "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
       "[%6];\n" ::"r"(dst),
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int c0, int c1, int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(
+          dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* map, int c0, int c1, int c2, int c3, int c4,

@@ -666,31 +666,6 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
 // ---- TMA tensor maps (host). Encoded through the driver entry point fetched from the
 // runtime (no link against libcuda) and cached per cache-tensor geometry, so a decode loop
 // over the same caches encodes once.
-using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
-
-EncodeFn tensor_map_encoder() {
-  static EncodeFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(f);
-  });
-  return fn;
-}
-
-// rank-R tiled map (R = 4 or 5): dims[0] is the contiguous one, strides (bytes) of dims 1..R-1
-bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
-                const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
-  const EncodeFn enc = tensor_map_encoder();
-  if (!enc) return false;
-  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
-  return enc(m, dt, cuuint32_t(rank), const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 struct TmaKey {
   const void* kq; const void* vq; const void* vs; const void* vm;
   int64_t W, Sq, Hk, B, kq_sc, kq_sh, kq_sb, vq_st, vq_sh, vq_sb, vs_sh, vs_sb, vm_sh, vm_sb;

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 namespace bd {
 namespace {
@@ -38,6 +39,7 @@ constexpr int kPStages = 2;  // 2 stages: the LUT chunk plus two tiles fit twice
 constexpr int kHC = 4;              // query heads per CTA
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kLn2P = 0.6931471805599453f;
+constexpr float kPHeadroom = 4.f;  // log2 headroom of the lazily moved softmax reference
 
 enum VKind { V_BF16 = 0, V_FP8 = 1, V_INT8 = 2, V_PQ = 3, V_NONE = 4 };
 
@@ -60,11 +62,16 @@ struct PqParams {
 
 struct PqSmem {
   int lut_bytes, codes_pitch, codes_bytes, kout_pitch, kout_bytes, v_pitch, v_bytes, vs_bytes, stage, recon_bytes;
+  int off_stages;                          // first stage, past the LUT
+  int off_codes, off_kout, off_v, off_vs;  // regions inside a stage
 };
 
 __host__ __device__ inline int round16(int x) { return (x + 15) & ~15; }
 
-__host__ __device__ inline PqSmem pq_smem(int vk, int M, int K, int C, int D, int Mv) {
+// tma: the tensor-map form (1-byte values, D = 128, no outliers, not paged): values first
+// in 128-byte rows under the 128-byte swizzle, then codes, then value scales; stages start
+// on 1024-byte boundaries.
+__host__ __device__ inline PqSmem pq_smem(int vk, int M, int K, int C, int D, int Mv, bool tma = false) {
   PqSmem s{};
   s.lut_bytes = M * K * kHC * 4;
   s.codes_pitch = round16(M);
@@ -78,25 +85,56 @@ __host__ __device__ inline PqSmem pq_smem(int vk, int M, int K, int C, int D, in
   s.v_pitch = vk == V_PQ ? vrow : (vrow ? vrow + 16 : 0);
   s.v_bytes = kPRows * s.v_pitch;
   s.vs_bytes = vk == V_INT8 ? kPRows * 2 : 0;
-  s.stage = s.codes_bytes + s.kout_bytes + s.v_bytes + s.vs_bytes;
   s.recon_bytes = vk == V_PQ ? kPRows * (D * 2 + 16) : 0;
+  if (tma) {
+    s.v_pitch = D;
+    s.v_bytes = kPRows * D;
+    s.off_v = 0;
+    s.off_codes = s.v_bytes;
+    s.off_kout = s.off_codes + s.codes_bytes;
+    s.off_vs = s.off_kout + s.kout_bytes;
+    s.stage = (s.off_vs + s.vs_bytes + 1023) & ~1023;
+    s.off_stages = (s.lut_bytes + 1023) & ~1023;
+  } else {
+    s.off_codes = 0;
+    s.off_kout = s.codes_bytes;
+    s.off_v = s.off_kout + s.kout_bytes;
+    s.off_vs = s.off_v + s.v_bytes;
+    s.stage = s.off_vs + s.vs_bytes;
+    s.off_stages = s.lut_bytes;
+  }
   return s;
 }
+
+// TMA waits that ran past their iteration limit (a non-zero count means a result is wrong)
+__device__ unsigned int g_pq_tma_timeouts = 0;
 
 __device__ __forceinline__ float ld16f(const uint16_t* p, int64_t off, int dt) {
   const uint16_t u = p[off];
   return dt == BD_BF16 ? __uint_as_float(uint32_t(u) << 16) : __half2float(__ushort_as_half(u));
 }
 
-template <int VK, bool PAGED, bool OUTL, int D>
-__global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+template <int VK, bool PAGED, bool OUTL, int D, bool TMA>
+__global__ void __launch_bounds__(kPW * 32, 2)
+    pq_decode_kernel(const PqParams p, const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_vs) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // TMA stages sit on the swizzle atom: align the working base by hand (the launch adds 1 KB)
+  uint8_t* smem = TMA ? smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : smem_raw;
   griddep_launch_dependents();  // the combine queued behind may start launching (it waits for this grid)
   constexpr int KSTEPS = D / 16;
-  const PqSmem L = pq_smem(VK, p.M, p.K, OUTL ? p.C : 0, D, p.Mv);
+  const PqSmem L = pq_smem(VK, p.M, p.K, OUTL ? p.C : 0, D, p.Mv, TMA);
   float* lut_s = reinterpret_cast<float*>(smem);
-  uint8_t* stages = smem + L.lut_bytes;
+  uint8_t* stages = smem + L.off_stages;
   uint8_t* recon = stages + kPStages * L.stage;
+  const uint32_t bar0 = smem_u32(stages + kPStages * L.stage);  // TMA: one mbarrier per stage
+  if (TMA) {
+    if (threadIdx.x == 0) {
+      for (int s = 0; s < kPStages; ++s) mbar_init(bar0 + 8 * s, 1);
+      mbar_fence_init();
+    }
+    __syncthreads();
+  }
 
   const int split = blockIdx.x;
   const int hk = blockIdx.y / p.head_chunks;
@@ -168,6 +206,18 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
     const int t0 = t_begin + tile * kPRows;
     uint8_t* st = stages + stage * L.stage;
     const uint32_t sb = smem_u32(st);
+    if (TMA) {
+      // one thread moves the tile; rows past the sequence arrive as zeros and rows past the
+      // split are masked by the token bounds below
+      if (threadIdx.x == 0) {
+        const uint32_t bar = bar0 + 8 * stage;
+        mbar_arrive_expect_tx(bar, uint32_t(L.v_bytes + L.codes_bytes + L.vs_bytes));
+        tma_load_4d(sb + L.off_v, &tm_v, 0, t0, hk, b, bar);
+        tma_load_4d(sb + L.off_codes, &tm_codes, 0, t0, hk, b, bar);
+        if (VK == V_INT8) tma_load_3d(sb + L.off_vs, &tm_vs, t0, hk, b, bar);
+      }
+      return;
+    }
     // codes: M bytes per token (M <= 16 -> one 16-byte chunk; else several)
     const int cch = L.codes_pitch / 16;
     for (int c = threadIdx.x; c < kPRows * cch; c += kPW * 32) {
@@ -178,15 +228,15 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
       const uint8_t* src = p.codes + (ok ? row_of(t, p.c_sb, p.c_sh, p.c_ss) : 0) + cc * 16;
       // byte-granular copy of possibly unaligned rows
       if (nbytes == 16 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-        cp_async16(sb + r * L.codes_pitch + cc * 16, src, 16);
+        cp_async16(sb + L.off_codes + r * L.codes_pitch + cc * 16, src, 16);
       } else {
-        for (int e = 0; e < 16; ++e) st[r * L.codes_pitch + cc * 16 + e] = e < nbytes ? src[e] : 0;
+        for (int e = 0; e < 16; ++e) st[L.off_codes + r * L.codes_pitch + cc * 16 + e] = e < nbytes ? src[e] : 0;
       }
     }
     if (OUTL) {
       for (int r = threadIdx.x; r < kPRows; r += kPW * 32) {
         const int t = t0 + r;
-        uint16_t* dst = reinterpret_cast<uint16_t*>(st + L.codes_bytes + r * L.kout_pitch);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(st + L.off_kout + r * L.kout_pitch);
         if (t < t_end) {
           const uint16_t* src = p.kout + row_of(t, p.ko_sb, p.ko_sh, p.ko_ss);
           for (int c = 0; c < 8; ++c) dst[c] = c < p.C ? src[int64_t(c) * p.ko_sc] : 0;
@@ -195,7 +245,7 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
         }
       }
     }
-    uint8_t* vst = st + L.codes_bytes + L.kout_bytes;
+    uint8_t* vst = st + L.off_v;
     if (VK == V_BF16 || VK == V_FP8 || VK == V_INT8) {
       constexpr int ELT = VK == V_BF16 ? 2 : 1;
       constexpr int CH = D * ELT / 16;
@@ -204,10 +254,10 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
         const int t = t0 + r;
         const bool ok = t < t_end;
         const uint8_t* src = p.v + (ok ? row_of(t, p.v_sb, p.v_sh, p.v_ss) : 0) * ELT + cc * 16;
-        cp_async16(sb + L.codes_bytes + L.kout_bytes + r * L.v_pitch + cc * 16, src, ok ? 16 : 0);
+        cp_async16(sb + L.off_v + r * L.v_pitch + cc * 16, src, ok ? 16 : 0);
       }
       if (VK == V_INT8) {
-        __half* vs = reinterpret_cast<__half*>(vst + L.v_bytes);
+        __half* vs = reinterpret_cast<__half*>(st + L.off_vs);
         for (int r = threadIdx.x; r < kPRows; r += kPW * 32) {
           const int t = t0 + r;
           vs[r] = t < t_end ? p.vsc[int64_t(b) * p.vs_sb + int64_t(hk) * p.vs_sh + int64_t(t) * p.vs_ss]
@@ -239,7 +289,12 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
   const int jlo = (tq >> 1) ? jmid : 0, jhi = (tq >> 1) ? p.M : jmid;
   const int r0 = warp * 16;
   for (int it = 0; it < ntiles; ++it) {
-    cp_async_wait<kPStages - 2>();
+    if (TMA) {
+      if (!mbar_wait(bar0 + 8 * (it % kPStages), (it / kPStages) & 1) && threadIdx.x == 0)
+        atomicAdd(&g_pq_tma_timeouts, 1u);
+    } else {
+      cp_async_wait<kPStages - 2>();
+    }
     __syncthreads();
     {
       const int nxt = it + kPStages - 1;
@@ -247,7 +302,7 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
       cp_async_commit();
     }
     const uint8_t* st = stages + (it % kPStages) * L.stage;
-    const uint8_t* vst = st + L.codes_bytes + L.kout_bytes;
+    const uint8_t* vst = st + L.off_v;
     if (VK == V_PQ) {
       // reconstruct this tile's values as f16 rows: v[t][j*dsv + i] = cent[j][code][i]
       for (int i = threadIdx.x; i < kPRows * p.Mv; i += kPW * 32) {
@@ -270,8 +325,8 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
     // ---- LUT scores for tokens r0+g, r0+g+8 and heads 2hp, 2hp+1 over subspaces [jlo, jhi)
     float sc[4] = {0.f, 0.f, 0.f, 0.f};  // (row g: h0, h1), (row g+8: h0, h1)
     {
-      const uint8_t* ca = st + (r0 + g) * L.codes_pitch;
-      const uint8_t* cb = st + (r0 + g + 8) * L.codes_pitch;
+      const uint8_t* ca = st + L.off_codes + (r0 + g) * L.codes_pitch;
+      const uint8_t* cb = st + L.off_codes + (r0 + g + 8) * L.codes_pitch;
       const float* lj = lut_s + jlo * p.K * kHC + 2 * hp;  // LUT rows of subspace j, stepped per j
       const int jstep = p.K * kHC;
       if (p.M == 16) {
@@ -297,8 +352,8 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
 #pragma unroll
       for (int e = 0; e < 4; ++e) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
       if (OUTL) {
-        const uint16_t* ka = reinterpret_cast<const uint16_t*>(st + L.codes_bytes + (r0 + g) * L.kout_pitch);
-        const uint16_t* kb = reinterpret_cast<const uint16_t*>(st + L.codes_bytes + (r0 + g + 8) * L.kout_pitch);
+        const uint16_t* ka = reinterpret_cast<const uint16_t*>(st + L.off_kout + (r0 + g) * L.kout_pitch);
+        const uint16_t* kb = reinterpret_cast<const uint16_t*>(st + L.off_kout + (r0 + g + 8) * L.kout_pitch);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const float xa = ld16f(ka, c, p.ko_dtype), xb = ld16f(kb, c, p.ko_dtype);
@@ -321,27 +376,44 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
       continue;
     }
 
-    // ---- online softmax (exp2 domain) on accumulator-layout scores
+    // ---- online softmax (exp2 domain) on accumulator-layout scores. The reference mrow
+    // moves only when a score passes it, to that score + kPHeadroom, so the running sums
+    // are rescaled rarely and every weight 2^(x - mrow) stays <= 1.
     float pv[4];
+    {
+      float a[2], c[2], mx[2];
+      bool grow = false;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const float a = va ? sc[j] * kLog2eP : -INFINITY;
-      const float c = vb ? sc[2 + j] * kLog2eP : -INFINITY;
-      float mx = fmaxf(a, c);
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float mnew = fmaxf(mrow[j], mx);
-      const float muse = mnew == -INFINITY ? 0.f : mnew;
-      const float alpha = exp2f(mrow[j] - muse);
-      pv[j] = exp2f(a - muse);
-      pv[2 + j] = exp2f(c - muse);
-      lrow[j] = lrow[j] * alpha + pv[j] + pv[2 + j];
-      mrow[j] = mnew;
+      for (int j = 0; j < 2; ++j) {
+        a[j] = va ? sc[j] * kLog2eP : -INFINITY;
+        c[j] = vb ? sc[2 + j] * kLog2eP : -INFINITY;
+        float m = fmaxf(a[j], c[j]);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        mx[j] = m;
+        grow |= m > mrow[j];
+      }
+      if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-      for (int mt = 0; mt < KSTEPS; ++mt) {
-        o[mt][j] *= alpha;
-        o[mt][2 + j] *= alpha;
+        for (int j = 0; j < 2; ++j) {
+          const float mnew = mx[j] > mrow[j] ? mx[j] + kPHeadroom : mrow[j];
+          const float alpha = mrow[j] == -INFINITY ? 0.f : fast_exp2(mrow[j] - mnew);
+          mrow[j] = mnew;
+          lrow[j] *= alpha;
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt) {
+            o[mt][j] *= alpha;
+            o[mt][2 + j] *= alpha;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float muse = mrow[j] == -INFINITY ? 0.f : mrow[j];
+        pv[j] = fast_exp2(a[j] - muse);
+        pv[2 + j] = fast_exp2(c[j] - muse);
+        lrow[j] += pv[j] + pv[2 + j];
       }
     }
 
@@ -371,7 +443,7 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
     } else {
       float q0 = pv[0], q1 = pv[1], q2 = pv[2], q3 = pv[3];
       if (VK == V_INT8) {
-        const __half* vsr = reinterpret_cast<const __half*>(vst + L.v_bytes);
+        const __half* vsr = reinterpret_cast<const __half*>(st + L.off_vs);
         const float sa = __half2float(vsr[r0 + g]), sb = __half2float(vsr[r0 + g + 8]);
         q0 *= sa; q1 *= sa; q2 *= sb; q3 *= sb;
       }
@@ -382,7 +454,10 @@ __global__ void __launch_bounds__(kPW * 32, 2) pq_decode_kernel(const PqParams p
 #pragma unroll
       for (int m2 = 0; m2 < KSTEPS / 2; ++m2) {
         uint32_t x0, x1, x2, x3;
-        ldmatrix_x4_trans(x0, x1, x2, x3, vs + vrow * L.v_pitch + m2 * 32 + (lane >> 4) * 16);
+        // TMA tile: 128-byte rows, 16-byte chunk c of row r at chunk c ^ (r & 7) (vrow & 7 = lane & 7)
+        ldmatrix_x4_trans(x0, x1, x2, x3,
+                          TMA ? vs + vrow * 128 + (((2 * m2 + (lane >> 4)) ^ (lane & 7)) << 4)
+                              : vs + vrow * L.v_pitch + m2 * 32 + (lane >> 4) * 16);
         uint32_t a[8];
         const uint32_t xs[4] = {x0, x1, x2, x3};
 #pragma unroll
@@ -525,14 +600,52 @@ __global__ void pq_encode_kernel(const void* x, int x_dtype, int64_t x_sn, const
   else reinterpret_cast<uint8_t*>(codes)[n * M + j] = uint8_t(bi);
 }
 
-template <int VK, bool PAGED, bool OUTL, int D>
-int launch_pq(const PqParams& p, cudaStream_t st) {
-  const PqSmem L = pq_smem(VK, p.M, p.K, OUTL ? p.C : 0, D, p.Mv);
-  size_t smem = size_t(L.lut_bytes) + size_t(kPStages) * L.stage + L.recon_bytes;
-  const size_t red = (2 * kPW * 8 + size_t(kPW) * kHC * D) * sizeof(float);
-  smem = std::max(smem, red);
+// Dynamic shared memory of one CTA (the TMA form adds its alignment slack and barriers).
+inline size_t pq_cta_smem(const PqSmem& L, int D, bool tma) {
+  const size_t body = size_t(L.off_stages) + size_t(kPStages) * L.stage + L.recon_bytes + (tma ? 16 + 1024 : 0);
+  return std::max(body, (2 * kPW * 8 + size_t(kPW) * kHC * size_t(D)) * sizeof(float));
+}
+
+// Tensor maps of the TMA form: values [B,Hk,S,D] bytes (128-byte swizzle), codes
+// [B,Hk,S,M] bytes and, for int8 values, the per-token scales [B,Hk,S] f16. Needs 16-byte
+// aligned bases and strides, M a multiple of 16 stored densely, D = 128 and unit-stride scales.
+bool pq_tma_maps(const PqParams& p, int vk, CUtensorMap m[3]) {
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  auto st = [](int64_t bytes, int64_t size, int64_t fallback) -> int64_t { return size > 1 ? bytes : fallback; };
+  const int64_t S = p.S, Hk = p.Hk, B = p.B;
+  if (p.D != 128 || (p.M % 16) || p.c_sm != 1 || !a16(p.v) || !a16(p.codes) || S <= 0) return false;
+  const int64_t v_ss = p.v_ss, v_sh = st(p.v_sh, Hk, v_ss * S), v_sb = st(p.v_sb, B, v_sh * Hk);
+  const int64_t c_ss = p.c_ss, c_sh = st(p.c_sh, Hk, c_ss * S), c_sb = st(p.c_sb, B, c_sh * Hk);
+  for (int64_t x : {v_ss, v_sh, v_sb, c_ss, c_sh, c_sb})
+    if (x <= 0 || x % 16 || x >= (int64_t(1) << 40)) return false;
+  const cuuint64_t dv[4] = {128, cuuint64_t(S), cuuint64_t(Hk), cuuint64_t(B)};
+  const cuuint64_t sv[3] = {cuuint64_t(v_ss), cuuint64_t(v_sh), cuuint64_t(v_sb)};
+  const cuuint32_t bv[4] = {128, uint32_t(kPRows), 1, 1};
+  const cuuint64_t dc[4] = {cuuint64_t(p.M), cuuint64_t(S), cuuint64_t(Hk), cuuint64_t(B)};
+  const cuuint64_t sc[3] = {cuuint64_t(c_ss), cuuint64_t(c_sh), cuuint64_t(c_sb)};
+  const cuuint32_t bc[4] = {uint32_t(p.M), uint32_t(kPRows), 1, 1};
+  if (!encode_map(&m[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, p.v, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map(&m[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, p.codes, dc, sc, bc, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return false;
+  if (vk == V_INT8) {
+    if (p.vs_ss != 1 || !a16(p.vsc)) return false;
+    const int64_t s_sh = st(p.vs_sh * 2, Hk, S * 2), s_sb = st(p.vs_sb * 2, B, s_sh * Hk);
+    if (s_sh % 16 || s_sb % 16 || s_sh <= 0 || s_sb <= 0) return false;
+    const cuuint64_t ds[3] = {cuuint64_t(S), cuuint64_t(Hk), cuuint64_t(B)};
+    const cuuint64_t ss[2] = {cuuint64_t(s_sh), cuuint64_t(s_sb)};
+    const cuuint32_t bs[3] = {uint32_t(kPRows), 1, 1};
+    if (!encode_map(&m[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, p.vsc, ds, ss, bs, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return false;
+  }
+  return true;
+}
+
+template <int VK, bool PAGED, bool OUTL, int D, bool TMA>
+int launch_pq_as(const PqParams& p, const CUtensorMap* maps, cudaStream_t st) {
+  const PqSmem L = pq_smem(VK, p.M, p.K, OUTL ? p.C : 0, D, p.Mv, TMA);
+  const size_t smem = pq_cta_smem(L, D, TMA);
   if (smem > 225 * 1024) return fail(BD_ERR_UNSUPPORTED, "PQ LUT too large for shared memory (M*K too big)");
-  auto kern = pq_decode_kernel<VK, PAGED, OUTL, D>;
+  auto kern = pq_decode_kernel<VK, PAGED, OUTL, D, TMA>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -543,8 +656,18 @@ int launch_pq(const PqParams& p, cudaStream_t st) {
     attr[dev & 63] = true;
   }
   dim3 grid(p.n_splits, p.Hk * p.head_chunks, p.B);
-  kern<<<grid, kPW * 32, smem, st>>>(p);
+  kern<<<grid, kPW * 32, smem, st>>>(p, maps[0], maps[1], maps[2]);
   return cuda_check(cudaGetLastError(), "pq_decode_kernel launch");
+}
+
+template <int VK, bool PAGED, bool OUTL, int D>
+int launch_pq(const PqParams& p, cudaStream_t st) {
+  alignas(64) CUtensorMap maps[3];
+  std::memset(maps, 0, sizeof maps);
+  if constexpr (!PAGED && !OUTL && D == 128 && (VK == V_INT8 || VK == V_FP8)) {
+    if (pq_tma_maps(p, VK, maps)) return launch_pq_as<VK, false, false, D, true>(p, maps, st);
+  }
+  return launch_pq_as<VK, PAGED, OUTL, D, false>(p, maps, st);
 }
 
 template <int VK, int D>
@@ -643,8 +766,8 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
   const int64_t ntiles = (S + kPRows - 1) / kPRows;
   const int64_t pairs = B * Hk * head_chunks;
   // resident CTAs per SM from the shared-memory footprint (227 KB usable per SM)
-  const size_t cta_smem = std::max(size_t(Ls.lut_bytes) + size_t(kPStages) * Ls.stage + Ls.recon_bytes,
-                                   (2 * kPW * 8 + size_t(kPW) * kHC * size_t(D)) * sizeof(float)) + 1024;
+  const PqSmem Lt = pq_smem(vk, int(M), int(K), 0, int(D), int(Mv), true);
+  const size_t cta_smem = std::max(pq_cta_smem(Ls, int(D), false), pq_cta_smem(Lt, int(D), true)) + 1024;
   const int64_t per_sm = std::max<int64_t>(1, std::min<int64_t>(2, int64_t(227 * 1024) / int64_t(cta_smem)));
   const int64_t slots = per_sm * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / pairs;

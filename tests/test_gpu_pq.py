@@ -177,6 +177,23 @@ def test_pq_lut_int8v_config2(cuda, B, Hq, Hk, S):
     close(out, oracle.decode_attn_pq_lut_int8v(lut, codes, v8, vs))
 
 
+@pytest.mark.parametrize("M,code_pitch", [(8, 8), (16, 32), (32, 32)])
+def test_pq_lut_int8v_code_layouts(cuda, M, code_pitch):
+    """Subspace counts and code-row pitches on both tile paths: codes of 16 or 32 bytes in
+    16-byte-multiple rows take tensor-map (TMA) loads, 8-byte codes the per-thread copies."""
+    g = gen(100 + M + code_pitch)
+    B, Hq, Hk, S, D, K = 2, 8, 2, 700, 128, 256
+    cent = torch.randn(M, K, D // M, generator=g).half().float()
+    codes = torch.randint(0, K, (B, Hk, S, M), generator=g).to(torch.uint8)
+    lut = oracle.pq_lut(torch.randn(B, Hq, D, generator=g) / math.sqrt(D), cent)
+    v8 = torch.randint(-127, 128, (B, Hk, S, D), generator=g).to(torch.int8)
+    vs = (torch.rand(B, Hk, S, generator=g) * 0.02 + 0.001).half()
+    buf = torch.zeros(B, Hk, S, code_pitch, dtype=torch.uint8, device=cuda)
+    buf[..., :M] = codes.to(cuda)
+    out = ak.decode_attn_pq_lut_int8v(lut.to(cuda), buf[..., :M], v8.to(cuda), vs.to(cuda))
+    close(out, oracle.decode_attn_pq_lut_int8v(lut, codes, v8, vs))
+
+
 def test_sparse_pq_lut_scores_and_pipeline(cuda):
     g = gen(9)
     B, Hq, Hk, S, D = 2, 8, 2, 512, 128
