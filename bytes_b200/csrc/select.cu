@@ -384,6 +384,160 @@ __global__ void __launch_bounds__(kTkThreads, 1) topk_fast_kernel(const TopkPara
   }
 }
 
+// ---- short rows (n <= kSmRowMax): one 256-thread CTA per row, each thread holding a
+// contiguous run of up to kSmPer keys in registers. Four 8-bit MSB-first radix passes find
+// the k-th key T and how many keys equal to T to keep; two block scans then give every
+// selected key its output slot in index order (lower index first among equal keys), and
+// sorted output is a bitonic sort of those k entries in shared memory.
+constexpr int kSmThreads = 256;
+constexpr int kSmWarps = kSmThreads / 32;
+constexpr int kSmPer = 16;
+constexpr int kSmRowMax = kSmThreads * kSmPer;
+constexpr int kSmSortMax = 1024;  // largest k with sorted output on this path
+
+// Exclusive scan of one int per thread over kSmWarps warps; *total receives the sum.
+__device__ __forceinline__ int small_excl_scan(int v, int* red, int* total) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int x = lane < kSmWarps ? red[lane] : 0;
+    int wi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    if (lane < kSmWarps) red[lane] = wi - x;
+    if (lane == kSmWarps - 1) red[32] = wi;
+  }
+  __syncthreads();
+  const int r = red[warp] + incl - v;
+  *total = red[32];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kSmThreads) topk_small_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];  // sorted output: [kpow] keys, [kpow] indices
+  __shared__ int hist[256];
+  __shared__ int red[33];
+  __shared__ int s_digit, s_above;
+  const int row = blockIdx.x;
+  const float* src = p.scores + int64_t(row / p.rows_per_b) * p.b_stride + int64_t(row % p.rows_per_b) * p.row_stride;
+  const int n = p.n, k = min(p.k, p.n);
+  if (k <= 0) return;
+  const int per = (n + kSmThreads - 1) / kSmThreads;
+  const int i0 = int(threadIdx.x) * per;
+  uint32_t key[kSmPer];
+  const bool vec = (per % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+#pragma unroll
+  for (int e = 0; e < kSmPer; e += 4) {
+    if (vec && e < per && i0 + e + 3 < n) {
+      const float4 x = *reinterpret_cast<const float4*>(src + i0 + e);
+      key[e] = f2key(x.x); key[e + 1] = f2key(x.y); key[e + 2] = f2key(x.z); key[e + 3] = f2key(x.w);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) key[e + u] = (e + u < per && i0 + e + u < n) ? f2key(src[i0 + e + u]) : 0u;
+    }
+  }
+  auto valid = [&](int e) { return e < per && i0 + e < n; };
+
+  // ---- radix select of the k-th largest key
+  uint32_t prefix = 0, mask = 0;
+  int remaining = k;
+  if (k < n) {
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      hist[threadIdx.x] = 0;
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < kSmPer; ++e)
+        if (valid(e) && (key[e] & mask) == prefix) atomicAdd(&hist[(key[e] >> shift) & 255u], 1);
+      __syncthreads();
+      const int d = 255 - int(threadIdx.x);  // thread t owns digit 255 - t: the scan counts higher digits
+      const int c = hist[d];
+      int tot;
+      const int above = small_excl_scan(c, red, &tot);
+      if (above < remaining && above + c >= remaining) { s_digit = d; s_above = above; }
+      __syncthreads();
+      prefix |= uint32_t(s_digit) << shift;
+      mask |= 0xffu << shift;
+      remaining -= s_above;
+      __syncthreads();
+    }
+  }
+  // ---- keep every key above T and the first `remaining` keys equal to T (index order)
+  int eq = 0;
+#pragma unroll
+  for (int e = 0; e < kSmPer; ++e) eq += (k < n && valid(e) && key[e] == prefix) ? 1 : 0;
+  int tot;
+  int eq_rank = small_excl_scan(eq, red, &tot);
+  uint32_t selbits = 0;
+  int nsel = 0;
+#pragma unroll
+  for (int e = 0; e < kSmPer; ++e) {
+    bool sel = false;
+    if (valid(e)) {
+      if (k >= n || key[e] > prefix) sel = true;
+      else if (key[e] == prefix) sel = eq_rank++ < remaining;
+    }
+    selbits |= uint32_t(sel) << e;
+    nsel += sel;
+  }
+  int pos = small_excl_scan(nsel, red, &tot);
+  uint32_t* wk = reinterpret_cast<uint32_t*>(smem);
+  int kpow = 1;
+  while (kpow < max(k, 1)) kpow <<= 1;
+  int* wi = reinterpret_cast<int*>(smem + size_t(kpow) * 4);
+#pragma unroll
+  for (int e = 0; e < kSmPer; ++e) {
+    if (!((selbits >> e) & 1u)) continue;
+    const int idx = i0 + e;
+    if (p.sorted) {
+      wk[pos] = key[e];
+      wi[pos] = idx;
+    } else {
+      if (p.vals) p.vals[int64_t(row) * p.v_rs + pos] = key2f(key[e]);
+      if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + pos] = idx;
+      else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + pos] = idx;
+    }
+    ++pos;
+  }
+  if (!p.sorted) return;
+  for (int i = k + threadIdx.x; i < kpow; i += kSmThreads) { wk[i] = 0u; wi[i] = 0x7fffffff; }
+  __syncthreads();
+  // ---- bitonic sort of kpow entries (key desc, index asc); padding sorts last
+  for (int size = 2; size <= kpow; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int t = threadIdx.x; t < kpow / 2; t += kSmThreads) {
+        const int lo = 2 * t - (t & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc_block = ((lo & size) == 0);
+        const uint32_t ka = wk[lo], kb = wk[hi];
+        const int ia = wi[lo], ib = wi[hi];
+        const bool a_first = (ka > kb) || (ka == kb && ia < ib);
+        if (a_first != desc_block) {
+          wk[lo] = kb; wk[hi] = ka;
+          wi[lo] = ib; wi[hi] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int o = threadIdx.x; o < k; o += kSmThreads) {
+    if (p.vals) p.vals[int64_t(row) * p.v_rs + o] = key2f(wk[o]);
+    if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + o] = wi[o];
+    else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + o] = wi[o];
+  }
+}
+
 template <bool SMEM_ROW>
 __global__ void __launch_bounds__(kTkThreads, 1) topk_kernel(const TopkParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -548,6 +702,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) topk_kernel(const TopkParams p)
 }
 
 // ------------------------------------------------------------------ gather-attend
+constexpr int kGatherChunk = 1024;  // split positions staged in shared memory at a time
+
 struct GatherParams {
   const void* q; int64_t q_sb, q_sh; int q_dtype;
   const uint8_t* k; int64_t k_sb, k_sh, k_ss;
@@ -595,33 +751,30 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
     return p.idx64 ? reinterpret_cast<const int64_t*>(p.idx)[off] : int64_t(reinterpret_cast<const int32_t*>(p.idx)[off]);
   };
   constexpr int WPL = CPL * ELT / 4;  // 32-bit words per lane per row (1, 2, 4 or 8)
-  // all four 8-lane row groups of a warp iterate together (the shuffles below need every
-  // lane of the warp); a group whose row is past the end is predicated off
-  for (int rw = r_begin + warp * 4; rw < r_end; rw += 16) {
-    const int r = rw + grp;
-    const int64_t t = r < r_end ? row_index(r) : -1;
-    const bool ok = t >= 0 && t < p.S;
-    uint32_t kw[WPL], vw[WPL];
+  // one row's key and value words of this lane (zeros for a masked row)
+  auto load_row = [&](int t, uint32_t (&kw)[WPL], uint32_t (&vw)[WPL]) {
 #pragma unroll
     for (int w = 0; w < WPL; ++w) kw[w] = vw[w] = 0u;
-    if (ok) {
-      const uint8_t* kr = kb_ + t * p.k_ss * ELT;
-      const uint8_t* vr = vb_ + t * p.v_ss * ELT;
-      if (WPL == 1) {
-        kw[0] = __ldg(reinterpret_cast<const uint32_t*>(kr));
-        vw[0] = __ldg(reinterpret_cast<const uint32_t*>(vr));
-      } else if (WPL == 2) {
-        const uint2 a = __ldg(reinterpret_cast<const uint2*>(kr)), c = __ldg(reinterpret_cast<const uint2*>(vr));
-        kw[0] = a.x; kw[1] = a.y; vw[0] = c.x; vw[1] = c.y;
-      } else {
+    if (t < 0) return;
+    const uint8_t* kr = kb_ + int64_t(t) * p.k_ss * ELT;
+    const uint8_t* vr = vb_ + int64_t(t) * p.v_ss * ELT;
+    if (WPL == 1) {
+      kw[0] = __ldg(reinterpret_cast<const uint32_t*>(kr));
+      vw[0] = __ldg(reinterpret_cast<const uint32_t*>(vr));
+    } else if (WPL == 2) {
+      const uint2 a = __ldg(reinterpret_cast<const uint2*>(kr)), c = __ldg(reinterpret_cast<const uint2*>(vr));
+      kw[0] = a.x; kw[1] = a.y; vw[0] = c.x; vw[1] = c.y;
+    } else {
 #pragma unroll
-        for (int u = 0; u < WPL / 4; ++u) {
-          const uint4 a = __ldg(reinterpret_cast<const uint4*>(kr) + u), c = __ldg(reinterpret_cast<const uint4*>(vr) + u);
-          kw[4 * u] = a.x; kw[4 * u + 1] = a.y; kw[4 * u + 2] = a.z; kw[4 * u + 3] = a.w;
-          vw[4 * u] = c.x; vw[4 * u + 1] = c.y; vw[4 * u + 2] = c.z; vw[4 * u + 3] = c.w;
-        }
+      for (int u = 0; u < WPL / 4; ++u) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(kr) + u), c = __ldg(reinterpret_cast<const uint4*>(vr) + u);
+        kw[4 * u] = a.x; kw[4 * u + 1] = a.y; kw[4 * u + 2] = a.z; kw[4 * u + 3] = a.w;
+        vw[4 * u] = c.x; vw[4 * u + 1] = c.y; vw[4 * u + 2] = c.z; vw[4 * u + 3] = c.w;
       }
     }
+  };
+  // dot product with q (8-lane group reduction) and online-softmax update for one row
+  auto consume = [&](bool ok, const uint32_t (&kw)[WPL], const uint32_t (&vw)[WPL]) {
     float kf[CPL], vf[CPL];
 #pragma unroll
     for (int w = 0; w < WPL; ++w) {
@@ -641,21 +794,51 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
         vf[2 * w + 1] = __uint_as_float(vw[w] & 0xffff0000u);
       }
     }
-    float s = 0.f;
+    float sdot = 0.f;
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) s = fmaf(qv[c], kf[c], s);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    if (!ok) continue;  // masked position: contributes nothing (uniform within the 8-lane group)
-    s *= p.scaling;
-    const float mn = fmaxf(m, s);
+    for (int c = 0; c < CPL; ++c) sdot = fmaf(qv[c], kf[c], sdot);
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 4);
+    if (!ok) return;  // masked position: contributes nothing (uniform within the 8-lane group)
+    sdot *= p.scaling;
+    const float mn = fmaxf(m, sdot);
     const float alpha = __expf(m - mn);
-    const float pw = __expf(s - mn);
+    const float pw = __expf(sdot - mn);
     l = l * alpha + pw;
 #pragma unroll
     for (int c = 0; c < CPL; ++c) acc[c] = fmaf(pw, vf[c], acc[c] * alpha);
     m = mn;
+  };
+  // The split's positions come into shared memory a chunk at a time (one coalesced read;
+  // out-of-range or negative positions become -1), then every 8-lane group takes four rows
+  // per step (rows i, i + 16, i + 32, i + 48), all four rows' loads in flight before any
+  // is used.
+  __shared__ int s_pos[kGatherChunk];
+  for (int c0 = r_begin; c0 < r_end; c0 += kGatherChunk) {
+    const int n = min(kGatherChunk, r_end - c0);
+    __syncthreads();  // the previous chunk's readers are done
+    for (int i = threadIdx.x; i < n; i += 128) {
+      const int64_t t = row_index(c0 + i);
+      s_pos[i] = (t >= 0 && t < p.S) ? int(t) : -1;
+    }
+    __syncthreads();
+    // all four 8-lane row groups of a warp iterate together (the shuffles need every lane
+    // of the warp); a group whose row is past the chunk is predicated off
+    for (int i0 = warp * 4; i0 < n; i0 += 64) {
+      const int ia = i0 + grp, ib = ia + 16, ic = ia + 32, id = ia + 48;
+      const int ta = ia < n ? s_pos[ia] : -1, tb = ib < n ? s_pos[ib] : -1;
+      const int tc = ic < n ? s_pos[ic] : -1, td = id < n ? s_pos[id] : -1;
+      uint32_t ka[WPL], va[WPL], kb2[WPL], vb2[WPL], kc[WPL], vc[WPL], kd[WPL], vd[WPL];
+      load_row(ta, ka, va);
+      load_row(tb, kb2, vb2);
+      load_row(tc, kc, vc);
+      load_row(td, kd, vd);
+      consume(ta >= 0, ka, va);
+      consume(tb >= 0, kb2, vb2);
+      consume(tc >= 0, kc, vc);
+      consume(td >= 0, kd, vd);
+    }
   }
   // merge the 16 row groups
   if (sub == 0) { red_m[gid] = m; red_l[gid] = l; }
@@ -869,6 +1052,10 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
   const size_t smem = (in_smem ? size_t(n) * 4 : 0) + wbytes;
   if (smem > 220 * 1024) return fail(BD_ERR_UNSUPPORTED, "top-k: sorted output of this many elements does not fit");
   int rc;
+  if (n > 0 && n <= kSmRowMax && (!sorted || kk <= kSmSortMax)) {
+    topk_small_kernel<<<rows, kSmThreads, sorted ? wbytes : 0, st>>>(p);
+    return cuda_check(cudaGetLastError(), "topk_small_kernel launch");
+  }
   const size_t fast_smem = size_t(n) * 4 + 4096 * 4 + size_t(kCandMax) * 4 + wbytes;
   const bool aligned = (reinterpret_cast<uintptr_t>(scores) & 15) == 0 && row_stride % 4 == 0 &&
                        (rows_per_b >= rows || b_stride % 4 == 0);

@@ -111,6 +111,22 @@ def test_topk_threshold_bucket_overflow(cuda, sorted_):
         _topk_check(s, k, sorted_)
 
 
+@pytest.mark.parametrize("n", [1, 2047, 4096, 4097])
+def test_topk_short_rows(cuda, n):
+    """Row lengths around the short-row kernel's limit (4096 keys held in registers), odd
+    lengths (element loads) and rows that start off a 16-byte boundary."""
+    g = gen(n)
+    full = torch.randint(-20, 20, (33, n + 1), generator=g).float()
+    dev = full.to(cuda)[:, 1:]  # rows start 4 bytes past a 16-byte boundary
+    s = full[:, 1:].contiguous()
+    for k in sorted({1, min(n, 64), min(n, 1024), n}):
+        rv, ri = oracle.topk_lower_index(s, k)
+        v, i = ak.topk(dev, k, sorted=True)
+        assert torch.equal(i.cpu(), ri) and torch.equal(v.cpu(), rv)
+        _, i = ak.topk(dev, k, sorted=False)
+        assert torch.equal(i.cpu(), ri.sort(-1).values)
+
+
 def test_topk_3d_rows(cuda):
     g = gen(3)
     s = torch.randn(2, 8, 3000, generator=g)
