@@ -53,7 +53,11 @@ struct DenseParams {
   // 1 (with pdl, one split): after that wait, merge partial slots [0, split_offset) of each
   // row with this CTA's own result and write `out`
   int merge;
+  int smem_bytes;  // dynamic shared memory of the launch (the merge stages the slot rows there)
 };
+
+// merge-mode bulk copies whose barrier wait ran past its limit (a result is then wrong)
+__device__ unsigned int g_merge_timeouts = 0;
 
 template <typename T>
 __device__ __forceinline__ float ldq(const void* base, int64_t off) {
@@ -352,6 +356,21 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
     constexpr int TPH = kWarps * 32 / NH;
     float* wts = red_o + kWarps * NH * D;  // [NH][n + 1]; slot n = this CTA
     float* sl = wts + NH * (n + 1);        // [NH] total sums
+    // The group's rows are consecutive, so all their slots form one block of
+    // nheads * split_stride * D floats: one bulk copy brings it into shared memory while
+    // the weights are computed (when it fits; else the slots are read from global memory).
+    const int64_t row0 = int64_t(b) * p.Hq + hk * p.G + h0;
+    const uint32_t blk_off = (uint32_t((reinterpret_cast<uint8_t*>(sl + NH) - smem)) + 15u) & ~15u;
+    const uint32_t blk_bytes = uint32_t(nheads) * uint32_t(p.split_stride) * uint32_t(D) * 4u;
+    const bool staged = blk_off + blk_bytes + 8u <= uint32_t(p.smem_bytes);
+    const float* ob = reinterpret_cast<const float*>(smem + blk_off);
+    const uint32_t mbar = smem_u32(smem + blk_off + blk_bytes);
+    if (staged && threadIdx.x == 0) {
+      mbar_init(mbar, 1);
+      mbar_fence_init();
+      mbar_arrive_expect_tx(mbar, blk_bytes);
+      bulk_load(smem_u32(smem + blk_off), p.part_o + row0 * p.split_stride * D, blk_bytes, mbar);
+    }
     {
       const int h = threadIdx.x / TPH, part = threadIdx.x % TPH;
       const int hq = hk * p.G + h0 + min(h, nheads - 1);
@@ -383,6 +402,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
         sl[h] = L + Lo * wo;
       }
     }
+    if (staged && !mbar_wait(mbar, 0) && threadIdx.x == 0) atomicAdd(&g_merge_timeouts, 1u);
     __syncthreads();
     constexpr int C4 = D / 4;
     for (int idx = threadIdx.x; idx < nheads * C4; idx += kWarps * 32) {
@@ -398,12 +418,22 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
       }
       const float wo = wr[n];
       O.x *= wo; O.y *= wo; O.z *= wo; O.w *= wo;
-      const float* orow = p.part_o + row * p.split_stride * D + c;
+      if (staged) {
+        const float* orow = ob + int64_t(h) * p.split_stride * D + c;
 #pragma unroll 6
-      for (int s = 0; s < n; ++s) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(orow + int64_t(s) * D));
-        const float w = wr[s];
-        O.x = fmaf(v.x, w, O.x); O.y = fmaf(v.y, w, O.y); O.z = fmaf(v.z, w, O.z); O.w = fmaf(v.w, w, O.w);
+        for (int s = 0; s < n; ++s) {
+          const float4 v = *reinterpret_cast<const float4*>(orow + s * D);
+          const float w = wr[s];
+          O.x = fmaf(v.x, w, O.x); O.y = fmaf(v.y, w, O.y); O.z = fmaf(v.z, w, O.z); O.w = fmaf(v.w, w, O.w);
+        }
+      } else {
+        const float* orow = p.part_o + row * p.split_stride * D + c;
+#pragma unroll 6
+        for (int s = 0; s < n; ++s) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(orow + int64_t(s) * D));
+          const float w = wr[s];
+          O.x = fmaf(v.x, w, O.x); O.y = fmaf(v.y, w, O.y); O.z = fmaf(v.z, w, O.z); O.w = fmaf(v.w, w, O.w);
+        }
       }
       const float inv = 1.f / sl[h];
       const int64_t off = int64_t(b) * p.o_sb + int64_t(hq) * p.o_sh + c;
@@ -581,6 +611,8 @@ int launch_dense(const DenseParams& p, const Plan& pl, cudaStream_t st) {
   size_t red = (2 * kWarps * 8 * NT + size_t(kWarps) * 8 * NT * D) * sizeof(float);
   if (p.merge) red += (size_t(8 * NT) * (p.split_offset + 1) + 8 * NT) * sizeof(float);
   smem = std::max(smem, red);
+  DenseParams q = p;
+  q.smem_bytes = int(smem);
   auto kern = dense_decode_kernel<D, NT, FP8>;
   static size_t attr_set[64] = {0};  // dynamic shared memory allowed so far, per device
   int dev = 0;
@@ -592,8 +624,8 @@ int launch_dense(const DenseParams& p, const Plan& pl, cudaStream_t st) {
     attr_set[dev & 63] = smem;
   }
   dim3 grid(pl.n_splits, p.Hk * pl.head_chunks, p.B);
-  if (p.pdl) return launch_programmatic(kern, grid, dim3(kWarps * 32), smem, st, p, "dense_decode_kernel launch");
-  kern<<<grid, kWarps * 32, smem, st>>>(p);
+  if (p.pdl) return launch_programmatic(kern, grid, dim3(kWarps * 32), smem, st, q, "dense_decode_kernel launch");
+  kern<<<grid, kWarps * 32, smem, st>>>(q);
   return cuda_check(cudaGetLastError(), "dense_decode_kernel launch");
 }
 
