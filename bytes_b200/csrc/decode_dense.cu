@@ -592,6 +592,9 @@ int make_plan(const bd_tensor* q, const bd_tensor* k, Plan* pl, int target_ctas 
   int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
   int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;
+  // at least 4 tiles (256 tokens) per split unless the caller fixed the CTA count: a short
+  // context then keeps fewer, fuller splits, and the merge reads fewer partial rows
+  if (target_ctas <= 0) tps = std::min<int64_t>(std::max<int64_t>(tps, 4), std::max<int64_t>(ntiles, 1));
   splits = ntiles > 0 ? (ntiles + tps - 1) / tps : 1;
   pl->n_splits = int(splits);
   pl->tiles_per_split = int(tps);
