@@ -296,6 +296,29 @@ def gather_attn(q3, k, v, idx, scaling, out):
     return out
 
 
+def gather_attn_partial(q3, k, v, idx, scaling):
+    """Shard partials (m, l, o) of gather-attend over this device's positions in idx."""
+    N.require_cuda(q3, k, v, idx)
+    k, v = rows_aligned(k), rows_aligned(v)
+    q3 = inner_contig(q3)
+    idx = inner_contig(idx)
+    if idx.dtype not in (torch.int32, torch.int64):
+        idx = idx.long()
+    B, Hq, D = q3.shape
+    m = torch.empty(B, Hq, dtype=torch.float32, device=q3.device)
+    l = torch.empty_like(m)
+    o = torch.empty(B, Hq, D, dtype=torch.float32, device=q3.device)
+    dq, di = N.desc(q3), N.desc(idx)
+    nws = _fn("bd_sparse_gather_attn_workspace", [P, P], SZ)(ctypes.byref(dq), ctypes.byref(di))
+    buf, nb = _ws(nws, q3.device)
+    dk, dv, dm, dl, dO = N.desc(k), N.desc(v), N.desc(m), N.desc(l), N.desc(o)
+    rc = _fn("bd_sparse_gather_attn_partial", [P, P, P, P, F, P, P, P, VP, SZ, VP])(
+        ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(di), float(scaling), ctypes.byref(dm),
+        ctypes.byref(dl), ctypes.byref(dO), _ptr(buf), nb, N.stream_of(q3))
+    N.check(rc, "bd_sparse_gather_attn_partial")
+    return m, l, o
+
+
 def quest_page_minmax(k, page):
     N.require_cuda(k)
     k = inner_contig(k)

@@ -727,6 +727,16 @@ int launch_dense_merge(const bd_tensor* q, const bd_tensor* k, const bd_tensor* 
   return dispatch_dense(p, pl, st);
 }
 
+int launch_combine_export(const Partials& part, int B, int Hq, int D, float* em, float* el, float* eo,
+                          cudaStream_t st, bool pdl) {
+  CombineParams c{};
+  c.m = part.m; c.l = part.l; c.o = part.o;
+  c.rows = B * Hq; c.n = part.nsplit; c.D = D; c.Hq = Hq; c.ms_rows = 1;
+  c.mode = 1;
+  c.em = em; c.el = el; c.eo = eo;
+  return launch_combine_kernel(c, st, pdl);
+}
+
 int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st, bool pdl) {
   CombineParams c{};
   c.m = part.m; c.l = part.l; c.o = part.o;

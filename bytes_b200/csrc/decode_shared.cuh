@@ -44,6 +44,10 @@ int launch_dense_merge(const bd_tensor* q, const bd_tensor* k, const bd_tensor* 
 
 // Final merge of all splits in `part` into out [B,Hq,D] (bf16/f16/f32). pdl: launch as a
 // programmatic dependent; the kernel waits for its predecessor before reading partials.
+// Merge of the split partials exported as one (m, l, o) per row: m,l [B*Hq] (m in natural-log
+// units of scaling*q.k), o [B*Hq,D] un-normalised — the shard partial of a split-KV exchange.
+int launch_combine_export(const Partials& part, int B, int Hq, int D, float* em, float* el, float* eo,
+                          cudaStream_t st, bool pdl);
 int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st,
                    bool pdl = false);
 

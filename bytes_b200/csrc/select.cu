@@ -1164,13 +1164,19 @@ size_t bd_sparse_gather_attn_workspace(const bd_tensor* q, const bd_tensor* idx)
   return partials_bytes(size_t(rows), gather_splits(rows, idx->shape[2]), int(q->shape[2]));
 }
 
-int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
-                          float scaling, const bd_tensor* out, void* workspace, size_t workspace_bytes,
-                          bd_stream_t stream) {
+// Gather-attend over idx into split partials, then either the final output (`out`) or one
+// exported (m, l, o) per row (`em`, `el`, `eo`: the shard partial of a multi-GPU exchange).
+static int sparse_gather_run(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
+                             float scaling, const bd_tensor* out, const bd_tensor* em, const bd_tensor* el,
+                             const bd_tensor* eo, void* workspace, size_t workspace_bytes, bd_stream_t stream) {
   using namespace bd;
   int rc;
   if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(k, "k", 4)) || (rc = check_tensor(v, "v", 4)) ||
-      (rc = check_tensor(idx, "idx", 3)) || (rc = check_tensor(out, "out", 3)))
+      (rc = check_tensor(idx, "idx", 3)))
+    return rc;
+  if (out ? (rc = check_tensor(out, "out", 3))
+          : ((rc = check_tensor(em, "m", 2, BD_F32)) || (rc = check_tensor(el, "l", 2, BD_F32)) ||
+             (rc = check_tensor(eo, "o", 3, BD_F32))))
     return rc;
   if (k->dtype != v->dtype || (k->dtype != BD_BF16 && k->dtype != BD_F8E4M3))
     return fail(BD_ERR_DTYPE, "k and v must both be bf16 or both fp8 e4m3");
@@ -1184,8 +1190,16 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
     if (k->shape[i] != v->shape[i]) return fail(BD_ERR_SHAPE, "k and v shapes differ");
   if (k->shape[0] != B || k->shape[3] != D || idx->shape[0] != B || idx->shape[1] != Hq)
     return fail(BD_ERR_SHAPE, "expect q [B,Hq,D], k/v [B,Hk,S,D], idx [B,Hq,kb]");
-  if (out->shape[0] != B || out->shape[1] != Hq || out->shape[2] != D || out->stride[2] != 1)
+  if (out && (out->shape[0] != B || out->shape[1] != Hq || out->shape[2] != D || out->stride[2] != 1))
     return fail(BD_ERR_SHAPE, "out must be [B,Hq,D] with contiguous rows");
+  if (!out) {
+    if (em->shape[0] != B || em->shape[1] != Hq || el->shape[0] != B || el->shape[1] != Hq || eo->shape[0] != B ||
+        eo->shape[1] != Hq || eo->shape[2] != D)
+      return fail(BD_ERR_SHAPE, "m,l must be [B,Hq] and o [B,Hq,D]");
+    if (em->stride[1] != 1 || em->stride[0] != Hq || el->stride[1] != 1 || el->stride[0] != Hq ||
+        eo->stride[2] != 1 || eo->stride[1] != D || eo->stride[0] != Hq * D)
+      return fail(BD_ERR_STRIDE, "m, l, o must be contiguous");
+  }
   if (idx->stride[2] != 1 && kb > 1) return fail(BD_ERR_STRIDE, "idx rows must be contiguous");
   if (q->stride[2] != 1) return fail(BD_ERR_STRIDE, "q innermost dim must be contiguous");
   if ((rc = check_rows_aligned(k, "k")) || (rc = check_rows_aligned(v, "v"))) return rc;
@@ -1219,7 +1233,24 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
     else gather_attn_kernel<32, false><<<grid, 128, 0, st>>>(p);
   }
   if ((rc = cuda_check(cudaGetLastError(), "gather_attn_kernel launch"))) return rc;
-  return launch_combine(part, int(B), int(Hq), int(D), out, st, true);
+  if (out) return launch_combine(part, int(B), int(Hq), int(D), out, st, true);
+  return launch_combine_export(part, int(B), int(Hq), int(D), static_cast<float*>(em->data),
+                               static_cast<float*>(el->data), static_cast<float*>(eo->data), st, true);
+}
+
+
+int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
+                          float scaling, const bd_tensor* out, void* workspace, size_t workspace_bytes,
+                          bd_stream_t stream) {
+  if (!out) return bd::fail(BD_ERR_NULL, "out is NULL");
+  return sparse_gather_run(q, k, v, idx, scaling, out, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int bd_sparse_gather_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, const bd_tensor* idx,
+                                  float scaling, const bd_tensor* m, const bd_tensor* l, const bd_tensor* o,
+                                  void* workspace, size_t workspace_bytes, bd_stream_t stream) {
+  if (!m || !l || !o) return bd::fail(BD_ERR_NULL, "m, l or o is NULL");
+  return sparse_gather_run(q, k, v, idx, scaling, nullptr, m, l, o, workspace, workspace_bytes, stream);
 }
 
 int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, const bd_tensor* kmax,

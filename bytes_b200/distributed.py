@@ -9,6 +9,12 @@ One process per GPU (torch.distributed, NCCL over NVLink/NVSwitch).
   partials with one split-KV kernel, the ranks all-gather those partials (B*Hq*(D+2)
   floats per rank, ~14.6 KB for 28 heads x 128 dims), and every rank merges them with a
   log-sum-exp combine kernel, so all ranks end with the full attention output.
+* Exact top-k sparse decode over such a sharded sequence: each rank scores its shard and
+  keeps its own top-kb (value, global position) pairs; one all-gather of those pairs lets
+  every rank pick the same global top-kb (value descending, lower position first on
+  ties — the single-GPU rule, since the union of the shard top-kb sets holds the global
+  top-kb); each rank gather-attends over the winners inside its shard and one more
+  all-gather of (max, sum, numerator) partials feeds the same combine.
 
 The reference is single-GPU; this module has no counterpart there. The merge is the same
 online-softmax identity its kernels apply across key blocks
@@ -62,3 +68,76 @@ def split_kv_decode(q, k_shard, v_shard, scaling, group=None, partial_fn=None, m
     l_all = g[:, n_ml:2 * n_ml].reshape(world, B, Hq)
     o_all = g[:, 2 * n_ml:].reshape(world, B, Hq, D)
     return merge_fn(m_all, l_all, o_all, out_dtype)
+
+
+def _shard_scores(q, k_shard, scaling):
+    from . import attention_kernels as ak
+    return ak.sparse_score_scalar(q if q.dim() == 4 else q.unsqueeze(2), k_shard, scaling, score_bits=16)
+
+
+def _shard_topk(scores, k):
+    return _ops.topk(scores, k, sorted=True, want_values=True, idx_dtype=torch.int64)
+
+
+def _shard_gather_partial(q, k_shard, v_shard, idx_local, scaling):
+    if q.dim() == 4:
+        q = q[:, :, 0, :]
+    return _ops.gather_attn_partial(q, k_shard, v_shard, idx_local, scaling)
+
+
+def global_topk_merge(vals_all, pos_all, kb):
+    """Top-kb of per-shard candidates: vals_all, pos_all [n, B, Hq, kc] (pos global) ->
+    pos [B, Hq, kb], ordered by value descending, lower position first among equals."""
+    n, B, Hq, kc = vals_all.shape
+    v = vals_all.permute(1, 2, 0, 3).reshape(B, Hq, n * kc)
+    p = pos_all.permute(1, 2, 0, 3).reshape(B, Hq, n * kc)
+    # stable two-key order: sort by position, then stably by value descending
+    order = torch.argsort(p, dim=-1, stable=True)
+    v, p = torch.gather(v, -1, order), torch.gather(p, -1, order)
+    order = torch.argsort(v, dim=-1, descending=True, stable=True)
+    return torch.gather(p, -1, order)[..., :kb]
+
+
+def split_kv_sparse_decode(q, k_shard, v_shard, kb, scaling, shard_start, seq_len, group=None, score_fn=None,
+                           topk_fn=None, partial_fn=None, merge_fn=None, out_dtype=torch.bfloat16):
+    """Exact top-kb sparse decode of q over a sequence sharded along its tokens.
+
+    Every rank passes its own contiguous token shard starting at global position
+    `shard_start` (of `seq_len`); every rank returns the full output [B,Hq,1,D], equal to
+    the single-GPU pipeline (scores -> top-kb -> gather-attend) over the whole sequence.
+    Two all-gathers: B*Hq*kb (value, position) pairs, then B*Hq*(D+2) partial floats.
+    The four kernel steps are parameters so the exchange runs on CPU ranks too.
+    """
+    import torch.distributed as dist
+    score_fn = score_fn or _shard_scores
+    topk_fn = topk_fn or _shard_topk
+    partial_fn = partial_fn or _shard_gather_partial
+    merge_fn = merge_fn or merge_partials
+    world = dist.get_world_size(group)
+    S_loc = k_shard.shape[2]
+    kc = min(kb, S_loc)
+    scores = score_fn(q, k_shard, scaling)  # [B, Hq, S_loc] fp32
+    vals, idx = topk_fn(scores, kc)
+    pos = idx.long() + shard_start
+    B, Hq = vals.shape[:2]
+    # shards shorter than kb pad with -inf / sentinel positions that never win
+    if kc < kb:
+        pad = kb - kc
+        vals = torch.cat([vals.float(), vals.new_full((B, Hq, pad), float("-inf"), dtype=torch.float32)], -1)
+        pos = torch.cat([pos, pos.new_full((B, Hq, pad), seq_len)], -1)
+    vals_all = [torch.empty_like(vals, dtype=torch.float32) for _ in range(world)]
+    pos_all = [torch.empty_like(pos) for _ in range(world)]
+    dist.all_gather(vals_all, vals.float().contiguous(), group=group)
+    dist.all_gather(pos_all, pos.contiguous(), group=group)
+    win = global_topk_merge(torch.stack(vals_all), torch.stack(pos_all), kb)  # [B, Hq, kb] global
+    local = win - shard_start
+    local = torch.where((local >= 0) & (local < S_loc), local, torch.full_like(local, -1))
+    m, l, o = partial_fn(q, k_shard, v_shard, local, scaling)
+    D = o.shape[-1]
+    flat = torch.cat([m.reshape(-1), l.reshape(-1), o.reshape(-1)]).contiguous()
+    parts = [torch.empty_like(flat) for _ in range(world)]
+    dist.all_gather(parts, flat, group=group)
+    g = torch.stack(parts)
+    n_ml = B * Hq
+    return merge_fn(g[:, :n_ml].reshape(world, B, Hq), g[:, n_ml:2 * n_ml].reshape(world, B, Hq),
+                    g[:, 2 * n_ml:].reshape(world, B, Hq, D), out_dtype)

@@ -202,6 +202,18 @@ int bd_sparse_gather_attn(const bd_tensor* q, const bd_tensor* k, const bd_tenso
                           float scaling, const bd_tensor* out, void* workspace, size_t workspace_bytes,
                           bd_stream_t stream);
 
+/* Shard step of a sparse decode whose keys are split across GPUs: the same gather-attend
+ * over this device's selected positions (others -1 or out of range), exported as one
+ * (m, l, o) per (b, q-head) for bd_lse_combine after an all-gather -- m,l [B,Hq] f32
+ * (m in natural-log units of scaling*q.k), o [B,Hq,D] f32 un-normalised, all contiguous.
+ * Same workspace as bd_sparse_gather_attn.
+ * ref: no single counterpart -- the reference is single-GPU; this is attend_topk
+ *      (benchmarks/sparse_attention.py:367) cut at a shard of the positions. */
+int bd_sparse_gather_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v,
+                                  const bd_tensor* idx, float scaling, const bd_tensor* m, const bd_tensor* l,
+                                  const bd_tensor* o, void* workspace, size_t workspace_bytes,
+                                  bd_stream_t stream);
+
 /* Quest page metadata: elementwise min / max of each page of `page` tokens
  * (a ragged last page covers the real tokens only). k [B,H,S,D]; kmin, kmax
  * [B,H,ceil(S/page),D] in k's dtype, channels contiguous, other strides free -- so a

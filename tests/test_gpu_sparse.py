@@ -238,3 +238,36 @@ def test_select_topk_exact_matches_oracle(cuda):
     idx_o = oracle.select_topk_exact(q, keys, S, kb, 0.17)
     agree = (idx.cpu().sort(-1).values == idx_o.sort(-1).values).float().mean().item()
     assert agree > 0.97
+
+
+def test_sharded_sparse_decode_matches_single_device(cuda):
+    """The kernels of the cross-GPU sparse decode, with two shards emulated on one device:
+    per-shard scores and top-kb, the global pick, per-shard gather partials
+    (bd_sparse_gather_attn_partial) and the combine equal the single-device pipeline."""
+    from bytes_b200 import _ops
+    from bytes_b200 import distributed as bdist
+    g = gen(21)
+    B, Hq, Hk, S, D, kb, sc = 2, 8, 2, 1500, 128, 100, 0.088
+    q = torch.randn(B, Hq, 1, D, generator=g).bfloat16().to(cuda)
+    k = torch.randn(B, Hk, S, D, generator=g).bfloat16().to(cuda)
+    v = torch.randn(B, Hk, S, D, generator=g).bfloat16().to(cuda)
+    k[:, :, 1200] = k[:, :, 30]  # a tie across the shard boundary
+    full_scores = ak.sparse_score_scalar(q, k, sc, score_bits=16)
+    _, idx = ak.topk(full_scores, kb, sorted=True)
+    ref = ak.sparse_gather_attn(q, k, v, idx, sc)
+    cut = 700
+    vals, poss, shards = [], [], [(0, cut), (cut, S)]
+    for s0, s1 in shards:
+        s_ = ak.sparse_score_scalar(q, k[:, :, s0:s1], sc, score_bits=16)
+        v_, i_ = ak.topk(s_, kb, sorted=True)
+        vals.append(v_.float()); poss.append(i_.long() + s0)
+    win = bdist.global_topk_merge(torch.stack(vals), torch.stack(poss), kb)
+    assert torch.equal(win.sort(-1).values, idx.long().sort(-1).values)
+    ms, ls, os_ = [], [], []
+    for s0, s1 in shards:
+        loc = win - s0
+        loc = torch.where((loc >= 0) & (loc < s1 - s0), loc, torch.full_like(loc, -1))
+        m, l, o = _ops.gather_attn_partial(q[:, :, 0], k[:, :, s0:s1], v[:, :, s0:s1], loc, sc)
+        ms.append(m); ls.append(l); os_.append(o)
+    out = _ops.lse_combine(torch.stack(ms), torch.stack(ls), torch.stack(os_), torch.bfloat16)
+    close(out.unsqueeze(2), ref, max_abs=1e-2, mean_abs=1e-4)
