@@ -356,7 +356,54 @@ def path_topk(dev, peak, g):
                            "GBps": round(rows * n * 4 / us_tk / 1e3, 1)}}
 
 
-PATHS = {"c0": path_c0, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3, "topk": path_topk}
+def path_c4(dev, peak, g):
+    """c4 (8-GPU box), one GPU's share: 8 sequences x 131072 tokens with the c1 head shapes
+    (28/4, D=128) as bf16 and as KIVI-2; and one rank's shard of a 1M-token sequence split
+    8 ways (B=1, 131072 tokens): its split-KV partial, then the combine of 8 shard partials
+    (the partials of this shard stand in for the all-gather's result on one GPU)."""
+    from bytes_b200 import attention_kernels as ak, kivi as kv, _ops
+    out = {}
+    D, S = 128, 131072
+    q = torch.randn(8, 28, 1, D, device=dev, generator=g).bfloat16()
+    k = torch.randn(8, 4, S, D, device=dev, generator=g).bfloat16()
+    v = torch.randn(8, 4, S, D, device=dev, generator=g).bfloat16()
+    gr = graph_of([lambda: ak.decode_attn_bf16(q, k, v)])
+    time_graph(gr, 2)
+    us = time_graph(gr, 10) / 10
+    b = nbytes(k, v)
+    out["c4_bf16_131k_B8"] = {"us": round(us, 2), "GBps": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 3)}
+    del k, v, gr
+    torch.cuda.empty_cache()
+    c = dict(CFG1, S=S)
+    s = kivi_inputs(dev, 4242, c)
+    gr = graph_of([lambda: kv.kivi_decode_attn(*s, c["bits"], c["group"])])
+    time_graph(gr, 2)
+    us = time_graph(gr, 10) / 10
+    b = nbytes(*s[1:])
+    out["c4_kivi2_131k_B8"] = {"us": round(us, 2), "MB": round(b / 1e6, 1), "GBps": round(b / us / 1e3, 1),
+                               "frac": round(b / us / 1e3 / peak, 3)}
+    del s, gr
+    torch.cuda.empty_cache()
+    q1 = torch.randn(1, 28, D, device=dev, generator=g).bfloat16()
+    k1 = torch.randn(1, 4, S, D, device=dev, generator=g).bfloat16()
+    v1 = torch.randn(1, 4, S, D, device=dev, generator=g).bfloat16()
+    scal = 1.0 / math.sqrt(D)
+    gr = graph_of([lambda: _ops.decode_attn_partial(q1, k1, v1, scal)])
+    time_graph(gr, 2)
+    us_p = time_graph(gr, 10) / 10
+    m, l, o = _ops.decode_attn_partial(q1, k1, v1, scal)
+    m8, l8, o8 = (t.unsqueeze(0).repeat(8, *([1] * t.dim())).contiguous() for t in (m, l, o))
+    gr2 = graph_of([lambda: _ops.lse_combine(m8, l8, o8, torch.bfloat16)])
+    time_graph(gr2, 2)
+    us_c = time_graph(gr2, 20) / 20
+    b = nbytes(k1, v1)
+    out["c4_1M_shard_of_8"] = {"partial_us": round(us_p, 2), "combine8_us": round(us_c, 2),
+                               "GBps": round(b / us_p / 1e3, 1), "frac": round(b / us_p / 1e3 / peak, 3),
+                               "exchange_bytes_per_rank": int(m.numel() * 8 + o.numel() * 4)}
+    return out
+
+
+PATHS = {"c0": path_c0, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3, "topk": path_topk, "c4": path_c4}
 
 
 def extras(dev, peak, only=None):
