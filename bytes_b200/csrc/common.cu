@@ -120,6 +120,12 @@ extern "C" {
 
 int bd_abi_version(void) { return 1; }
 
+long long bd_wait_timeouts(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  const long long a = bd::kivi_wait_timeouts(), b = bd::pq_wait_timeouts(), c = bd::merge_wait_timeouts();
+  return (a < 0 || b < 0 || c < 0) ? -1 : a + b + c;
+}
+
 const char* bd_status_name(int s) {
   switch (s) {
     case BD_OK: return "BD_OK";

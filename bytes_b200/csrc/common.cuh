@@ -37,6 +37,10 @@ int check_tensor(const bd_tensor* t, const char* name, int ndim, int dtype = -1)
 // base pointer to be multiples of `align` bytes.
 int check_rows_aligned(const bd_tensor* t, const char* name, size_t align = 16);
 std::string shape_str(const bd_tensor* t);
+// Host reads of the per-file counters of device waits that ran past their limit.
+long long kivi_wait_timeouts();
+long long pq_wait_timeouts();
+long long merge_wait_timeouts();
 // Tiled TMA tensor map of rank 3..5 (dims[0] contiguous; strides in bytes of dims 1..rank-1),
 // encoded through the driver entry point fetched from the runtime. False if unavailable or
 // rejected.

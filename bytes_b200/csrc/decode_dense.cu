@@ -776,6 +776,14 @@ int static_scratch_address(void** ptr) {
 
 }  // namespace bd
 
+namespace bd {
+// host read of this file's wait-timeout counter (-1 on failure)
+long long merge_wait_timeouts() {
+  unsigned int v = 0;
+  return cudaMemcpyFromSymbol(&v, g_merge_timeouts, sizeof v) == cudaSuccess ? (long long)v : -1;
+}
+}  // namespace bd
+
 extern "C" {
 
 size_t bd_decode_attn_workspace(const bd_tensor* q, const bd_tensor* k) {

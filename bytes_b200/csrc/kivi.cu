@@ -1003,6 +1003,14 @@ __global__ void kivi_gemv_kernel(const GemvParams p) {
 }  // namespace
 }  // namespace bd
 
+namespace bd {
+// host read of this file's wait-timeout counter (-1 on failure)
+long long kivi_wait_timeouts() {
+  unsigned int v = 0;
+  return cudaMemcpyFromSymbol(&v, g_kivi_tma_timeouts, sizeof v) == cudaSuccess ? (long long)v : -1;
+}
+}  // namespace bd
+
 extern "C" {
 
 size_t bd_kivi_decode_attn_workspace(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_residual,

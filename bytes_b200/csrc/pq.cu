@@ -698,6 +698,14 @@ int dispatch_pq(const PqParams& p, int vk, bool paged, bool outl, cudaStream_t s
 }  // namespace
 }  // namespace bd
 
+namespace bd {
+// host read of this file's wait-timeout counter (-1 on failure)
+long long pq_wait_timeouts() {
+  unsigned int v = 0;
+  return cudaMemcpyFromSymbol(&v, g_pq_tma_timeouts, sizeof v) == cudaSuccess ? (long long)v : -1;
+}
+}  // namespace bd
+
 extern "C" {
 
 // Shared front end of the PQ-LUT decode entry points.

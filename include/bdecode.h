@@ -59,6 +59,13 @@ int bd_abi_version(void);
 const char* bd_status_name(int status);
 const char* bd_last_error(void);
 
+/* Number of bounded device waits (TMA or bulk-copy barriers) on the current device that
+ * ran past their iteration limit since the library was loaded; a non-zero count means
+ * some earlier result is wrong. Synchronises the device (a diagnostic, not for the hot
+ * path). Returns -1 if the counters cannot be read.
+ * ref: none (the reference's Triton kernels have no bounded waits). */
+long long bd_wait_timeouts(void);
+
 /* ---------------------------------------------------------------------------
  * Dense GQA decode attention, split-KV (flash-decoding) with a log-sum-exp
  * combine. q [B,Hq,D] (the reference's [B,Hq,1,D] with the singleton dropped),
@@ -102,8 +109,10 @@ int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o,
                    const bd_tensor* out, bd_stream_t stream);
 
 /* ---------------------------------------------------------------------------
- * KIVI 2/4-bit KV-cache decode (fused: packed-cache split-KV kernel + bf16
- * residual window + log-sum-exp combine). Q [B,Hq,D=128] bf16/f16/f32;
+ * KIVI 2/4-bit KV-cache decode: a packed-cache split-KV kernel, then a bf16
+ * residual-window kernel that (when the window takes one CTA per head group) also
+ * merges the split partials into `out`; otherwise a log-sum-exp combine follows.
+ * Q [B,Hq,D=128] bf16/f16/f32;
  * Kq int32 [B,Hk,D,Sq*bits/32]; K_scale,K_mn f16 [B,Hk,D,Sq/32];
  * Vq int32 [B,Hk,Sq,D*bits/32]; V_scale,V_mn f16 [B,Hk,Sq,D/32];
  * K_residual,V_residual bf16 [B,Hk,R,D]; out [B,Hq,D]; group_size 32.
@@ -120,7 +129,7 @@ int bd_kivi_decode_attn(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor
 
 /* Profiling form of bd_kivi_decode_attn: launches only the selected stages of the
  * step (bit 0: packed-cache split kernel, bit 1: residual-window kernel, bit 2:
- * combine). stages = 7 is bd_kivi_decode_attn. Used to time kernels one by one.
+ * merge into `out`). stages = 7 is bd_kivi_decode_attn. Used to time kernels one by one.
  * ref: none (measurement helper around kivi_decode_attn). */
 int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd_tensor* K_scale,
                                const bd_tensor* K_mn, const bd_tensor* K_residual, const bd_tensor* Vq,
