@@ -424,65 +424,100 @@ __device__ __forceinline__ int small_excl_scan(int v, int* red, int* total) {
   return r;
 }
 
-__global__ void __launch_bounds__(kSmThreads) topk_small_kernel(const TopkParams p) {
+template <int PER>
+__global__ void __launch_bounds__(kSmThreads, 4) topk_small_kernel(const TopkParams p) {
   extern __shared__ __align__(16) uint8_t smem[];  // sorted output: [kpow] keys, [kpow] indices
-  __shared__ int hist[256];
+  __shared__ int hist[2][256];
   __shared__ int red[33];
   __shared__ int s_digit, s_above;
   const int row = blockIdx.x;
   const float* src = p.scores + int64_t(row / p.rows_per_b) * p.b_stride + int64_t(row % p.rows_per_b) * p.row_stride;
   const int n = p.n, k = min(p.k, p.n);
   if (k <= 0) return;
-  const int per = (n + kSmThreads - 1) / kSmThreads;
-  const int i0 = int(threadIdx.x) * per;
-  uint32_t key[kSmPer];
-  const bool vec = (per % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  const int i0 = int(threadIdx.x) * PER;  // this thread's run of PER positions
+  uint32_t key[PER];
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
 #pragma unroll
-  for (int e = 0; e < kSmPer; e += 4) {
-    if (vec && e < per && i0 + e + 3 < n) {
+  for (int e = 0; e < PER; e += 4) {
+    if (vec && i0 + e + 3 < n) {
       const float4 x = *reinterpret_cast<const float4*>(src + i0 + e);
       key[e] = f2key(x.x); key[e + 1] = f2key(x.y); key[e + 2] = f2key(x.z); key[e + 3] = f2key(x.w);
     } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) key[e + u] = (e + u < per && i0 + e + u < n) ? f2key(src[i0 + e + u]) : 0u;
+      for (int u = 0; u < 4; ++u) key[e + u] = i0 + e + u < n ? f2key(src[i0 + e + u]) : 0u;
     }
   }
-  auto valid = [&](int e) { return e < per && i0 + e < n; };
+  // candidates of the digit passes: bit e set while key e matches the prefix found so far
+  uint32_t cand = 0;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) cand |= uint32_t(i0 + e < n) << e;
+  const uint32_t valid_bits = cand;
+  auto valid = [&](int e) { return (valid_bits >> e) & 1u; };
 
-  // ---- radix select of the k-th largest key
+  // ---- radix select of the k-th largest key: per pass one shared histogram (two buffers,
+  // each cleared right after its pass) and one warp that scans the 256 bins from the top
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t prefix = 0, mask = 0;
   int remaining = k;
   if (k < n) {
+    hist[0][threadIdx.x] = 0;
+    hist[1][threadIdx.x] = 0;
+    __syncthreads();
 #pragma unroll 1
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      hist[threadIdx.x] = 0;
-      __syncthreads();
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      int* h = hist[pass & 1];
 #pragma unroll
-      for (int e = 0; e < kSmPer; ++e)
-        if (valid(e) && (key[e] & mask) == prefix) atomicAdd(&hist[(key[e] >> shift) & 255u], 1);
+      for (int e = 0; e < PER; ++e)
+        if ((cand >> e) & 1u) atomicAdd(&h[(key[e] >> shift) & 255u], 1);
       __syncthreads();
-      const int d = 255 - int(threadIdx.x);  // thread t owns digit 255 - t: the scan counts higher digits
-      const int c = hist[d];
-      int tot;
-      const int above = small_excl_scan(c, red, &tot);
-      if (above < remaining && above + c >= remaining) { s_digit = d; s_above = above; }
+      if (warp == 0) {
+        // lane L owns digits 255-8L down to 248-8L
+        int c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = h[255 - 8 * lane - j];
+          sum += c[j];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        int acc = incl - sum;  // keys in higher digits
+        if (acc < remaining && acc + sum >= remaining) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (acc + c[j] >= remaining) {
+              s_digit = 255 - 8 * lane - j;
+              s_above = acc;
+              break;
+            }
+            acc += c[j];
+          }
+        }
+      }
       __syncthreads();
       prefix |= uint32_t(s_digit) << shift;
       mask |= 0xffu << shift;
       remaining -= s_above;
-      __syncthreads();
+      h[threadIdx.x] = 0;  // this buffer serves pass + 2, after the other buffer's barriers
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if ((key[e] & mask) != prefix) cand &= ~(1u << e);
     }
   }
   // ---- keep every key above T and the first `remaining` keys equal to T (index order)
   int eq = 0;
 #pragma unroll
-  for (int e = 0; e < kSmPer; ++e) eq += (k < n && valid(e) && key[e] == prefix) ? 1 : 0;
+  for (int e = 0; e < PER; ++e) eq += (k < n && valid(e) && key[e] == prefix) ? 1 : 0;
   int tot;
   int eq_rank = small_excl_scan(eq, red, &tot);
   uint32_t selbits = 0;
   int nsel = 0;
 #pragma unroll
-  for (int e = 0; e < kSmPer; ++e) {
+  for (int e = 0; e < PER; ++e) {
     bool sel = false;
     if (valid(e)) {
       if (k >= n || key[e] > prefix) sel = true;
@@ -497,7 +532,7 @@ __global__ void __launch_bounds__(kSmThreads) topk_small_kernel(const TopkParams
   while (kpow < max(k, 1)) kpow <<= 1;
   int* wi = reinterpret_cast<int*>(smem + size_t(kpow) * 4);
 #pragma unroll
-  for (int e = 0; e < kSmPer; ++e) {
+  for (int e = 0; e < PER; ++e) {
     if (!((selbits >> e) & 1u)) continue;
     const int idx = i0 + e;
     if (p.sorted) {
@@ -513,7 +548,65 @@ __global__ void __launch_bounds__(kSmThreads) topk_small_kernel(const TopkParams
   if (!p.sorted) return;
   for (int i = k + threadIdx.x; i < kpow; i += kSmThreads) { wk[i] = 0u; wi[i] = 0x7fffffff; }
   __syncthreads();
-  // ---- bitonic sort of kpow entries (key desc, index asc); padding sorts last
+  auto before = [](uint32_t ka, int ia, uint32_t kb, int ib) { return ka > kb || (ka == kb && ia < ib); };
+  if (kpow <= 128) {
+    // ---- one warp sorts in registers: element i = lane + 32r (r < E), bitonic network
+    // (key desc, index asc); pairs 32 or more apart sit in one lane, closer ones meet by
+    // shuffle. Padding (key 0, largest index) sorts last.
+    if (warp != 0) return;
+    const int E = (kpow + 31) / 32;
+    uint32_t kk[4];
+    int ii[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = lane + 32 * r;
+      const bool in = r < E && i < kpow;
+      kk[r] = in ? wk[i] : 0u;
+      ii[r] = in ? wi[i] : 0x7fffffff;
+    }
+    for (int size = 2; size <= kpow; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        if (stride >= 32) {
+          const int rs = stride >> 5;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (r >= E || (r & rs)) continue;
+            const int r2 = r | rs;
+            const int i = lane + 32 * r;
+            const bool desc = (i & size) == 0;
+            if (before(kk[r], ii[r], kk[r2], ii[r2]) != desc) {
+              const uint32_t tk = kk[r]; kk[r] = kk[r2]; kk[r2] = tk;
+              const int ti = ii[r]; ii[r] = ii[r2]; ii[r2] = ti;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (r >= E) continue;  // warp-uniform
+            const int i = lane + 32 * r;
+            const uint32_t pk = __shfl_xor_sync(0xffffffffu, kk[r], stride);
+            const int pi = __shfl_xor_sync(0xffffffffu, ii[r], stride);
+            const bool lo = (lane & stride) == 0;
+            const bool desc = (i & size) == 0;
+            // the lower element of the pair keeps the one that comes first in this block's order
+            const bool mine_first = before(kk[r], ii[r], pk, pi);
+            const bool keep = (lo == desc) ? mine_first : !mine_first;
+            if (!keep) { kk[r] = pk; ii[r] = pi; }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int o = lane + 32 * r;
+      if (r >= E || o >= k) continue;
+      if (p.vals) p.vals[int64_t(row) * p.v_rs + o] = key2f(kk[r]);
+      if (p.idx64) reinterpret_cast<int64_t*>(p.idx)[int64_t(row) * p.i_rs + o] = ii[r];
+      else reinterpret_cast<int32_t*>(p.idx)[int64_t(row) * p.i_rs + o] = ii[r];
+    }
+    return;
+  }
+  // ---- bitonic sort of kpow entries in shared memory (key desc, index asc); padding last
   for (int size = 2; size <= kpow; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int t = threadIdx.x; t < kpow / 2; t += kSmThreads) {
@@ -1053,7 +1146,10 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
   if (smem > 220 * 1024) return fail(BD_ERR_UNSUPPORTED, "top-k: sorted output of this many elements does not fit");
   int rc;
   if (n > 0 && n <= kSmRowMax && (!sorted || kk <= kSmSortMax)) {
-    topk_small_kernel<<<rows, kSmThreads, sorted ? wbytes : 0, st>>>(p);
+    const size_t sm = sorted ? wbytes : 0;
+    if (n <= kSmThreads * 4) topk_small_kernel<4><<<rows, kSmThreads, sm, st>>>(p);
+    else if (n <= kSmThreads * 8) topk_small_kernel<8><<<rows, kSmThreads, sm, st>>>(p);
+    else topk_small_kernel<16><<<rows, kSmThreads, sm, st>>>(p);
     return cuda_check(cudaGetLastError(), "topk_small_kernel launch");
   }
   const size_t fast_smem = size_t(n) * 4 + 4096 * 4 + size_t(kCandMax) * 4 + wbytes;

@@ -15,9 +15,9 @@ def kivi_decode_attn(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_resi
     Kq int32 [B,H_k,D,Sq*bits/32]; K_scale/K_mn f16 [B,H_k,D,Sq/32];
     K_residual bf16 [B,H_k,R,D]; Vq int32 [B,H_k,Sq,D*bits/32];
     V_scale/V_mn f16 [B,H_k,Sq,D/32]; V_residual bf16 [B,H_k,R,D].
-    Returns [B,H_q,1,D] in Q.dtype. One split-KV kernel over the packed cache, one
-    over the residual window and a log-sum-exp combine (the reference issues 6+
-    launches and materialises the scores).
+    Returns [B,H_q,1,D] in Q.dtype. Two launches: a split-KV kernel over the packed
+    cache, then one over the residual window that also merges the split partials (the
+    reference issues 6+ launches and materialises the scores).
     """
     if Q.dim() != 4 or Q.shape[2] != 1:
         raise ValueError("Q must be [B, H_q, 1, D]")

@@ -86,7 +86,7 @@ def test_topk_bit_exact_with_ties(cuda, sorted_):
     s[0, :] = 3.0  # all equal
     s[1, ::3] = -0.0
     s[1, 1::3] = 0.0
-    for k in (1, 7, 64, 1000, 2048):
+    for k in (1, 7, 33, 64, 100, 1000, 2048):
         _topk_check(s, k, sorted_)
     assert oracle.topk_lower_index(torch.tensor([[1., 3., 3., 2., 3., 0.]]), 2)[1].tolist() == [[1, 2]]
     v, i = ak.topk(torch.tensor([[1., 3., 3., 2., 3., 0.]], device=cuda), 2)
