@@ -1054,29 +1054,40 @@ struct QuestMmaParams {
   const __nv_bfloat16* q; int64_t q_sb, q_sh;
   const __nv_bfloat16* kmin; const __nv_bfloat16* kmax; int64_t m_sb, m_sh, m_sp;
   int Hq, Hk, G, head_chunks, np, force_from;
+  int blocks_per_cta;  // 64-page blocks each CTA streams
   float scaling;
   float* bounds;
 };
 
+// One CTA streams `blocks_per_cta` consecutive blocks of 64 pages of one (b, KV head,
+// head chunk) through a two-stage cp.async pipeline (the next block's [max | min] rows load
+// while this one's bounds are computed); the query fragments are built once per CTA.
 template <int D>
 __global__ void __launch_bounds__(128) quest_bounds_mma_kernel(const QuestMmaParams p) {
   constexpr int ROWB = 4 * D;        // [max | min] bf16 bytes per page
   constexpr int PITCH = ROWB + 16;   // padded row
   constexpr int CH = ROWB / 16;      // 16-byte chunks per page
   constexpr int KSTEPS = 2 * D / 16;
-  __shared__ __align__(16) uint8_t sm[kQmPages * PITCH];
+  constexpr int STAGE = kQmPages * PITCH;
+  extern __shared__ __align__(16) uint8_t sm[];  // [2 stages][64 pages][PITCH]
   const int b = blockIdx.z, hk = blockIdx.y / p.head_chunks, chunk = blockIdx.y % p.head_chunks;
-  const int p0 = blockIdx.x * kQmPages;
-  const int npg = min(kQmPages, p.np - p0);
+  const int blk0 = blockIdx.x * p.blocks_per_cta;
+  const int nblk = min(p.blocks_per_cta, (p.np + kQmPages - 1) / kQmPages - blk0);
+  if (nblk <= 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int64_t mbase = int64_t(b) * p.m_sb + int64_t(hk) * p.m_sh;
-  for (int c = threadIdx.x; c < kQmPages * CH; c += 128) {
-    const int r = c / CH, cc = c % CH;
-    const bool ok = r < npg;
-    const __nv_bfloat16* src = (cc < CH / 2 ? p.kmax : p.kmin) + mbase + int64_t(ok ? p0 + r : 0) * p.m_sp +
-                               (cc % (CH / 2)) * 8;
-    cp_async16(smem_u32(sm + r * PITCH + cc * 16), src, ok ? 16 : 0);
-  }
+  auto load_block = [&](int i, int stage) {
+    const int p0 = (blk0 + i) * kQmPages;
+    const int npg = min(kQmPages, p.np - p0);
+    for (int c = threadIdx.x; c < kQmPages * CH; c += 128) {
+      const int r = c / CH, cc = c % CH;
+      const bool ok = r < npg;
+      const __nv_bfloat16* src = (cc < CH / 2 ? p.kmax : p.kmin) + mbase + int64_t(ok ? p0 + r : 0) * p.m_sp +
+                                 (cc % (CH / 2)) * 8;
+      cp_async16(smem_u32(sm + stage * STAGE + r * PITCH + cc * 16), src, ok ? 16 : 0);
+    }
+  };
+  load_block(0, 0);
   cp_async_commit();
   // B fragments: head n = g of this chunk; k < D -> q+ (max rows), k >= D -> q- (min rows)
   const int h = chunk * 8 + g;
@@ -1095,24 +1106,29 @@ __global__ void __launch_bounds__(128) quest_bounds_mma_kernel(const QuestMmaPar
       x = k < D ? __hmax2(x, z) : __hmin2(x, z);
       bq[kk][e] = *reinterpret_cast<uint32_t*>(&x);
     }
-  cp_async_wait<0>();
-  __syncthreads();
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const uint32_t arow = smem_u32(sm + (warp * 16 + (lane & 15)) * PITCH + (lane >> 4) * 16);
+  for (int i = 0; i < nblk; ++i) {
+    cp_async_wait<0>();
+    __syncthreads();  // block i landed; the stage block i+1 goes to was read last round
+    if (i + 1 < nblk) load_block(i + 1, (i + 1) & 1);
+    cp_async_commit();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t arow = smem_u32(sm + (i & 1) * STAGE + (warp * 16 + (lane & 15)) * PITCH + (lane >> 4) * 16);
 #pragma unroll
-  for (int kk = 0; kk < KSTEPS; ++kk) {
-    uint32_t a0, a1, a2, a3;
-    ldmatrix_x4(a0, a1, a2, a3, arow + kk * 32);
-    mma_bf16(acc, a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
-  }
-  // acc: (page 16w+g, heads 2tq, 2tq+1), (page 16w+g+8, heads 2tq, 2tq+1)
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4(a0, a1, a2, a3, arow + kk * 32);
+      mma_bf16(acc, a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
+    }
+    // acc: (page 16w+g, heads 2tq, 2tq+1), (page 16w+g+8, heads 2tq, 2tq+1)
+    const int p0 = (blk0 + i) * kQmPages;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int pg = p0 + warp * 16 + g + (e >> 1) * 8;
-    const int hh = chunk * 8 + 2 * tq + (e & 1);
-    if (pg < p.np && hh < p.G) {
-      const float v = pg >= p.force_from ? INFINITY : acc[e] * p.scaling;
-      p.bounds[(int64_t(b) * p.Hq + hk * p.G + hh) * p.np + pg] = v;
+    for (int e = 0; e < 4; ++e) {
+      const int pg = p0 + warp * 16 + g + (e >> 1) * 8;
+      const int hh = chunk * 8 + 2 * tq + (e & 1);
+      if (pg < p.np && hh < p.G) {
+        const float v = pg >= p.force_from ? INFINITY : acc[e] * p.scaling;
+        p.bounds[(int64_t(b) * p.Hq + hk * p.G + hh) * p.np + pg] = v;
+      }
     }
   }
 }
@@ -1418,11 +1434,29 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
     p.kmin = mn; p.kmax = mx; p.m_sb = kmin->stride[0]; p.m_sh = kmin->stride[1]; p.m_sp = kmin->stride[2];
     p.Hq = int(Hq); p.Hk = int(Hk); p.G = int(Hq / Hk); p.head_chunks = (p.G + 7) / 8; p.np = int(np);
     p.force_from = force_from_page; p.scaling = scaling; p.bounds = static_cast<float*>(bounds->data);
-    dim3 gm(unsigned((np + kQmPages - 1) / kQmPages), unsigned(Hk * p.head_chunks), unsigned(B));
-    if (D == 128) quest_bounds_mma_kernel<128><<<gm, 128, 0, st>>>(p);
-    else if (D == 64) quest_bounds_mma_kernel<64><<<gm, 128, 0, st>>>(p);
-    else quest_bounds_mma_kernel<32><<<gm, 128, 0, st>>>(p);
-    return cuda_check(cudaGetLastError(), "quest_bounds_mma_kernel launch");
+    // enough CTAs for one wave at three per SM; each streams an equal run of page blocks
+    const int64_t nblk = (np + kQmPages - 1) / kQmPages;
+    const int64_t groups = int64_t(B) * Hk * p.head_chunks;
+    const int64_t per_group = std::max<int64_t>(1, std::min<int64_t>(nblk, 3LL * num_sms() / std::max<int64_t>(groups, 1)));
+    p.blocks_per_cta = int((nblk + per_group - 1) / per_group);
+    dim3 gm(unsigned((nblk + p.blocks_per_cta - 1) / p.blocks_per_cta), unsigned(Hk * p.head_chunks), unsigned(B));
+    const size_t smem = size_t(2) * kQmPages * (4 * D + 16);
+    auto launch = [&](auto kern) {
+      static bool attr[64] = {false};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!attr[dev & 63]) {
+        const int r = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                                 "cudaFuncSetAttribute(quest_bounds)");
+        if (r) return r;
+        attr[dev & 63] = true;
+      }
+      kern<<<gm, 128, smem, st>>>(p);
+      return cuda_check(cudaGetLastError(), "quest_bounds_mma_kernel launch");
+    };
+    if (D == 128) return launch(quest_bounds_mma_kernel<128>);
+    if (D == 64) return launch(quest_bounds_mma_kernel<64>);
+    return launch(quest_bounds_mma_kernel<32>);
   }
   dim3 grid(unsigned((np + kQPages - 1) / kQPages), unsigned(Hk), unsigned(B));
   if (D == 128)
