@@ -805,7 +805,8 @@ struct GatherParams {
   int B, Hq, Hk, G, S, kb;
   float scaling;
   int rows_per_split, nsplit;
-  float* part_m; float* part_l; float* part_o;
+  float* part_m; float* part_l; float* part_o;  // split partials (or, with one split, the exported m, l, o)
+  void* out; int out_dtype; int64_t o_sb, o_sh;  // one split and a final output: written directly
 };
 
 template <int D, bool FP8>
@@ -948,6 +949,14 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
       const float f = M == -INFINITY ? 0.f : __expf(red_m[i] - M);
       L += red_l[i] * f;
       O += red_o[i][c] * f;
+    }
+    if (p.out) {  // one split: the final output, no combine
+      const int64_t off = int64_t(b) * p.o_sb + int64_t(hq) * p.o_sh + c;
+      const float x = O / L;
+      if (p.out_dtype == BD_BF16) reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
+      else if (p.out_dtype == BD_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
+      else reinterpret_cast<float*>(p.out)[off] = x;
+      continue;
     }
     const int64_t pi = (int64_t(b) * p.Hq + hq) * p.nsplit + split;
     p.part_o[pi * D + c] = O;
@@ -1213,10 +1222,11 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
 
 }  // namespace
 
-// Index-list splits of the gather-attention: enough 4-warp CTAs for ~8 per SM (random
-// row gathers need many rows in flight), at least 64 index entries per split.
+// Index-list splits of the gather-attention: enough 4-warp CTAs for about two per SM, at
+// least 64 index entries per split. Longer runs per CTA beat more splits (measured at c3:
+// one split per row, 512 CTAs, then no combine at all).
 int gather_splits(int64_t rows, int64_t kb) {
-  const int64_t target = 8LL * num_sms();
+  const int64_t target = 2LL * num_sms();
   const int64_t want = std::max<int64_t>(1, (target + std::max<int64_t>(rows, 1) - 1) / std::max<int64_t>(rows, 1));
   return int(std::max<int64_t>(1, std::min<int64_t>(want, (kb + 63) / 64)));
 }
@@ -1331,6 +1341,13 @@ static int sparse_gather_run(const bd_tensor* q, const bd_tensor* k, const bd_te
   p.rows_per_split = int((kb + nsplit - 1) / nsplit);
   p.nsplit = nsplit;
   p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
+  const bool direct = nsplit == 1;
+  if (direct && out) {
+    p.out = out->data; p.out_dtype = out->dtype; p.o_sb = out->stride[0]; p.o_sh = out->stride[1];
+  } else if (direct) {  // the row's (m, l, o) are the exported partial
+    p.part_m = static_cast<float*>(em->data); p.part_l = static_cast<float*>(el->data);
+    p.part_o = static_cast<float*>(eo->data);
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(nsplit, unsigned(Hq), unsigned(B));
   const bool fp8 = k->dtype == BD_F8E4M3;
@@ -1345,6 +1362,7 @@ static int sparse_gather_run(const bd_tensor* q, const bd_tensor* k, const bd_te
     else gather_attn_kernel<32, false><<<grid, 128, 0, st>>>(p);
   }
   if ((rc = cuda_check(cudaGetLastError(), "gather_attn_kernel launch"))) return rc;
+  if (direct) return BD_OK;
   if (out) return launch_combine(part, int(B), int(Hq), int(D), out, st, true);
   return launch_combine_export(part, int(B), int(Hq), int(D), static_cast<float*>(em->data),
                                static_cast<float*>(el->data), static_cast<float*>(eo->data), st, true);
