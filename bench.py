@@ -554,7 +554,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": _profile_traffic("kivi_decode_kernel_c1.md"),
-                         "kernel": "kivi_decode_kernel<2,1>", "algorithmic_bytes_per_launch": kern_bytes,
+                         "kernel": "kivi_decode_kernel<2,1,3>", "algorithmic_bytes_per_launch": kern_bytes,
                          "kernel_us": round(us_kern, 2)},
             "cpu_baseline": cpu_base,
             "e2e": {"value": round(us_e2e, 2), "unit": "us/step", "h2d_bytes_per_step": nbytes(sets[0][0]),

@@ -34,7 +34,7 @@
 //    partial buffer; a log-sum-exp combine produces the output. Both are launched as
 //    programmatic dependents, so the residual CTAs fill the SMs this grid's tail frees
 //    and the combine is resident before its inputs are complete.
-//  * Splits are balanced to one wave of 4 CTAs per SM (split s owns tiles
+//  * Splits are balanced to one wave of 3 or 4 CTAs per SM (split s owns tiles
 //    [s*T/n, (s+1)*T/n)), so no SM carries a second round.
 #include "common.cuh"
 #include "decode_shared.cuh"
@@ -139,8 +139,8 @@ __device__ unsigned int g_kivi_tma_timeouts = 0;
 // every weight 2^(x - reference) stays <= 1.
 constexpr float kHeadroom = 4.f;
 
-template <int BITS, bool TMA>
-__global__ void __launch_bounds__(kWarpsK * 32, 4)
+template <int BITS, bool TMA, int MINB>
+__global__ void __launch_bounds__(kWarpsK * 32, MINB)
     kivi_decode_kernel(const KiviParams p, const __grid_constant__ CUtensorMap tm_kq,
                        const __grid_constant__ CUtensorMap tm_vq, const __grid_constant__ CUtensorMap tm_vs,
                        const __grid_constant__ CUtensorMap tm_vm) {
@@ -467,16 +467,19 @@ __global__ void __launch_bounds__(kWarpsK * 32, 4)
       bool grow = false;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        float m = fmaxf(fmaxf(x[j][0], x[j][1]), fmaxf(x[j][2], x[j][3]));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-        mx[j] = m;
-        grow |= m > mref[j];
+        mx[j] = fmaxf(fmaxf(x[j][0], x[j][1]), fmaxf(x[j][2], x[j][3]));
+        grow |= mx[j] > mref[j];
       }
-      // move the reference only when some head's maximum passed it (rare after the first
-      // tile of a split): then alpha = 2^(old - new) rescales the running sums
+      // move the reference only when some score passed it (rare after the first tile of a
+      // split): then the head maxima are reduced over the warp and alpha = 2^(old - new)
+      // rescales the running sums
       if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 4));
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 8));
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 16));
+        }
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const float mnew = mx[j] > mref[j] ? mx[j] + kHeadroom : mref[j];
@@ -737,11 +740,11 @@ bool kivi_tma_maps(const KiviParams& kp, int64_t W, CUtensorMap out[4]) {
   return true;
 }
 
-template <int BITS, bool TMA>
+template <int BITS, bool TMA, int MINB>
 int launch_kivi_as(const KiviParams& kp, int n_splits, const CUtensorMap* maps, cudaStream_t st) {
   using L = KL<BITS, TMA>;
   const size_t smem = std::max<size_t>(L::SMEM, (2 * 4 * 8 + 4 * 8 * kRedPitch) * sizeof(float)) + (TMA ? 1024 : 0);
-  auto kern = kivi_decode_kernel<BITS, TMA>;
+  auto kern = kivi_decode_kernel<BITS, TMA, MINB>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -759,15 +762,19 @@ int launch_kivi_as(const KiviParams& kp, int n_splits, const CUtensorMap* maps, 
 // W = words per key row (Kq's last dim). 2-bit caches whose geometry TMA can address take
 // the TMA form; everything else the cp.async form.
 template <int BITS>
-int launch_kivi(const KiviParams& kp, int n_splits, int64_t W, cudaStream_t st) {
+int launch_kivi(const KiviParams& kp, int n_splits, int64_t W, int ctas_per_sm, cudaStream_t st) {
   alignas(64) CUtensorMap maps[4];
   std::memset(maps, 0, sizeof maps);
-  if (BITS == 2 && kivi_tma_maps(kp, W, maps)) return launch_kivi_as<2, true>(kp, n_splits, maps, st);
-  return launch_kivi_as<BITS, false>(kp, n_splits, maps, st);
+  const bool four = ctas_per_sm == 4;
+  if (BITS == 2 && kivi_tma_maps(kp, W, maps))
+    return four ? launch_kivi_as<2, true, 4>(kp, n_splits, maps, st) : launch_kivi_as<2, true, 3>(kp, n_splits, maps, st);
+  return four ? launch_kivi_as<BITS, false, 4>(kp, n_splits, maps, st)
+              : launch_kivi_as<BITS, false, 3>(kp, n_splits, maps, st);
 }
 
 struct KiviPlan {
   int n_kivi, ntiles, n_res, head_chunks;
+  int ctas_per_sm;  // occupancy the split count is balanced for (and the kernel compiled for)
 };
 
 int kivi_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t Sq, int64_t R, KiviPlan* pl) {
@@ -775,7 +782,11 @@ int kivi_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t Sq, int64_t R, KiviPlan
   pl->head_chunks = (G + 7) / 8;
   const int64_t ntiles = (Sq + kTile - 1) / kTile;
   const int64_t pairs = B * Hk * pl->head_chunks;
-  const int64_t slots = 4LL * num_sms();
+  // three CTAs per SM while each split streams few tiles: the room left over lets the
+  // residual-window CTAs, launched behind this pass, run beside it, which shortens the
+  // step's tail; four when the packed pass is long and its own throughput dominates
+  pl->ctas_per_sm = ntiles > 256 ? 4 : 3;
+  const int64_t slots = int64_t(pl->ctas_per_sm) * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
   pl->n_kivi = ntiles > 0 ? int(splits) : 0;
@@ -1083,7 +1094,8 @@ int bd_kivi_decode_attn_stages(const bd_tensor* Q, const bd_tensor* Kq, const bd
     kp.head_chunks = pl.head_chunks; kp.nsplit = pl.n_kivi; kp.ntiles = pl.ntiles;
     kp.scale_log2 = scaling * kLog2eK;
     kp.part_m = part.m; kp.part_l = part.l; kp.part_o = part.o; kp.split_stride = ntot;
-    rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, Kq->shape[3], st) : launch_kivi<4>(kp, pl.n_kivi, Kq->shape[3], st);
+    rc = bits == 2 ? launch_kivi<2>(kp, pl.n_kivi, Kq->shape[3], pl.ctas_per_sm, st)
+                   : launch_kivi<4>(kp, pl.n_kivi, Kq->shape[3], pl.ctas_per_sm, st);
     if (rc) return rc;
   }
   if (pl.n_res == 1 && pl.n_kivi > 0 && (stages & 7) == 7) {
