@@ -208,54 +208,6 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
   const __half* vs_base = p.vs + int64_t(b) * p.vs_sb + int64_t(hk) * p.vs_sh;
   const __half* vm_base = p.vm + int64_t(b) * p.vm_sb + int64_t(hk) * p.vm_sh;
 
-  // query of head g as f16 pairs in MMA k order: qh[j][0] = channels 16j+2tq,+1;
-  // qh[j][1] = 16j+8+2tq,+1. A power-of-two pre-scale keeps |q| <= 2^8 in f16.
-  uint32_t qh[8][2];
-  float score_mul = p.scale_log2;
-  {
-    const bool ok = g < nheads;
-    const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? g : 0)) * p.q_sh;
-    float qv[8][4];
-    float amax = 0.f;
-    // channel pairs (2tq, 2tq+1) are adjacent: one 32-bit load per pair for 16-bit queries
-    // whose rows start on an even element (the common case), element loads otherwise
-    const bool pairs = p.q_dtype != BD_F32 && ((qoff & 1) == 0) && ((reinterpret_cast<uintptr_t>(p.q) & 3) == 0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int64_t off = qoff + 16 * j + 2 * tq + (e >> 1) * 8;
-        float2 v = make_float2(0.f, 0.f);
-        if (ok && pairs) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(p.q) + off);
-          v = p.q_dtype == BD_BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w))
-                                   : __half22float2(*reinterpret_cast<const __half2*>(&w));
-        } else if (ok) {
-          v = make_float2(load_qk(p, off), load_qk(p, off + 1));
-        }
-        qv[j][e] = v.x;
-        qv[j][e + 1] = v.y;
-        amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
-      }
-    amax = warp_max(amax);
-    int ex = 0;
-    frexpf(amax, &ex);
-    const int shift = ex > 8 ? ex - 8 : 0;
-    const float qs = ldexpf(1.f, -shift);
-    score_mul = ldexpf(p.scale_log2, shift);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      qh[j][0] = pack_f16x2(qv[j][0] * qs, qv[j][1] * qs);
-      qh[j][1] = pack_f16x2(qv[j][2] * qs, qv[j][3] * qs);
-    }
-  }
-
-  // accumulator -> log2-domain score: kmul[2rb + h] for row g + 8h of row block rb
-  float kmul[4];
-#pragma unroll
-  for (int f = 0; f < 4; ++f)
-    kmul[f] = BITS == 2 ? __int_as_float((127 + 24 - 2 * f) << 23) * score_mul : subK * score_mul;
-
   // Global -> shared copy assignment of this thread, fixed over the split's tiles.
   constexpr int NCH = L::KQ_WORDS / 4;  // 16-byte key chunks per channel row (2 or 4)
   constexpr int NVC = L::VQ_WORDS / 4;  // 16-byte value chunks per token row (2 or 4)
@@ -350,6 +302,56 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
     if (s < ntiles) load_tile(s, s);
     cp_async_commit();
   }
+
+  // the query loads follow the first tile copies, so their latencies overlap
+  // query of head g as f16 pairs in MMA k order: qh[j][0] = channels 16j+2tq,+1;
+  // qh[j][1] = 16j+8+2tq,+1. A power-of-two pre-scale keeps |q| <= 2^8 in f16.
+  uint32_t qh[8][2];
+  float score_mul = p.scale_log2;
+  {
+    const bool ok = g < nheads;
+    const int64_t qoff = int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + (ok ? g : 0)) * p.q_sh;
+    float qv[8][4];
+    float amax = 0.f;
+    // channel pairs (2tq, 2tq+1) are adjacent: one 32-bit load per pair for 16-bit queries
+    // whose rows start on an even element (the common case), element loads otherwise
+    const bool pairs = p.q_dtype != BD_F32 && ((qoff & 1) == 0) && ((reinterpret_cast<uintptr_t>(p.q) & 3) == 0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int64_t off = qoff + 16 * j + 2 * tq + (e >> 1) * 8;
+        float2 v = make_float2(0.f, 0.f);
+        if (ok && pairs) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(p.q) + off);
+          v = p.q_dtype == BD_BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w))
+                                   : __half22float2(*reinterpret_cast<const __half2*>(&w));
+        } else if (ok) {
+          v = make_float2(load_qk(p, off), load_qk(p, off + 1));
+        }
+        qv[j][e] = v.x;
+        qv[j][e + 1] = v.y;
+        amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
+      }
+    amax = warp_max(amax);
+    int ex = 0;
+    frexpf(amax, &ex);
+    const int shift = ex > 8 ? ex - 8 : 0;
+    const float qs = ldexpf(1.f, -shift);
+    score_mul = ldexpf(p.scale_log2, shift);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      qh[j][0] = pack_f16x2(qv[j][0] * qs, qv[j][1] * qs);
+      qh[j][1] = pack_f16x2(qv[j][2] * qs, qv[j][3] * qs);
+    }
+  }
+
+  // accumulator -> log2-domain score: kmul[2rb + h] for row g + 8h of row block rb
+  float kmul[4];
+#pragma unroll
+  for (int f = 0; f < 4; ++f)
+    kmul[f] = BITS == 2 ? __int_as_float((127 + 24 - 2 * f) << 23) * score_mul : subK * score_mul;
+
 
   for (int it = 0; it < ntiles; ++it) {
     cp_async_wait<kStagesK - 2>();  // key scale/min chunks (and, without TMA, the tile)
