@@ -91,8 +91,8 @@ struct KL {
   static constexpr int T_COL = 80;
   static constexpr int T_GROUP = 4 * T_COL;
   static constexpr int T_BYTES = 8 * T_GROUP;
-  static constexpr int OFF_T = OFF_KC + 2 * KC_BYTES;
-  static constexpr int OFF_BAR = OFF_T + T_BYTES;  // TMA: one mbarrier per stage
+  static constexpr int OFF_T = OFF_KC + 2 * KC_BYTES;  // two buffers: tile it and tile it + 1
+  static constexpr int OFF_BAR = OFF_T + 2 * T_BYTES;  // TMA: one mbarrier per stage
   static constexpr int SMEM = OFF_BAR + kStagesK * 8;
   static constexpr uint32_t TMA_BYTES = 128 * 32 + kTile * 32 + 2 * kTile * 8;  // K, V codes, V scale, V min
   static_assert(!TMA || (BITS == 2 && STAGE % 1024 == 0), "TMA stages hold the 2-bit tile at 1024-byte alignment");
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
   // TMA destinations must sit on the swizzle atom: align the working base by hand (the
   // launch adds 1 KB); every shared-memory access below goes through `smem`
   uint8_t* smem = TMA ? smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : smem_raw;
-  uint8_t* tsm = smem + L::OFF_T;  // key scale / min of the current tile, per lane column
+  uint8_t* tsm = smem + L::OFF_T;  // key scale / min per lane column, buffer tile & 1
   const uint32_t bar0 = smem_u32(smem + L::OFF_BAR);
   if (TMA) {
     if (threadIdx.x == 0) {
@@ -234,17 +234,6 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
     const int t0 = t_begin + tile * kTile;
     const uint32_t sbase = smem_u32(smem + stage * L::STAGE);
     const int64_t vt = int64_t(tile) * kTile;
-    if (tile % kKChunk == 0) {
-      // key scale/min of tiles [tile, tile + kKChunk): 16 groups per channel row
-      const uint32_t dst = kc_dst + ((tile / kKChunk) & 1) * L::KC_BYTES;
-      const int goff = tile * 4 + 4 * kc_piece;  // first group of this piece, relative to t_begin
-      const int gv = max(0, min(4, groups_end - (t_begin / 32 + goff)));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        cp_async8(dst + i * 32 * L::KC_ROW, gv ? ks_src + i * ks_pass + tile * 4 : ks_base, gv * 2);
-        cp_async8(dst + 128 * L::KC_ROW + i * 32 * L::KC_ROW, gv ? km_src + i * km_pass + tile * 4 : km_base, gv * 2);
-      }
-    }
     if (TMA) {
       // one thread moves the whole tile; rows past the sequence end arrive as zeros
       if (threadIdx.x == 0) {
@@ -284,6 +273,18 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
       cp_async8(sbase + L::OFF_VM + threadIdx.x * 8, ok ? vm_src + vt * p.vm_st : vm_base, ok ? 8 : 0);
     }
   };
+  // key scale/min of tiles [tile, tile + kKChunk) (16 groups per channel row) into chunk
+  // buffer (tile / kKChunk) & 1
+  auto load_chunk = [&](int tile) {
+    const uint32_t dst = kc_dst + ((tile / kKChunk) & 1) * L::KC_BYTES;
+    const int goff = tile * 4 + 4 * kc_piece;  // first group of this piece, relative to t_begin
+    const int gv = max(0, min(4, groups_end - (t_begin / 32 + goff)));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      cp_async8(dst + i * 32 * L::KC_ROW, gv ? ks_src + i * ks_pass + tile * 4 : ks_base, gv * 2);
+      cp_async8(dst + 128 * L::KC_ROW + i * 32 * L::KC_ROW, gv ? km_src + i * km_pass + tile * 4 : km_base, gv * 2);
+    }
+  };
 
   float o[8][4];
 #pragma unroll
@@ -297,11 +298,30 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
   // 2-bit value reads: row block (tq + 4 warp) of the interleaved tile, word g >> 2
   const uint32_t v_lane = (tq + 4 * warp) * 32 + 4 * (g >> 2);
 
-#pragma unroll
-  for (int s = 0; s < kStagesK - 1; ++s) {
-    if (s < ntiles) load_tile(s, s);
-    cp_async_commit();
+  // key scale/min of tile `tile`, regrouped per lane column into buffer tile & 1 (one
+  // channel per thread); reads a chunk that every thread's copies filled
+  auto regroup = [&](int tile) {
+    const uint8_t* kc = smem + L::OFF_KC + ((tile / kKChunk) & 1) * L::KC_BYTES + threadIdx.x * L::KC_ROW +
+                        (tile % kKChunk) * 8;
+    const uint2 s4 = *reinterpret_cast<const uint2*>(kc);
+    const uint2 m4 = *reinterpret_cast<const uint2*>(kc + 128 * L::KC_ROW);
+    uint8_t* ts = tsm + (tile & 1) * L::T_BYTES + t_slot;
+    *reinterpret_cast<uint16_t*>(ts + 0 * L::T_GROUP) = uint16_t(s4.x);
+    *reinterpret_cast<uint16_t*>(ts + 1 * L::T_GROUP) = uint16_t(s4.x >> 16);
+    *reinterpret_cast<uint16_t*>(ts + 2 * L::T_GROUP) = uint16_t(s4.y);
+    *reinterpret_cast<uint16_t*>(ts + 3 * L::T_GROUP) = uint16_t(s4.y >> 16);
+    *reinterpret_cast<uint16_t*>(ts + 4 * L::T_GROUP) = uint16_t(m4.x);
+    *reinterpret_cast<uint16_t*>(ts + 5 * L::T_GROUP) = uint16_t(m4.x >> 16);
+    *reinterpret_cast<uint16_t*>(ts + 6 * L::T_GROUP) = uint16_t(m4.y);
+    *reinterpret_cast<uint16_t*>(ts + 7 * L::T_GROUP) = uint16_t(m4.y >> 16);
+  };
+
+  // prologue: tile 0 and the first key scale/min chunk in flight
+  if (ntiles > 0) {
+    load_tile(0, 0);
+    load_chunk(0);
   }
+  cp_async_commit();
 
   // the query loads follow the first tile copies, so their latencies overlap
   // query of head g as f16 pairs in MMA k order: qh[j][0] = channels 16j+2tq,+1;
@@ -353,34 +373,27 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
     kmul[f] = BITS == 2 ? __int_as_float((127 + 24 - 2 * f) << 23) * score_mul : subK * score_mul;
 
 
+  // tile 0's key scale/min regrouped before the loop; each iteration regroups the next
+  // tile's while this one computes, so one barrier per tile orders both buffers
+  cp_async_wait<0>();
+  __syncthreads();
+  if (ntiles > 0) regroup(0);
+
   for (int it = 0; it < ntiles; ++it) {
-    cp_async_wait<kStagesK - 2>();  // key scale/min chunks (and, without TMA, the tile)
+    // outstanding cp.async: the next key scale/min chunk (and, without TMA, this tile)
+    cp_async_wait<0>();
     if (TMA && !mbar_wait(bar0 + 8 * (it % kStagesK), (it / kStagesK) & 1) && threadIdx.x == 0)
       atomicAdd(&g_kivi_tma_timeouts, 1u);
+    // this tile landed, the regrouped scales of this tile are visible, and every thread is
+    // done with the previous tile's stage and scale buffer
     __syncthreads();
-    {
-      const int nxt = it + kStagesK - 1;
-      if (nxt < ntiles) load_tile(nxt, nxt % kStagesK);
-      cp_async_commit();
-    }
+    if (it + 1 < ntiles) load_tile(it + 1, (it + 1) % kStagesK);
+    // the chunk after next, into the buffer whose last reader was the regroup of tile it
+    if (it % kKChunk == 0 && it + kKChunk < ntiles) load_chunk(it + kKChunk);
+    cp_async_commit();
+    if (it + 1 < ntiles) regroup(it + 1);
     const uint8_t* st = smem + (it % kStagesK) * L::STAGE;
-    {
-      // regroup key scale / min of this tile per lane column (one channel per thread)
-      const uint8_t* kc = smem + L::OFF_KC + ((it / kKChunk) & 1) * L::KC_BYTES + threadIdx.x * L::KC_ROW +
-                          (it % kKChunk) * 8;
-      const uint2 s4 = *reinterpret_cast<const uint2*>(kc);
-      const uint2 m4 = *reinterpret_cast<const uint2*>(kc + 128 * L::KC_ROW);
-      uint8_t* ts = tsm + t_slot;
-      *reinterpret_cast<uint16_t*>(ts + 0 * L::T_GROUP) = uint16_t(s4.x);
-      *reinterpret_cast<uint16_t*>(ts + 1 * L::T_GROUP) = uint16_t(s4.x >> 16);
-      *reinterpret_cast<uint16_t*>(ts + 2 * L::T_GROUP) = uint16_t(s4.y);
-      *reinterpret_cast<uint16_t*>(ts + 3 * L::T_GROUP) = uint16_t(s4.y >> 16);
-      *reinterpret_cast<uint16_t*>(ts + 4 * L::T_GROUP) = uint16_t(m4.x);
-      *reinterpret_cast<uint16_t*>(ts + 5 * L::T_GROUP) = uint16_t(m4.x >> 16);
-      *reinterpret_cast<uint16_t*>(ts + 6 * L::T_GROUP) = uint16_t(m4.y);
-      *reinterpret_cast<uint16_t*>(ts + 7 * L::T_GROUP) = uint16_t(m4.y >> 16);
-    }
-    __syncthreads();
+    const uint8_t* tsc = tsm + (it & 1) * L::T_BYTES;
     const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
     if (tb >= t_end) continue;
 
@@ -391,8 +404,8 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
     uint32_t qb[8][2];
     float bias[2];
     {
-      const uint4* tsr = reinterpret_cast<const uint4*>(tsm + warp * L::T_GROUP + tq * L::T_COL);
-      const uint4* tmr = reinterpret_cast<const uint4*>(tsm + (4 + warp) * L::T_GROUP + tq * L::T_COL);
+      const uint4* tsr = reinterpret_cast<const uint4*>(tsc + warp * L::T_GROUP + tq * L::T_COL);
+      const uint4* tmr = reinterpret_cast<const uint4*>(tsc + (4 + warp) * L::T_GROUP + tq * L::T_COL);
       float be[4] = {0.f, 0.f, 0.f, 0.f}, bo[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
