@@ -10,8 +10,9 @@
 //  * The GQA group makes QK^T a dense contraction: S^T[16 tokens x 8 heads] =
 //    K[16 x D] . Q^T[D x 8] on the tensor cores (mma.sync m16n8k16, bf16 or f16 in,
 //    fp32 accumulate). Every K/V byte is read from HBM once per KV head, not G times.
-//  * Online softmax in exp2 space on the accumulator fragments; P is transposed in
-//    registers (movmatrix) into the B operand of O^T[D x 8] += V^T[D x 16] . P^T[16 x 8].
+//  * Online softmax in exp2 space on the accumulator fragments, its reference moved
+//    lazily; P is transposed in registers (movmatrix) into the B operand of
+//    O^T[D x 8] += V^T[D x 16] . P^T[16 x 8].
 //  * Warps merge through shared memory; splits merge in a log-sum-exp combine kernel.
 // fp8 keys/values are widened to f16 (exact) in registers; the query is fed as f16,
 // pre-scaled by a power of two when its magnitude would exceed the f16 range.
@@ -31,6 +32,10 @@ constexpr int kRows = 16 * kWarps;  // tokens per tile
 constexpr int kStages = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+// log2 headroom of the lazily moved softmax reference. Zero: the reference is the running
+// maximum as in plain online softmax (the largest weight of a tile that moved it is exactly
+// 1, which keeps bf16 P exact there); only the rescale is skipped when no score passes it.
+constexpr float kHeadroomD = 0.f;
 
 struct DenseParams {
   const void* q; int64_t q_sb, q_sh; int q_dtype;
@@ -242,27 +247,40 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
     uint32_t pb[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      float pv[4];
+      // mrow moves only when a score passes it (to that score + kHeadroomD); the head maxima
+      // are reduced over the warp and the running sums rescaled only then
+      float pv[4], a[2], c[2], mx[2];
+      bool grow = false;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const float a = v0 ? s[nt][j] * score_mul : -INFINITY;
-        const float c = v1 ? s[nt][2 + j] * score_mul : -INFINITY;
-        float mx = fmaxf(a, c);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mnew = fmaxf(mrow[nt][j], mx);
-        const float muse = mnew == -INFINITY ? 0.f : mnew;
-        const float alpha = exp2f(mrow[nt][j] - muse);
-        pv[j] = exp2f(a - muse);
-        pv[2 + j] = exp2f(c - muse);
-        lrow[nt][j] = lrow[nt][j] * alpha + pv[j] + pv[2 + j];
-        mrow[nt][j] = mnew;
+        a[j] = v0 ? s[nt][j] * score_mul : -INFINITY;
+        c[j] = v1 ? s[nt][2 + j] * score_mul : -INFINITY;
+        mx[j] = fmaxf(a[j], c[j]);
+        grow |= mx[j] > mrow[nt][j];
+      }
+      if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-        for (int mt = 0; mt < KSTEPS; ++mt) {
-          o[mt][nt][j] *= alpha;
-          o[mt][nt][2 + j] *= alpha;
+        for (int j = 0; j < 2; ++j) {
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 4));
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 8));
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 16));
+          const float mnew = mx[j] > mrow[nt][j] ? mx[j] + kHeadroomD : mrow[nt][j];
+          const float alpha = mrow[nt][j] == -INFINITY ? 0.f : fast_exp2(mrow[nt][j] - mnew);
+          mrow[nt][j] = mnew;
+          lrow[nt][j] *= alpha;
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt) {
+            o[mt][nt][j] *= alpha;
+            o[mt][nt][2 + j] *= alpha;
+          }
         }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float muse = mrow[nt][j] == -INFINITY ? 0.f : mrow[nt][j];
+        pv[j] = fast_exp2(a[j] - muse);
+        pv[2 + j] = fast_exp2(c[j] - muse);
+        lrow[nt][j] += pv[j] + pv[2 + j];
       }
       if (FP8) {
         pb[nt][0] = movmatrix_trans(pack_f16x2(pv[0], pv[1]));

@@ -387,14 +387,17 @@ __global__ void __launch_bounds__(kPW * 32, 2)
       for (int j = 0; j < 2; ++j) {
         a[j] = va ? sc[j] * kLog2eP : -INFINITY;
         c[j] = vb ? sc[2 + j] * kLog2eP : -INFINITY;
-        float m = fmaxf(a[j], c[j]);
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-        mx[j] = m;
-        grow |= m > mrow[j];
+        mx[j] = fmaxf(a[j], c[j]);
+        grow |= mx[j] > mrow[j];
       }
+      // the head maxima are reduced over the warp only when some score passed the reference
       if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 4));
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 8));
+          mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 16));
+        }
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const float mnew = mx[j] > mrow[j] ? mx[j] + kPHeadroom : mrow[j];
