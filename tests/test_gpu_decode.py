@@ -144,6 +144,7 @@ def test_kivi_pack_bit_exact(cuda, bits):
     (1, 16, 1, 1024 + 5, 5),      # G=16 (two head chunks)
     (2, 4, 4, 96, 0),             # no residual window
     (1, 7, 1, 512 + 300, 300),    # window longer than a tile: spread over three splits
+    (1, 7, 1, 40000 + 64, 64),    # long packed pass (> 256 tiles): the four-CTAs-per-SM build
 ])
 def test_kivi_decode_matches_oracle(cuda, bits, B, Hq, Hk, S, R):
     D = 128
