@@ -274,6 +274,10 @@ __global__ void __launch_bounds__(kPW * 32, 2)
   };
 
   float o[KSTEPS][4];
+  // int8 values enter the MMA as 1152 + x (the f16 halves 0x64XX, XX = x ^ 0x80); oc
+  // accumulates 1152 * sum_t P'_t with the same f16 P' (one MMA of a constant operand per
+  // tile) and is subtracted from every channel at the end
+  float oc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int mt = 0; mt < KSTEPS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
@@ -409,6 +413,8 @@ __global__ void __launch_bounds__(kPW * 32, 2)
             o[mt][j] *= alpha;
             o[mt][2 + j] *= alpha;
           }
+          oc[j] *= alpha;
+          oc[2 + j] *= alpha;
         }
       }
 #pragma unroll
@@ -469,19 +475,16 @@ __global__ void __launch_bounds__(kPW * 32, 2)
             a[2 * u] = e4m3x2_to_f16x2(prmt(xs[u], 0, 0x0020));
             a[2 * u + 1] = e4m3x2_to_f16x2(prmt(xs[u], 0, 0x0031));
           } else {
-            // int8 -> f16: halves 0x64xx with xx = x ^ 0x80 are 1024 + x + 128, minus 1152
-            const __half2 off = __floats2half2_rn(1152.f, 1152.f);
-            const uint32_t e0 = prmt(xs[u], 0x64646464u, 0x4240) ^ 0x00800080u;
-            const uint32_t e1 = prmt(xs[u], 0x64646464u, 0x4341) ^ 0x00800080u;
-            const __half2 h0v = __hsub2(*reinterpret_cast<const __half2*>(&e0), off);
-            const __half2 h1v = __hsub2(*reinterpret_cast<const __half2*>(&e1), off);
-            a[2 * u] = *reinterpret_cast<const uint32_t*>(&h0v);
-            a[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&h1v);
+            // int8 -> f16 halves 0x64XX, XX = x ^ 0x80: the value 1024 + x + 128 (one
+            // byte-select PRMT and one XOR per register); the 1152 comes off through oc
+            a[2 * u] = prmt(xs[u], 0x64646464u, 0x4240) ^ 0x00800080u;
+            a[2 * u + 1] = prmt(xs[u], 0x64646464u, 0x4341) ^ 0x00800080u;
           }
         }
         mma_f16(o[2 * m2], a[0], a[1], a[2], a[3], pb0, pb1);
         mma_f16(o[2 * m2 + 1], a[4], a[5], a[6], a[7], pb0, pb1);
       }
+      if (VK == V_INT8) mma_f16(oc, 0x64806480u, 0x64806480u, 0x64806480u, 0x64806480u, pb0, pb1);
     }
   }
   if (VK == V_NONE) return;
@@ -521,8 +524,9 @@ __global__ void __launch_bounds__(kPW * 32, 2)
         const bool wide = (VK == V_FP8 || VK == V_INT8);
         const int ca = wide ? mt * 16 + 2 * g : mt * 16 + g;
         const int cb = wide ? ca + 1 : ca + 8;
-        red_o[(warp * kHC + h) * D + ca] = o[mt][j] * f;
-        red_o[(warp * kHC + h) * D + cb] = o[mt][2 + j] * f;
+        // (oc is zero unless the values are int8)
+        red_o[(warp * kHC + h) * D + ca] = (o[mt][j] - oc[j]) * f;
+        red_o[(warp * kHC + h) * D + cb] = (o[mt][2 + j] - oc[2 + j]) * f;
       }
     }
   }
