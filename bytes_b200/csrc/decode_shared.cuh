@@ -51,6 +51,25 @@ int launch_combine_export(const Partials& part, int B, int Hq, int D, float* em,
 int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* out, cudaStream_t st,
                    bool pdl = false);
 
+// Launch `kern` with the programmatic stream serialization attribute, any parameter list.
+// The kernel may then start while the previous kernel in the stream is finishing, so it
+// must call griddep_wait() before it reads or writes global memory.
+template <typename... Params, typename... Args>
+int launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char* what,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...), what);
+}
+
 // Launch `kern` with the programmatic stream serialization attribute.
 template <typename Params>
 int launch_programmatic(void (*kern)(Params), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

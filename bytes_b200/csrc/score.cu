@@ -14,6 +14,7 @@
 // AND give two MMA operands. Per-token scale/zero enter in fp32 after the contraction:
 // score = sum_g s_g * (sum_{c in g} q_c code_c) + z_g * (sum_{c in g} q_c).
 #include "common.cuh"
+#include "decode_shared.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -64,6 +65,8 @@ __device__ __forceinline__ float h16_to_f(uint16_t u, int is_bf16) {
 
 template <int KT, int D, int NT>
 __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   using L = SL<KT, D>;
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int KSTEPS = D / 16;
@@ -335,8 +338,7 @@ int launch_score(const ScoreParams& p, int n_splits, cudaStream_t st) {
     attr[dev & 63] = true;
   }
   dim3 grid(n_splits, p.Hk * p.head_chunks, p.B);
-  kern<<<grid, kSW * 32, smem, st>>>(p);
-  return cuda_check(cudaGetLastError(), "score_kernel launch");
+  return launch_programmatic(kern, grid, dim3(kSW * 32), smem, st, p, "score_kernel launch");
 }
 
 template <int KT, int D>

@@ -13,6 +13,11 @@
 // compaction then emits every key > T plus the lowest-index keys == T, in ascending index
 // order. Ties are therefore broken by lower index, exactly like a stable descending sort.
 // Optionally the k winners are bitonic-sorted by (key desc, index asc).
+//
+// The kernels of a selection chain (Quest bounds -> top-k -> page expansion -> gather, and
+// scores -> top-k -> gather) are programmatic launches: each waits (griddepcontrol.wait)
+// before touching global memory, so its CTAs are resident when the previous kernel ends.
+// The one-CTA-per-SM top-k kernels for long rows are launched plainly.
 #include "common.cuh"
 #include "decode_shared.cuh"
 
@@ -126,6 +131,8 @@ constexpr int kWarpCand = kCandMax / kTkWarps;  // candidate slots per warp
 // indices; the remaining 20 bits (12 + 8) are resolved on those candidates only, or on the
 // whole row if they overflow kCandMax. Selection and ordering rules as topk_kernel.
 __global__ void __launch_bounds__(kTkThreads, 1) topk_fast_kernel(const TopkParams p) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ int red[33];
   __shared__ int s_digit, s_above, s_overflow;
@@ -426,6 +433,8 @@ __device__ __forceinline__ int small_excl_scan(int v, int* red, int* total) {
 
 template <int PER>
 __global__ void __launch_bounds__(kSmThreads, 4) topk_small_kernel(const TopkParams p) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   extern __shared__ __align__(16) uint8_t smem[];  // sorted output: [kpow] keys, [kpow] indices
   __shared__ int hist[2][256];
   __shared__ int red[33];
@@ -633,6 +642,8 @@ __global__ void __launch_bounds__(kSmThreads, 4) topk_small_kernel(const TopkPar
 
 template <bool SMEM_ROW>
 __global__ void __launch_bounds__(kTkThreads, 1) topk_kernel(const TopkParams p) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ int hist[256];
   __shared__ int red[33];
@@ -811,6 +822,7 @@ struct GatherParams {
 
 template <int D, bool FP8>
 __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
   griddep_launch_dependents();  // the combine queued behind may start launching (it waits for this grid)
   constexpr int CPL = D / 8;  // channels per lane (8 lanes per row)
   constexpr int ELT = FP8 ? 1 : 2;
@@ -998,6 +1010,8 @@ __global__ void __launch_bounds__(kQPages) quest_bounds_kernel(const void* q, in
                                                          const __nv_bfloat16* kmin, const __nv_bfloat16* kmax,
                                                          int64_t m_sb, int64_t m_sh, int64_t m_sp, int Hq, int Hk,
                                                          int np, float scaling, int force_from, float* bounds) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   constexpr int PITCH = D * 2 + 16;
   __shared__ __align__(16) uint8_t sm[2][kQPages * PITCH];
   const int b = blockIdx.z, hk = blockIdx.y, p0 = blockIdx.x * kQPages;
@@ -1073,6 +1087,8 @@ struct QuestMmaParams {
 // while this one's bounds are computed); the query fragments are built once per CTA.
 template <int D>
 __global__ void __launch_bounds__(128) quest_bounds_mma_kernel(const QuestMmaParams p) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   constexpr int ROWB = 4 * D;        // [max | min] bf16 bytes per page
   constexpr int PITCH = ROWB + 16;   // padded row
   constexpr int CH = ROWB / 16;      // 16-byte chunks per page
@@ -1144,6 +1160,8 @@ __global__ void __launch_bounds__(128) quest_bounds_mma_kernel(const QuestMmaPar
 
 __global__ void quest_expand_kernel(const int64_t* pidx, int npick, int page, int S, int rows, void* out, int out64,
                                     int64_t o_rs) {
+  griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
+  griddep_launch_dependents();
   const int row = blockIdx.y;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= npick * page || row >= rows) return;
@@ -1172,10 +1190,9 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
   int rc;
   if (n > 0 && n <= kSmRowMax && (!sorted || kk <= kSmSortMax)) {
     const size_t sm = sorted ? wbytes : 0;
-    if (n <= kSmThreads * 4) topk_small_kernel<4><<<rows, kSmThreads, sm, st>>>(p);
-    else if (n <= kSmThreads * 8) topk_small_kernel<8><<<rows, kSmThreads, sm, st>>>(p);
-    else topk_small_kernel<16><<<rows, kSmThreads, sm, st>>>(p);
-    return cuda_check(cudaGetLastError(), "topk_small_kernel launch");
+    auto kern = n <= kSmThreads * 4 ? topk_small_kernel<4> : n <= kSmThreads * 8 ? topk_small_kernel<8>
+                                                                                 : topk_small_kernel<16>;
+    return launch_programmatic(kern, dim3(rows), dim3(kSmThreads), sm, st, p, "topk_small_kernel launch");
   }
   const size_t fast_smem = size_t(n) * 4 + 4096 * 4 + size_t(kCandMax) * 4 + wbytes;
   const bool aligned = (reinterpret_cast<uintptr_t>(scores) & 15) == 0 && row_stride % 4 == 0 &&
@@ -1191,6 +1208,8 @@ int run_topk(const float* scores, int rows, int rows_per_b, int64_t b_stride, in
         return rc;
       attr_f[dev & 63] = true;
     }
+    // a plain launch: launched early behind the score pass, these one-per-SM CTAs measured
+    // 20 us slower at c3's shape
     topk_fast_kernel<<<rows, kTkThreads, fast_smem, st>>>(p);
     return cuda_check(cudaGetLastError(), "topk_fast_kernel launch");
   }
@@ -1352,16 +1371,16 @@ static int sparse_gather_run(const bd_tensor* q, const bd_tensor* k, const bd_te
   dim3 grid(nsplit, unsigned(Hq), unsigned(B));
   const bool fp8 = k->dtype == BD_F8E4M3;
   if (D == 128) {
-    if (fp8) gather_attn_kernel<128, true><<<grid, 128, 0, st>>>(p);
-    else gather_attn_kernel<128, false><<<grid, 128, 0, st>>>(p);
+    rc = launch_programmatic(fp8 ? gather_attn_kernel<128, true> : gather_attn_kernel<128, false>, grid, dim3(128), 0,
+                             st, p, "gather_attn_kernel launch");
   } else if (D == 64) {
-    if (fp8) gather_attn_kernel<64, true><<<grid, 128, 0, st>>>(p);
-    else gather_attn_kernel<64, false><<<grid, 128, 0, st>>>(p);
+    rc = launch_programmatic(fp8 ? gather_attn_kernel<64, true> : gather_attn_kernel<64, false>, grid, dim3(128), 0,
+                             st, p, "gather_attn_kernel launch");
   } else {
-    if (fp8) gather_attn_kernel<32, true><<<grid, 128, 0, st>>>(p);
-    else gather_attn_kernel<32, false><<<grid, 128, 0, st>>>(p);
+    rc = launch_programmatic(fp8 ? gather_attn_kernel<32, true> : gather_attn_kernel<32, false>, grid, dim3(128), 0,
+                             st, p, "gather_attn_kernel launch");
   }
-  if ((rc = cuda_check(cudaGetLastError(), "gather_attn_kernel launch"))) return rc;
+  if (rc) return rc;
   if (direct) return BD_OK;
   if (out) return launch_combine(part, int(B), int(Hq), int(D), out, st, true);
   return launch_combine_export(part, int(B), int(Hq), int(D), static_cast<float*>(em->data),
@@ -1469,27 +1488,17 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
         if (r) return r;
         attr[dev & 63] = true;
       }
-      kern<<<gm, 128, smem, st>>>(p);
-      return cuda_check(cudaGetLastError(), "quest_bounds_mma_kernel launch");
+      return launch_programmatic(kern, gm, dim3(128), smem, st, p, "quest_bounds_mma_kernel launch");
     };
     if (D == 128) return launch(quest_bounds_mma_kernel<128>);
     if (D == 64) return launch(quest_bounds_mma_kernel<64>);
     return launch(quest_bounds_mma_kernel<32>);
   }
   dim3 grid(unsigned((np + kQPages - 1) / kQPages), unsigned(Hk), unsigned(B));
-  if (D == 128)
-    quest_bounds_kernel<128><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
-        kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
-        static_cast<float*>(bounds->data));
-  else if (D == 64)
-    quest_bounds_kernel<64><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
-        kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
-        static_cast<float*>(bounds->data));
-  else
-    quest_bounds_kernel<32><<<grid, kQPages, 0, st>>>(q->data, q->dtype, q->stride[0], q->stride[1], mn, mx,
-        kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling, force_from_page,
-        static_cast<float*>(bounds->data));
-  return cuda_check(cudaGetLastError(), "quest_bounds_kernel launch");
+  auto kern = D == 128 ? quest_bounds_kernel<128> : D == 64 ? quest_bounds_kernel<64> : quest_bounds_kernel<32>;
+  return launch_pdl(kern, grid, dim3(kQPages), 0, st, "quest_bounds_kernel launch", q->data, q->dtype, q->stride[0],
+                    q->stride[1], mn, mx, kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np),
+                    scaling, force_from_page, static_cast<float*>(bounds->data));
 }
 
 size_t bd_quest_select_workspace(const bd_tensor* q, const bd_tensor* kmin, int kb, int page) {
@@ -1533,9 +1542,9 @@ int bd_quest_select(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* 
   if ((rc = run_topk(bounds, int(rows), int(rows), 0, np, int(np), int(npick), nullptr, 0, pidx, 1, npick, 1, st)))
     return rc;
   dim3 grid(unsigned((npick * page + 255) / 256), unsigned(rows));
-  quest_expand_kernel<<<grid, 256, 0, st>>>(pidx, int(npick), page, S, int(rows), idx_out->data,
-                                            idx_out->dtype == BD_I64, npick * page);
-  return cuda_check(cudaGetLastError(), "quest_expand_kernel launch");
+  return launch_pdl(quest_expand_kernel, grid, dim3(256), 0, st, "quest_expand_kernel launch",
+                    static_cast<const int64_t*>(pidx), int(npick), page, S, int(rows), idx_out->data,
+                    int(idx_out->dtype == BD_I64), int64_t(npick * page));
 }
 
 }  // extern "C"
