@@ -1,0 +1,51 @@
+"""A transformers Llama (random weights, bf16) decoding through the bytes_b200 attention.
+
+Teacher-forced decode steps after a prefill: the logits of every step with the bytes_b200
+attention implementation must match those with transformers' SDPA attention, and the
+kernel path must have served each layer of each step.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(cuda):
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.LlamaConfig(vocab_size=512, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                                   max_position_embeddings=1024)
+    torch.manual_seed(0)
+    return transformers.LlamaForCausalLM(cfg).to(device=cuda, dtype=torch.bfloat16).eval()
+
+
+def _decode_logits(model, impl, prompt, forced):
+    model.set_attn_implementation(impl)
+    steps = []
+    with torch.no_grad():
+        out = model(prompt, use_cache=True)
+        past = out.past_key_values
+        for t in range(forced.shape[1]):
+            out = model(forced[:, t:t + 1], past_key_values=past, use_cache=True)
+            past = out.past_key_values
+            steps.append(out.logits[:, -1].float())
+    return torch.stack(steps)
+
+
+def test_llama_decode_steps_match_sdpa(cuda):
+    from bytes_b200 import hf_attention
+    name = hf_attention.register()
+    model = _model(cuda)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, 512, (2, 300), generator=g).to(cuda)
+    forced = torch.randint(0, 512, (2, 8), generator=g).to(cuda)
+    ref = _decode_logits(model, "sdpa", prompt, forced)
+    before = hf_attention.calls
+    got = _decode_logits(model, name, prompt, forced)
+    assert hf_attention.calls - before == 8 * 2  # every decode step of both layers on the kernel
+    d = (got - ref).abs()
+    scale = ref.abs().max().item()
+    assert torch.isfinite(got).all()
+    # bf16 model: attention outputs rounded to bf16 on both paths, two layers deep
+    assert d.max().item() <= 2e-2 * max(scale, 1.0), (d.max().item(), scale)
+    assert d.mean().item() <= 2e-3 * max(scale, 1.0), (d.mean().item(), scale)
