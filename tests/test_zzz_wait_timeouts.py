@@ -1,4 +1,5 @@
-"""Collected last: no bounded device wait (TMA tile barriers of the KIVI and PQ kernels,
+"""Collected after every kernel test (only the no-alloc entry point's own test follows; its
+dense kernels have no bounded waits): no bounded device wait (TMA tile barriers of the KIVI and PQ kernels,
 the bulk copy of the window-merge pass) ran past its iteration limit during this GPU
 session — every tile those tests checked arrived before its consumers read it."""
 import ctypes

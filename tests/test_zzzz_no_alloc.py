@@ -5,6 +5,9 @@ holding only the q/k/v/out buffers, cannot hand the engine a workspace. This ent
 keeps its split partials in a fixed device array inside the library instead. The test
 calls it through the C ABI twice in a row (the array keeps the previous call's contents)
 and compares each result with bd_decode_attn given a normal workspace.
+
+This file is collected last (after test_zzz_wait_timeouts.py), so a run that stops at the
+first failure has run every other test before it.
 """
 import ctypes
 
