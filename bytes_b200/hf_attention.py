@@ -157,6 +157,27 @@ def _kivi_layer_class():
             k._bytes_kivi = self
             return k, v
 
+        def _batch_apply(self, fn):
+            # every buffer has batch first: packed codes, scales, minima and the window
+            for name in ("Kq", "Ks", "Km", "Vq", "Vs", "Vm", "res_k", "res_v"):
+                setattr(self, name, fn(getattr(self, name)).contiguous())
+            self.keys, self.values = self.res_k, self.res_v
+
+        def reorder_cache(self, beam_idx):
+            if self.is_initialized:
+                self._batch_apply(lambda t: t.index_select(0, beam_idx.to(t.device)))
+
+        def batch_repeat_interleave(self, repeats):
+            if self.is_initialized:
+                self._batch_apply(lambda t: t.repeat_interleave(repeats, dim=0))
+
+        def batch_select_indices(self, indices):
+            if self.is_initialized:
+                self._batch_apply(lambda t: t[indices])
+
+        def crop(self, max_length):
+            raise NotImplementedError("KiviCache: packed tokens cannot be cropped")
+
         def get_mask_sizes(self, query_length):
             return self.cumulative_length + query_length, 0
 

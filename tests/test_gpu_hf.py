@@ -102,3 +102,25 @@ def test_llama_kivi_cache_decode_matches_oracle(cuda, bits):
     assert torch.isfinite(got).all()
     assert d.max().item() <= 2e-2 * max(scale, 1.0), (d.max().item(), scale)
     assert d.mean().item() <= 2e-3 * max(scale, 1.0), (d.mean().item(), scale)
+
+
+def test_kivi_cache_reorder_follows_the_batch(cuda):
+    """Beam-search reordering moves packed codes, scales, minima and window together: a
+    reordered cache decodes exactly like the original one with the batch rows swapped."""
+    from bytes_b200 import hf_attention
+    name = hf_attention.register()
+    model = _model(cuda)
+    model.set_attn_implementation(name)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, 512, (2, 260), generator=g).to(cuda)
+    nxt = torch.randint(0, 512, (2, 1), generator=g).to(cuda)
+    with torch.no_grad():
+        a = hf_attention.KiviCache(model.config, bits=2, residual=128, max_tokens=512)
+        model(prompt, past_key_values=a, use_cache=True)
+        la = model(nxt, past_key_values=a, use_cache=True).logits[:, -1].float()
+        b = hf_attention.KiviCache(model.config, bits=2, residual=128, max_tokens=512)
+        model(prompt, past_key_values=b, use_cache=True)
+        b.reorder_cache(torch.tensor([1, 0], device=cuda))
+        lb = model(nxt.flip(0), past_key_values=b, use_cache=True).logits[:, -1].float()
+    d = (la - lb.flip(0)).abs().max().item()
+    assert d <= 1e-3 * max(la.abs().max().item(), 1.0), d
