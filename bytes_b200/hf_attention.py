@@ -24,6 +24,8 @@ window. Prefill attention stays full precision (SDPA over the prompt).
     cache = hf_attention.KiviCache(model.config, bits=2, residual=128, max_tokens=4096)
     model(prompt, past_key_values=cache, use_cache=True)        # then decode steps as usual
 """
+import functools
+
 import torch
 
 from . import _ops
@@ -80,7 +82,9 @@ def register(name=NAME):
     return name
 
 
+@functools.lru_cache(maxsize=None)
 def _kivi_layer_class():
+    # built on first use, so importing this module does not import transformers
     from transformers.cache_utils import CacheLayerMixin
 
     class KiviLayer(CacheLayerMixin):
