@@ -1,27 +1,35 @@
 #!/usr/bin/env python
 """Decode-attention benchmark: prints ONE JSON line (rank 0).
 
-Headline workload (config 1 of the reference study's B200 plan): KIVI-style 2-bit KV
-cache decode, batch 8 per GPU, 28 query / 4 KV heads, head_dim 128, context 16384 of which
-the last 128 tokens are a bf16 residual window; keys quantised per channel over groups of
-32 tokens, values per token over groups of 32 channels (f16 scale / minimum). Synthetic
-seeded inputs (N(0,1) bf16 with 4 of 128 key channels x8), packed once by the engine's own
-packer before timing.
+Headline workload: KIVI-style 2-bit KV-cache decode at the metric's 32K context with the
+config-1 head shapes: batch 8 per GPU, 28 query / 4 KV heads, head_dim 128, context 32768
+of which the last 128 tokens are a bf16 residual window; keys quantised per channel over
+groups of 32 tokens, values per token over groups of 32 channels (f16 scale / minimum).
+Synthetic seeded inputs (N(0,1) bf16 with 4 of 128 key channels x8), packed once by the
+engine's own packer before timing.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...   (batch-sharded, weak scaling)
 
-value      device time per decode step (µs, max over ranks), CUDA-graph replay of the
-           public API call with the packed cache resident in HBM; 8 rotating input sets
-           (416 MB > 3x L2) so no step reads its inputs from L2.
-e2e        the same step through the public Python API with host buffers: every step copies
-           its queries host->device from pinned memory and reads the output back.
-roofline   the packed-cache kernel alone (no residual window / combine), algorithmic bytes
-           per launch / its CUDA-event time, against MEASURED_PEAKS.json's copy bandwidth.
-cpu_baseline / --impl reference: the CPU oracle (a fp32 torch restatement of the
-           reference's kivi_decode_attn) on the host cores.
+value      device time per decode step (us, max over ranks): a CUDA graph of exactly K
+           steps of the public API call, replayed once after a graph of exactly W warm-up
+           steps; the steps rotate over 4 input sets (416 MB > 3x L2) so no step reads its
+           inputs from L2.
+e2e        the same K steps through the public Python API with host buffers: every step
+           copies its queries host->device from pinned memory and reads the output back.
+roofline   the packed-cache kernel alone (no residual window), algorithmic bytes per launch
+           / its CUDA-event time, against MEASURED_PEAKS.json's copy bandwidth.
+cpu_baseline / --impl reference: the reference's own CPU-runnable KIVI path
+           (benchmarks/kivi_latency.py dequant_k + dequant_v + kivi_decode_attn_ref, from
+           the installed reference in baseline/_ref), else the fp32 torch restatement of it
+           in oracle/, on the host cores.
+split_kv   (every N) one 1M-token bf16 sequence split across the N ranks: per-rank split-KV
+           partial, one NCCL all-gather of the (max, sum, numerator) partials and the
+           log-sum-exp combine inside the timed step; the result is checked against
+           single-GPU decode of the whole sequence before timing (parity_ok).
 """
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -37,8 +45,17 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "decode-attn µs/step & HBM GB/s (% of 8 TB/s) at 32K ctx; top-k select µs"
-CFG1 = dict(B=8, Hq=28, Hk=4, D=128, S=16384, R=128, bits=2, group=32)
-NBUF = 8
+HEAD = dict(B=8, Hq=28, Hk=4, D=128, S=32768, R=128, bits=2, group=32)  # config-1 heads at 32K
+CFG1 = dict(HEAD, S=16384)  # config 1 as stated (16K context)
+NBUF = 4
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "kivi_decode_kernel_32k.traffic.json")
+KIVI_SOURCES = ("bytes_b200/csrc/kivi.cu", "bytes_b200/csrc/common.cuh")
+
+
+def _workload(c):
+    return (f"KIVI-{c['bits']} decode B={c['B']} Hq={c['Hq']} Hk={c['Hk']} D={c['D']} S={c['S']} R={c['R']} "
+            f"group={c['group']}")
 
 
 def _metric():
@@ -66,20 +83,30 @@ def _host_cores():
         return os.cpu_count() or 1
 
 
-def _profile_traffic(name):
-    """bytes per launch from a committed ncu summary line 'traffic_bytes_per_launch: N'."""
-    path = os.path.join(ROOT, "profiles", name)
+def _sources_sha():
+    h = hashlib.sha256()
+    for rel in KIVI_SOURCES:
+        with open(os.path.join(ROOT, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
+def _measured_traffic(workload):
+    """DRAM bytes per launch of the packed-cache kernel from an ncu capture recorded for
+    the current kernel sources and this workload; None when no such record exists (a
+    record made for other sources is stale and not used)."""
     try:
-        for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return int(float(line.split(":", 1)[1].strip()))
+        with open(TRAFFIC_FILE) as f:
+            rec = json.load(f)
+        if rec.get("source_sha256") == _sources_sha() and rec.get("workload") == workload:
+            return int(rec["dram_bytes_per_launch"])
     except Exception:
         pass
     return None
 
 
 # ----------------------------------------------------------------------------- inputs
-def kivi_inputs(dev, seed, c=CFG1):
+def kivi_inputs(dev, seed, c=HEAD):
     from bytes_b200 import kivi as kv
     g = torch.Generator(device=dev).manual_seed(seed)
     B, Hq, Hk, D, S, R = c["B"], c["Hq"], c["Hk"], c["D"], c["S"], c["R"]
@@ -148,17 +175,20 @@ class ClockSampler:
             self.max = None
         self._stop = threading.Event()
 
-    def _run(self):
+    def _sample(self):
         nv = self.nv
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
+            self._sample()
             time.sleep(0.005)
 
     def __enter__(self):
@@ -171,6 +201,8 @@ class ClockSampler:
         if self.ok:
             self._stop.set()
             self.t.join()
+            if not self.samples:
+                self._sample()  # a timed region shorter than one polling interval
 
     def summary(self):
         if not self.ok or not self.samples:
@@ -180,26 +212,56 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU side
-def cpu_kivi_step(inputs_cpu, b=None, tok_frac=1.0):
-    """The oracle's KIVI step on host cores; optional sample of one sequence / a token slice."""
+def _reference_kivi():
+    """The reference's own KIVI helpers (benchmarks/kivi_latency.py) from the installed
+    reference, or None. Its module insists on a KIVI checkout at import; the engine's
+    ``quant`` shim satisfies that (only the pure-torch helpers are called here)."""
+    if not os.path.isdir(os.path.join(REF_DIR, "benchmarks")):
+        return None
+    os.environ.setdefault("KIVI_REPO", os.path.join(ROOT, "bytes_b200", "kivi_shim"))
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    try:
+        import importlib
+        return importlib.import_module("benchmarks.kivi_latency")
+    except Exception:
+        return None
+
+
+def cpu_step_fn(c):
+    """(step(inputs, b, tok_frac), kind, what) for one sequence of the KIVI step on the host."""
+    kl = _reference_kivi()
+    fpi = 32 // c["bits"]
+
+    def cut(inp, b, tok_frac):
+        q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr = (t[b:b + 1] for t in inp)
+        if tok_frac < 1.0:
+            ng = max(1, int(Ks.shape[-1] * tok_frac))
+            Kq, Ks, Km = Kq[..., :ng * 32 // fpi], Ks[..., :ng], Km[..., :ng]
+            Vq, Vs, Vm = Vq[:, :, :ng * 32], Vs[:, :, :ng * 32], Vm[:, :, :ng * 32]
+        return q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr
+
+    if kl is not None:
+        G = c["Hq"] // c["Hk"]
+
+        def step(inp, b, tok_frac=1.0):
+            q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr = cut(inp, b, tok_frac)
+            Kd = kl.dequant_k(Kq, Ks, Km, c["group"], c["bits"]).to(torch.bfloat16)
+            Vd = kl.dequant_v(Vq, Vs, Vm, c["group"], c["bits"]).to(torch.bfloat16)
+            return kl.kivi_decode_attn_ref(q, Kd, Kr, Vd, Vr, G)
+        return step, "reference", "benchmarks/kivi_latency.py dequant_k + dequant_v + kivi_decode_attn_ref"
+
     import oracle
-    q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr = inputs_cpu
-    if b is not None:
-        sl = slice(b, b + 1)
-        q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr = (t[sl] for t in (q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr))
-    if tok_frac < 1.0:
-        fpi = 32 // CFG1["bits"]
-        ng = max(1, int(Ks.shape[-1] * tok_frac))
-        Kq, Ks, Km = Kq[..., :ng * 32 // fpi], Ks[..., :ng], Km[..., :ng]
-        Vq, Vs, Vm = Vq[:, :, :ng * 32], Vs[:, :, :ng * 32], Vm[:, :, :ng * 32]
-    return oracle.kivi_decode_attn(q, Kq, Ks, Km, Kr, Vq, Vs, Vm, Vr, CFG1["bits"], CFG1["group"])
+
+    def step(inp, b, tok_frac=1.0):
+        return oracle.kivi_decode_attn(*cut(inp, b, tok_frac), c["bits"], c["group"])
+    return step, "port", "oracle.kivi_decode_attn (fp32 torch restatement)"
 
 
-def cpu_inputs():
-    """Config-1 inputs built on the host (same generator recipe as the GPU inputs)."""
+def cpu_inputs(c):
+    """Inputs of the workload built on the host (same generator recipe as the GPU inputs)."""
     import oracle
     g = torch.Generator().manual_seed(1000)
-    c = CFG1
     B, Hq, Hk, D, S, R = c["B"], c["Hq"], c["Hk"], c["D"], c["S"], c["R"]
     Sq = S - R
     k = torch.randn(B, Hk, S, D, generator=g)
@@ -213,43 +275,87 @@ def cpu_inputs():
     return q, Kq, Ks, Km, k[:, :, Sq:].contiguous(), Vq, Vs, Vm, v[:, :, Sq:].contiguous()
 
 
-def run_reference(args, rank):
-    """--impl reference: the CPU restatement of the reference path, timed on host cores."""
-    if rank != 0:
-        return None
+def cpu_baseline(c, budget_s=10.0):
+    """Time the host-side step on a bounded sample: single sequences, scaled to the full batch."""
     cores = _host_cores()
     torch.set_num_threads(cores)
-    inp = cpu_inputs()
-    # size the per-step sample so the whole run stays within ~2 minutes
+    step, kind, what = cpu_step_fn(c)
+    inp = cpu_inputs(c)
     t0 = time.perf_counter()
-    cpu_kivi_step(inp, b=0)
+    step(inp, 0)
+    one = time.perf_counter() - t0
+    frac = min(1.0, budget_s / 2 / max(one, 1e-9))
+    t0 = time.perf_counter()
+    n = 0
+    while n < 2 or (time.perf_counter() - t0 < budget_s / 2 and n < 20):
+        step(inp, n % c["B"], frac)
+        n += 1
+    us = (time.perf_counter() - t0) / n * 1e6 * c["B"] / frac
+    sample = f"{n} single-sequence steps of {what}" + (f" over the first {frac:.3f} of the packed tokens"
+                                                       if frac < 1 else "") + f", scaled to the {c['B']}-sequence step"
+    return {"value": round(us, 1), "unit": "us/step", "cores": cores, "kind": kind, "sample": sample}
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference's CPU path for the workload, timed on host cores."""
+    if rank != 0:
+        return None
+    c = HEAD
+    cores = _host_cores()
+    torch.set_num_threads(cores)
+    step, kind, what = cpu_step_fn(c)
+    inp = cpu_inputs(c)
+    t0 = time.perf_counter()
+    step(inp, 0)
     one_seq = time.perf_counter() - t0
-    total_steps = args.steps + args.warmup
-    frac = min(1.0, 110.0 / max(one_seq * total_steps, 1e-9))
+    # size the per-step sample so the whole run stays within ~2 minutes
+    frac = min(1.0, 110.0 / max(one_seq * (args.steps + args.warmup), 1e-9))
     for i in range(args.warmup):
-        cpu_kivi_step(inp, b=i % CFG1["B"], tok_frac=frac)
+        step(inp, i % c["B"], frac)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        cpu_kivi_step(inp, b=i % CFG1["B"], tok_frac=frac)
+        step(inp, i % c["B"], frac)
     dt = (time.perf_counter() - t0) / args.steps
-    us = dt * 1e6 * CFG1["B"] / frac  # one sequence (and a token fraction) per step, scaled to the full step
-    sample = f"one of {CFG1['B']} sequences per step" + (f", first {frac:.3f} of the packed tokens" if frac < 1 else "")
-    line = {
+    us = dt * 1e6 * c["B"] / frac  # one sequence (and a token fraction) per step, scaled to the full step
+    sample = (f"{what}: one of {c['B']} sequences per step"
+              + (f", first {frac:.3f} of the packed tokens" if frac < 1 else "") + ", time scaled to the full step")
+    return {
         "impl": "reference", "metric": _metric(), "value": round(us, 1), "unit": "us/step", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c1 KIVI-2 decode B=8 Hq=28 Hk=4 D=128 S=16384 R=128 group=32",
-                   "global_batch": CFG1["B"], "seq_len": CFG1["S"], "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": cores, "kind": "port",
-                         "sample": sample + ", time scaled to the full step"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if kind == "port" else "bf16", "data": "synthetic",
+        "config": {"workload": _workload(c), "global_batch": c["B"], "seq_len": c["S"], "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    return line
 
 
 # ----------------------------------------------------------------------------- extras
 def _rot(make, n):
     return [make() for _ in range(n)]
+
+
+def _line(us, b, peak):
+    return {"us": round(us, 2), "GBps": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 3)}
+
+
+def path_c1(dev, peak, g):
+    """Config 1 as stated: KIVI-2 decode at 16K context (B=8, 28/4), whole step and the
+    packed-cache kernel alone."""
+    from bytes_b200 import kivi as kv, _ops
+    c = CFG1
+    sets = [kivi_inputs(dev, 2000 + i, c) for i in range(8)]
+    gr = graph_of([lambda s=s: kv.kivi_decode_attn(*s, c["bits"], c["group"]) for s in sets])
+    time_graph(gr, 2)
+    us = time_graph(gr, 20) / (20 * len(sets))
+    scal = 1.0 / math.sqrt(c["D"])
+    outs = [torch.empty(c["B"], c["Hq"], c["D"], dtype=torch.bfloat16, device=dev) for _ in sets]
+    gk = graph_of([lambda s=s, o=o: _ops.kivi_decode(s[0][:, :, 0, :], *s[1:], c["bits"], c["group"], scal, o,
+                                                     stages=1) for s, o in zip(sets, outs)])
+    time_graph(gk, 2)
+    us_k = time_graph(gk, 20) / (20 * len(sets))
+    kb = nbytes(*(sets[0][i] for i in (1, 2, 3, 5, 6, 7)))
+    out = {"c1_kivi2_16k_B8": dict(_line(us, nbytes(*sets[0][1:]), peak), kernel=_line(us_k, kb, peak))}
+    return out
 
 
 def path_c0(dev, peak, g):
@@ -261,13 +367,11 @@ def path_c0(dev, peak, g):
                          torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16()), 16)
     gr = graph_of([lambda s=s: ak.decode_attn_bf16(*s) for s in sets])
     us = time_graph(gr, 20) / (20 * len(sets))
-    b = nbytes(*sets[0][1:])
-    return {"c0_bf16_decode": {"us": round(us, 2), "GBps": round(b / us / 1e3, 1),
-                               "frac": round(b / us / 1e3 / peak, 3)}}
+    return {"c0_bf16_decode": _line(us, nbytes(*sets[0][1:]), peak)}
 
 
 def path_bf16_32k(dev, peak, g):
-    """bf16 dense decode at 32K context with the c1 head shapes (B=8, 28/4)."""
+    """bf16 and fp8 dense decode at 32K context with the c1 head shapes (B=8, 28/4)."""
     from bytes_b200 import attention_kernels as ak
     D = 128
     sets = _rot(lambda: (torch.randn(8, 28, 1, D, device=dev, generator=g).bfloat16(),
@@ -275,9 +379,13 @@ def path_bf16_32k(dev, peak, g):
                          torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16()), 2)
     gr = graph_of([lambda s=s: ak.decode_attn_bf16(*s) for s in sets])
     us = time_graph(gr, 10) / (10 * len(sets))
-    b = nbytes(*sets[0][1:])
-    return {"bf16_decode_32k_B8": {"us": round(us, 2), "GBps": round(b / us / 1e3, 1),
-                                   "frac": round(b / us / 1e3 / peak, 3)}}
+    out = {"bf16_decode_32k_B8": _line(us, nbytes(*sets[0][1:]), peak)}
+    sets8 = [(q, k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)) for q, k, v in sets]
+    del sets
+    gr = graph_of([lambda s=s: ak.decode_attn_fp8(*s) for s in sets8])
+    us = time_graph(gr, 10) / (10 * len(sets8))
+    out["fp8_decode_32k_B8"] = _line(us, nbytes(*sets8[0][1:]), peak)
+    return out
 
 
 def path_c2(dev, peak, g):
@@ -295,8 +403,7 @@ def path_c2(dev, peak, g):
     gr = graph_of([lambda s=s: ak.decode_attn_pq_lut_int8v(*s) for s in sets])
     us = time_graph(gr, 10) / (10 * len(sets))
     b = nbytes(*sets[0]) + M * K * 8 * 2 * Hk  # + per-head fp16 codebooks of the configuration
-    return {"c2_pq_lut_int8v": {"us": round(us, 2), "GBps": round(b / us / 1e3, 1),
-                                "frac": round(b / us / 1e3 / peak, 3)}}
+    return {"c2_pq_lut_int8v": _line(us, b, peak)}
 
 
 def path_c3(dev, peak, g):
@@ -343,6 +450,48 @@ def path_c3(dev, peak, g):
     return out
 
 
+def path_sparse_published(dev, peak, g):
+    """The reference's published sparse configurations on config 3's tensors (B=16, 32/8,
+    S=32768): two-pass sparse decode at k = 5 % with fp8, int4 and int2 score keys
+    (tables/profiling_latency.tex of the reference), each with its score / top-k / gather
+    split and the score pass's roofline fraction."""
+    from bytes_b200 import attention_kernels as ak, _ops
+    B, Hq, Hk, S, D = 16, 32, 8, 32768, 128
+    sc = 1 / math.sqrt(D)
+    q = torch.randn(B, Hq, 1, D, device=dev, generator=g).bfloat16()
+    k = torch.randn(B, Hk, S, D, device=dev, generator=g).bfloat16()
+    v = torch.randn(B, Hk, S, D, device=dev, generator=g).bfloat16()
+    kb = max(1, int(round(0.05 * S)))
+    out = {}
+    for bits in (8, 4, 2):
+        if bits == 8:
+            ks, s_, z_ = k.to(torch.float8_e4m3fn), None, None
+            score = lambda: ak.sparse_score_scalar(q, ks, sc, score_bits=8)
+            sbytes = nbytes(ks)
+        else:
+            ks, s_, z_ = ak.quantize_and_pack_score_keys(k, bits, 32)
+            score = lambda: ak.sparse_score_packed(q, ks, s_, z_, sc, score_bits=bits, group_size=32)
+            sbytes = nbytes(ks, s_, z_)
+        full = lambda: ak.sparse_decode_scalar(q, ks, s_, z_, k, v, 0.05, sc, score_bits=bits, group_size=32)
+        gr = graph_of([full])
+        us_full = time_graph(gr, 10) / 10
+        gr = graph_of([score])
+        us_s = time_graph(gr, 10) / 10
+        scores = score()
+        gr = graph_of([lambda: _ops.topk(scores, kb, sorted=False, want_values=False, idx_dtype=torch.int32)])
+        us_t = time_graph(gr, 10) / 10
+        _, idx = _ops.topk(scores, kb, sorted=False, want_values=False, idx_dtype=torch.int32)
+        gr = graph_of([lambda: ak.sparse_gather_attn(q, k, v, idx, sc)])
+        us_g = time_graph(gr, 10) / 10
+        name = {8: "fp8", 4: "int4", 2: "int2"}[bits]
+        out[f"sparse_{name}_score_k5pct"] = {
+            "us": round(us_full, 2), "kb": kb, "score_us": round(us_s, 2), "topk_us": round(us_t, 2),
+            "gather_us": round(us_g, 2), "score_bytes_MB": round((sbytes + B * Hq * S * 4) / 1e6, 1),
+            "score_frac": round((sbytes + B * Hq * S * 4) / us_s / 1e3 / peak, 3)}
+        del gr, scores, idx
+    return out
+
+
 def path_topk(dev, peak, g):
     """Top-k select alone: 512 rows x 32768 fp32 scores (c3's B*Hq rows), k = 1024, vs torch.topk."""
     from bytes_b200 import _ops
@@ -356,12 +505,10 @@ def path_topk(dev, peak, g):
                            "GBps": round(rows * n * 4 / us_tk / 1e3, 1)}}
 
 
-def path_c4(dev, peak, g):
-    """c4 (8-GPU box), one GPU's share: 8 sequences x 131072 tokens with the c1 head shapes
-    (28/4, D=128) as bf16 and as KIVI-2; and one rank's shard of a 1M-token sequence split
-    8 ways (B=1, 131072 tokens): its split-KV partial, then the combine of 8 shard partials
-    (the partials of this shard stand in for the all-gather's result on one GPU)."""
-    from bytes_b200 import attention_kernels as ak, kivi as kv, _ops
+def c4_batch_shard(dev, peak, g):
+    """c4, one GPU's batch shard: 8 sequences x 131072 tokens with the c1 head shapes
+    (28/4, D=128) as bf16 and as KIVI-2."""
+    from bytes_b200 import attention_kernels as ak, kivi as kv
     out = {}
     D, S = 128, 131072
     q = torch.randn(8, 28, 1, D, device=dev, generator=g).bfloat16()
@@ -370,40 +517,24 @@ def path_c4(dev, peak, g):
     gr = graph_of([lambda: ak.decode_attn_bf16(q, k, v)])
     time_graph(gr, 2)
     us = time_graph(gr, 10) / 10
-    b = nbytes(k, v)
-    out["c4_bf16_131k_B8"] = {"us": round(us, 2), "GBps": round(b / us / 1e3, 1), "frac": round(b / us / 1e3 / peak, 3)}
+    out["c4_bf16_131k_B8"] = _line(us, nbytes(k, v), peak)
     del k, v, gr
     torch.cuda.empty_cache()
-    c = dict(CFG1, S=S)
+    c = dict(HEAD, S=S)
     s = kivi_inputs(dev, 4242, c)
     gr = graph_of([lambda: kv.kivi_decode_attn(*s, c["bits"], c["group"])])
     time_graph(gr, 2)
     us = time_graph(gr, 10) / 10
-    b = nbytes(*s[1:])
-    out["c4_kivi2_131k_B8"] = {"us": round(us, 2), "MB": round(b / 1e6, 1), "GBps": round(b / us / 1e3, 1),
-                               "frac": round(b / us / 1e3 / peak, 3)}
-    del s, gr
-    torch.cuda.empty_cache()
-    q1 = torch.randn(1, 28, D, device=dev, generator=g).bfloat16()
-    k1 = torch.randn(1, 4, S, D, device=dev, generator=g).bfloat16()
-    v1 = torch.randn(1, 4, S, D, device=dev, generator=g).bfloat16()
-    scal = 1.0 / math.sqrt(D)
-    gr = graph_of([lambda: _ops.decode_attn_partial(q1, k1, v1, scal)])
-    time_graph(gr, 2)
-    us_p = time_graph(gr, 10) / 10
-    m, l, o = _ops.decode_attn_partial(q1, k1, v1, scal)
-    m8, l8, o8 = (t.unsqueeze(0).repeat(8, *([1] * t.dim())).contiguous() for t in (m, l, o))
-    gr2 = graph_of([lambda: _ops.lse_combine(m8, l8, o8, torch.bfloat16)])
-    time_graph(gr2, 2)
-    us_c = time_graph(gr2, 20) / 20
-    b = nbytes(k1, v1)
-    out["c4_1M_shard_of_8"] = {"partial_us": round(us_p, 2), "combine8_us": round(us_c, 2),
-                               "GBps": round(b / us_p / 1e3, 1), "frac": round(b / us_p / 1e3 / peak, 3),
-                               "exchange_bytes_per_rank": int(m.numel() * 8 + o.numel() * 4)}
+    out["c4_kivi2_131k_B8"] = dict(_line(us, nbytes(*s[1:]), peak), MB=round(nbytes(*s[1:]) / 1e6, 1))
     return out
 
 
-PATHS = {"c0": path_c0, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3, "topk": path_topk, "c4": path_c4}
+def path_c4(dev, peak, g):
+    return c4_batch_shard(dev, peak, g)
+
+
+PATHS = {"c0": path_c0, "c1": path_c1, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3,
+         "sparse_published": path_sparse_published, "topk": path_topk, "c4": path_c4}
 
 
 def extras(dev, peak, only=None):
@@ -420,6 +551,120 @@ def extras(dev, peak, only=None):
     return out
 
 
+# ----------------------------------------------------------------------------- split-KV
+SPLIT_TOKENS = 1 << 20  # config 4's long sequence
+
+
+def _split_shard(dev, i, n, Hk, D):
+    """Tokens [i*S/n, (i+1)*S/n) of the long sequence (a seed per shard: any rank can rebuild any shard)."""
+    g = torch.Generator(device=dev).manual_seed(90000 + 131 * n + i)
+    L = SPLIT_TOKENS // n
+    return (torch.randn(1, Hk, L, D, device=dev, generator=g).bfloat16(),
+            torch.randn(1, Hk, L, D, device=dev, generator=g).bfloat16())
+
+
+def split_kv_bench(dev, rank, world, dist, steps, warmup, peak):
+    """One 1M-token bf16 sequence (28/4 heads, D=128) split along its tokens across the ranks.
+
+    Step = this rank's split-KV partial over its shard (CUDA graph), one all-gather of the
+    packed (max, sum, numerator) partials of every rank (NCCL), and the log-sum-exp combine
+    (CUDA graph). Before timing, every rank checks the combined output against single-GPU
+    decode of the whole sequence; the ranks agree on the verdict through an all-reduce."""
+    from bytes_b200 import _ops, attention_kernels as ak
+    Hq, Hk, D = 28, 4, 128
+    scal = 1.0 / math.sqrt(D)
+    g = torch.Generator(device=dev).manual_seed(424242)
+    q3 = torch.randn(1, Hq, D, device=dev, generator=g).bfloat16()
+    k_sh, v_sh = _split_shard(dev, rank, world, Hk, D)
+    n_ml = Hq
+    width = 2 * n_ml + Hq * D
+    send = torch.empty(width, dtype=torch.float32, device=dev)
+    recv = torch.empty(world, width, dtype=torch.float32, device=dev)
+    out = torch.empty(1, Hq, D, dtype=torch.bfloat16, device=dev)
+
+    def partial():
+        m, l, o = _ops.decode_attn_partial(q3, k_sh, v_sh, scal)
+        send[:n_ml].copy_(m.view(-1))
+        send[n_ml:2 * n_ml].copy_(l.view(-1))
+        send[2 * n_ml:].copy_(o.view(-1))
+
+    def exchange():
+        if dist is not None:
+            dist.all_gather_into_tensor(recv, send)
+        else:
+            recv[0].copy_(send)
+
+    def combine():
+        out.copy_(_ops.lse_combine(recv[:, :n_ml].reshape(world, 1, Hq), recv[:, n_ml:2 * n_ml].reshape(world, 1, Hq),
+                                   recv[:, 2 * n_ml:].reshape(world, 1, Hq, D), torch.bfloat16))
+
+    g_part, g_comb = graph_of([partial]), graph_of([combine])
+
+    def step():
+        g_part.replay()
+        exchange()
+        g_comb.replay()
+
+    # parity: the split result against single-GPU decode of the whole sequence
+    step()
+    torch.cuda.synchronize()
+    parts = [_split_shard(dev, i, world, Hk, D) for i in range(world)]
+    k_full = torch.cat([p[0] for p in parts], 2)
+    v_full = torch.cat([p[1] for p in parts], 2)
+    del parts
+    ref = ak.decode_attn_bf16((q3.float() * scal).bfloat16().unsqueeze(2), k_full, v_full)[:, :, 0]
+    # the reference call takes a pre-scaled bf16 query; compare both against fp32 math too
+    ref32 = torch.softmax((k_full[0].float() @ (q3[0].float().view(Hk, Hq // Hk, D).transpose(1, 2)) * scal)
+                          .transpose(1, 2), -1) @ v_full[0].float()
+    del k_full, v_full
+    d = (out[0].float() - ref32.reshape(Hq, D)).abs()
+    d2 = (out.float() - ref.float()).abs()
+    ok = bool(torch.isfinite(out.float()).all().item() and d.max().item() <= 2e-2 and d.mean().item() <= 1e-3
+              and d2.max().item() <= 2e-2)
+    flag = torch.tensor([1.0 if ok else 0.0], device=dev)
+    if dist is not None:
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    parity_ok = bool(flag.item() == 1.0)
+    torch.cuda.empty_cache()
+
+    for _ in range(max(warmup, 3)):
+        step()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    e1.synchronize()
+    us_step = e0.elapsed_time(e1) * 1e3 / steps
+    # the all-gather alone, same loop length
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(steps):
+        exchange()
+    e1.record(st)
+    e1.synchronize()
+    us_ag = e0.elapsed_time(e1) * 1e3 / steps
+    t = torch.tensor([us_step, us_ag], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us_step, us_ag = float(t[0].item()), float(t[1].item())
+    shard_bytes = nbytes(k_sh, v_sh)
+    del g_part, g_comb
+    return {"tokens": SPLIT_TOKENS, "ranks": world, "shard_tokens": SPLIT_TOKENS // world, "us": round(us_step, 2),
+            "allgather_us": round(us_ag, 2), "allgather_share": round(us_ag / us_step, 3),
+            "exchange_bytes_per_rank": width * 4, "tokens_per_s": round(1e6 / us_step, 1),
+            "shard_GBps": round(shard_bytes / us_step / 1e3, 1),
+            "shard_frac": round(shard_bytes / us_step / 1e3 / peak, 3), "parity_ok": parity_ok,
+            "steps": steps, "timing": "partial and combine as CUDA graphs, NCCL all-gather between, CUDA events, "
+                                      "max over ranks"}
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -430,7 +675,10 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--path", choices=sorted(PATHS), help="time only this secondary path and print its numbers")
     args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    if args.steps < 1:
+        raise SystemExit("--steps must be at least 1")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -460,45 +708,49 @@ def main():
     if args.path:
         print(json.dumps(extras(dev, peak, only=args.path)), flush=True)
         return
-    c = CFG1
+    c = HEAD
     sets = [kivi_inputs(dev, 1000 + rank * NBUF + i) for i in range(NBUF)]
     step_bytes = nbytes(*sets[0][1:])
     kern_bytes = nbytes(*(sets[0][i] for i in (1, 2, 3, 5, 6, 7)))
     scal = 1.0 / math.sqrt(c["D"])
 
-    # device-time value: graph replay of the public call, NBUF rotating input sets per replay
-    calls = [lambda s=s: kv.kivi_decode_attn(*s, c["bits"], c["group"]) for s in sets]
-    g_step = graph_of(calls)
-    reps_w = max(1, math.ceil(args.warmup / NBUF))
-    reps = max(1, math.ceil(args.steps / NBUF))
-    steps_timed = reps * NBUF
-    time_graph(g_step, reps_w)
+    # device-time value: a graph of exactly `steps` decode steps (after one of `warmup`),
+    # rotating over the NBUF input sets
+    def step_call(i):
+        s = sets[i % NBUF]
+        return lambda: kv.kivi_decode_attn(*s, c["bits"], c["group"])
+
+    g_warm = graph_of([step_call(i) for i in range(args.warmup)])
+    g_step = graph_of([step_call(i) for i in range(args.steps)])
+    g_warm.replay()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        us_total = time_graph(g_step, reps)
+        us_total = time_graph(g_step, 1)
     torch.cuda.synchronize()
-    us_step = us_total / steps_timed
+    us_step = us_total / args.steps
     if dist is not None:
         t = torch.tensor([us_step], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us_step = float(t.item())
+    del g_warm, g_step
 
     # roofline: the packed-cache kernel alone
     outs = [torch.empty(c["B"], c["Hq"], c["D"], dtype=torch.bfloat16, device=dev) for _ in sets]
     kcalls = [lambda s=s, o=o: _ops.kivi_decode(s[0][:, :, 0, :], *s[1:], c["bits"], c["group"], scal, o, stages=1)
               for s, o in zip(sets, outs)]
     g_k = graph_of(kcalls)
-    time_graph(g_k, 2)
-    us_kern = time_graph(g_k, max(2, reps // 2)) / (max(2, reps // 2) * NBUF)
+    time_graph(g_k, 3)
+    reps_k = max(5, min(200, args.steps // NBUF))
+    us_kern = time_graph(g_k, reps_k) / (reps_k * NBUF)
     achieved = kern_bytes / us_kern / 1e3  # GB/s
+    del g_k
 
-    # e2e through the public API with host buffers
+    # e2e through the public API with host buffers, exactly `steps` steps after `warmup`
     q_host = [s[0].cpu().pin_memory() for s in sets]
     out_host = [torch.empty(c["B"], c["Hq"], 1, c["D"], dtype=torch.bfloat16).pin_memory() for _ in sets]
     q_dev = [torch.empty_like(s[0]) for s in sets]
-    n_e2e = max(NBUF, min(args.steps, 400))
     st = torch.cuda.current_stream()
 
     def e2e_step(i):
@@ -510,67 +762,82 @@ def main():
     for i in range(args.warmup):
         e2e_step(i)
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for i in range(n_e2e):
+    for i in range(args.steps):
         e2e_step(i)
     e1.record(st)
     e1.synchronize()
-    us_e2e = e0.elapsed_time(e1) * 1e3 / n_e2e
+    us_e2e = e0.elapsed_time(e1) * 1e3 / args.steps
     if dist is not None:
         t = torch.tensor([us_e2e], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us_e2e = float(t.item())
+    del sets, q_host, out_host, q_dev, outs
+    torch.cuda.empty_cache()
+
+    # the long sequence split across the ranks (NCCL all-gather inside the step)
+    split = split_kv_bench(dev, rank, world, dist, max(10, min(args.steps, 200)), args.warmup, peak)
+    torch.cuda.empty_cache()
 
     extra = None
     cpu_base = None
+    c4 = None
+    if world > 1:
+        # every rank times its own c4 batch shard; max over ranks
+        c4 = c4_batch_shard(dev, peak, torch.Generator(device=dev).manual_seed(11 + rank))
+        t = torch.tensor([c4["c4_bf16_131k_B8"]["us"], c4["c4_kivi2_131k_B8"]["us"]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        c4 = {"bf16_us": round(float(t[0].item()), 2), "kivi2_us": round(float(t[1].item()), 2),
+              "sequences": 8 * world, "tokens_per_sequence": 131072}
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1:
         if not args.no_extras:
             extra = extras(dev, peak)
-        cores = _host_cores()
-        torch.set_num_threads(cores)
-        inp = cpu_inputs()
-        t0 = time.perf_counter()
-        n_cpu = 0
-        while n_cpu < 2 or (time.perf_counter() - t0 < 10.0 and n_cpu < 20):
-            cpu_kivi_step(inp, b=n_cpu % c["B"])
-            n_cpu += 1
-        us_cpu = (time.perf_counter() - t0) / n_cpu * 1e6 * c["B"]
-        cpu_base = {"value": round(us_cpu, 1), "unit": "us/step", "cores": cores, "kind": "port",
-                    "sample": f"{n_cpu} single-sequence steps of the config-1 cache (fp32 torch oracle), x{c['B']}"}
+        cpu_base = cpu_baseline(c)
 
     if rank == 0:
+        wl = _workload(c)
         line = {
             "metric": _metric(), "value": round(us_step, 2), "unit": "us/step", "n_gpus": world,
-            "steps": steps_timed, "warmup": reps_w * NBUF, "ms_per_step": round(us_step / 1e3, 5),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 5),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
-            "config": {"workload": "c1 KIVI-2 decode B=8 Hq=28 Hk=4 D=128 S=16384 R=128 group=32",
-                       "global_batch": c["B"] * world, "seq_len": c["S"], "parallelism": f"batch-shard x{world}",
+            "config": {"workload": wl, "global_batch": c["B"] * world, "seq_len": c["S"],
+                       "parallelism": f"batch-shard x{world}",
                        "l2": f"{NBUF} rotating input sets ({NBUF * step_bytes / 1e6:.0f} MB > 3x L2)",
-                       "timing": "CUDA-graph replay, CUDA events, max over ranks"},
+                       "timing": "one CUDA graph of exactly `steps` steps, CUDA events, max over ranks"},
             "tokens_per_s": round(c["B"] * world / (us_step * 1e-6), 1),
             "hbm_GBps_step": round(step_bytes * world / us_step / 1e3, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": _profile_traffic("kivi_decode_kernel_c1.md"),
-                         "kernel": "kivi_decode_kernel<2,1,3>", "algorithmic_bytes_per_launch": kern_bytes,
+                         "traffic": _measured_traffic(wl),
+                         "kernel": "kivi_decode_kernel (packed-cache pass)", "algorithmic_bytes_per_launch": kern_bytes,
                          "kernel_us": round(us_kern, 2)},
             "cpu_baseline": cpu_base,
-            "e2e": {"value": round(us_e2e, 2), "unit": "us/step", "h2d_bytes_per_step": nbytes(sets[0][0]),
-                    "d2h_bytes_per_step": nbytes(outs[0])},
+            "e2e": {"value": round(us_e2e, 2), "unit": "us/step", "h2d_bytes_per_step": nbytes(q_dev_shape(c)),
+                    "d2h_bytes_per_step": nbytes(q_dev_shape(c))},
             # per step: the packed-cache pass and the residual-window pass, which also
             # merges the split partials (R = 128 takes one window CTA per group)
-            "gpu_launches": 2 * steps_timed,
+            "gpu_launches": 2 * args.steps,
             "clocks": clk.summary(),
+            "split_kv": split,
         }
+        if c4 is not None:
+            line["c4_batch_shard"] = c4
         if extra is not None:
             line["paths"] = extra
         print(json.dumps(line), flush=True)
-    del g_step, g_k
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def q_dev_shape(c):
+    """A meta tensor of one step's query (and output) shape, for byte counts."""
+    return torch.empty(c["B"], c["Hq"], 1, c["D"], dtype=torch.bfloat16, device="meta")
 
 
 if __name__ == "__main__":

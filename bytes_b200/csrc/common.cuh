@@ -157,12 +157,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the barrier phase `parity`: false if it did not complete within the
-// iteration limit (each try_wait also suspends for a hardware-chosen interval).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Limit of one bounded device wait. A tile copy normally lands within microseconds; a
+// wait this long means the copy is lost, and the kernel gives up instead of hanging.
+constexpr uint64_t kWaitLimitNs = 50ull * 1000 * 1000;  // 50 ms
+// Bounded wait for the barrier phase `parity`: false if it did not complete within
+// kWaitLimitNs (each try_wait also suspends for a hardware-chosen interval).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
 }
 // 4-D tiled TMA load of the box at {c0 (innermost), c1, c2, c3} into shared memory,
 // completing on `bar` (transaction bytes). `map` is a __grid_constant__ tensor map.

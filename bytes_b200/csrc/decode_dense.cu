@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
     const int64_t row0 = int64_t(b) * p.Hq + hk * p.G + h0;
     const uint32_t blk_off = (uint32_t((reinterpret_cast<uint8_t*>(sl + NH) - smem)) + 15u) & ~15u;
     const uint32_t blk_bytes = uint32_t(nheads) * uint32_t(p.split_stride) * uint32_t(D) * 4u;
-    const bool staged = blk_off + blk_bytes + 8u <= uint32_t(p.smem_bytes);
+    bool staged = blk_off + blk_bytes + 8u <= uint32_t(p.smem_bytes);
     const float* ob = reinterpret_cast<const float*>(smem + blk_off);
     const uint32_t mbar = smem_u32(smem + blk_off + blk_bytes);
     if (staged && threadIdx.x == 0) {
@@ -420,8 +420,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
         sl[h] = L + Lo * wo;
       }
     }
-    if (staged && !mbar_wait(mbar, 0) && threadIdx.x == 0) atomicAdd(&g_merge_timeouts, 1u);
-    __syncthreads();
+    // the staged slots never arrived: read them from global memory instead (the copy gets
+    // one more bounded wait before the CTA exits, below)
+    const bool lost = staged && !mbar_wait(mbar, 0);
+    if (__syncthreads_or(lost)) {
+      if (threadIdx.x == 0) atomicAdd(&g_merge_timeouts, 1u);
+      staged = false;
+    }
     constexpr int C4 = D / 4;
     for (int idx = threadIdx.x; idx < nheads * C4; idx += kWarps * 32) {
       const int h = idx / C4, c = 4 * (idx % C4);
@@ -460,6 +465,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const Dens
       store_out(p.out, p.out_dtype, off + 2, O.z * inv);
       store_out(p.out, p.out_dtype, off + 3, O.w * inv);
     }
+    if (lost) mbar_wait(mbar, 0);
     return;
   }
   for (int idx = threadIdx.x; idx < nheads * D; idx += kWarps * 32) {
@@ -770,23 +776,35 @@ int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* 
 // plain C / FFI host that only owns the q/k/v/out buffers. For them the split partials
 // live in this fixed array, which every GPU that loads the library keeps (4 MiB) until
 // the process exits. In host code the symbol is only a stand-in, so its device address
-// is looked up once per device with cudaGetSymbolAddress.
+// is looked up with cudaGetSymbolAddress on the calling device.
+//
+// Size: a plan that splits at all targets two CTAs per SM, so it holds at most
+// 2 x SMs CTAs x 16 heads of (D + 2) floats, D <= 128, plus 256 bytes of alignment slack:
+// 16,640 bytes per SM. 4 MiB therefore covers every plan on parts with up to 252 SMs
+// (B200: 148); a larger plan is rejected with BD_ERR_UNSUPPORTED before any launch.
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 static std::mutex g_scratch_mu;
 static void* g_scratch_addr[64] = {nullptr};
 
-int static_scratch_address(void** ptr) {
+// The address is looked up again on every call made outside a stream capture, so a
+// device reset (which reloads the module at a new address) never leaves a stale pointer;
+// a call made while `st` is capturing uses the address of the device's last uncaptured call.
+int static_scratch_address(cudaStream_t st, void** ptr) {
   int dev = 0;
   int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc) return rc;
   if (dev < 0 || dev >= 64) return fail(BD_ERR_UNSUPPORTED, "device index out of range for the static scratch");
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if ((rc = cuda_check(cudaStreamIsCapturing(st, &cap), "cudaStreamIsCapturing"))) return rc;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  if (cap == cudaStreamCaptureStatusNone) {
     void* a = nullptr;
     if ((rc = cuda_check(cudaGetSymbolAddress(&a, g_decode_scratch), "cudaGetSymbolAddress(static scratch)")))
       return rc;
     g_scratch_addr[dev] = a;
+  } else if (!g_scratch_addr[dev]) {
+    return fail(BD_ERR_VALUE, "bd_decode_attn_noalloc: make one call on this device outside stream capture first");
   }
   *ptr = g_scratch_addr[dev];
   return BD_OK;
@@ -869,7 +887,7 @@ int bd_decode_attn_noalloc(const bd_tensor* q, const bd_tensor* k, const bd_tens
                                         std::to_string(kStaticScratchBytes) +
                                         "; use bd_decode_attn with a caller workspace");
   void* scratch = nullptr;
-  if ((rc = static_scratch_address(&scratch))) return rc;
+  if ((rc = static_scratch_address(reinterpret_cast<cudaStream_t>(stream), &scratch))) return rc;
   return bd_decode_attn(q, k, v, out, scaling, scratch, kStaticScratchBytes, stream);
 }
 

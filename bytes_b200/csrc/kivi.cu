@@ -30,10 +30,11 @@
 //    minima contribute sum_t P_t m_t per (group, head), again one MMA per row block.
 //  * Row/token permutations are chosen so every shared-memory read is conflict-free
 //    and the movmatrix transpose of P lands directly in the PV operand layout.
-//  * The bf16 residual window runs through the dense split kernel into the same
-//    partial buffer; a log-sum-exp combine produces the output. Both are launched as
-//    programmatic dependents, so the residual CTAs fill the SMs this grid's tail frees
-//    and the combine is resident before its inputs are complete.
+//  * The bf16 residual window runs through the dense decode kernel in its merge mode,
+//    launched as a programmatic dependent of this grid: one window CTA per (batch, KV
+//    head, head chunk) attends the window, waits for this grid, then merges the group's
+//    split slots and the window partial into the output itself (no combine kernel).
+//    When the window needs several CTAs per group, a log-sum-exp combine follows instead.
 //  * Splits are balanced to one wave of 3 or 4 CTAs per SM (split s owns tiles
 //    [s*T/n, (s+1)*T/n)), so no SM carries a second round.
 #include "common.cuh"
@@ -380,13 +381,29 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
   if (ntiles > 0) regroup(0);
 
   for (int it = 0; it < ntiles; ++it) {
-    // outstanding cp.async: the next key scale/min chunk (and, without TMA, this tile)
-    cp_async_wait<0>();
-    if (TMA && !mbar_wait(bar0 + 8 * (it % kStagesK), (it / kStagesK) & 1) && threadIdx.x == 0)
-      atomicAdd(&g_kivi_tma_timeouts, 1u);
+    // cp.async groups (one committed per iteration): without TMA this tile's copies, the
+    // last group; with TMA only the key scale/min chunks, and the one regroup(it + 1)
+    // reads below was committed three iterations ago, so the two newest may stay pending
+    if (TMA) cp_async_wait<2>();
+    else cp_async_wait<0>();
+    const bool lost = TMA && !mbar_wait(bar0 + 8 * (it % kStagesK), (it / kStagesK) & 1);
     // this tile landed, the regrouped scales of this tile are visible, and every thread is
     // done with the previous tile's stage and scale buffer
-    __syncthreads();
+    if (__syncthreads_or(lost)) {
+      // a tile copy never completed: give it one more bounded wait (no copy may land in
+      // shared memory after this CTA exits), mark this CTA's partials as failed (NaN, so
+      // the merged output is NaN) and count the event for bd_wait_timeouts()
+      if (threadIdx.x == 0) atomicAdd(&g_kivi_tma_timeouts, 1u);
+      mbar_wait(bar0 + 8 * (it % kStagesK), (it / kStagesK) & 1);
+      cp_async_wait<0>();
+      const int64_t pi0 = (int64_t(b) * p.Hq + hk * p.G + h0) * p.split_stride + split;
+      for (int i = threadIdx.x; i < nheads * 128; i += kWarpsK * 32) {
+        const int64_t pi = pi0 + int64_t(i >> 7) * p.split_stride;
+        p.part_o[pi * 128 + (i & 127)] = __int_as_float(0x7fc00000);
+        if ((i & 127) == 0) p.part_m[pi] = p.part_l[pi] = __int_as_float(0x7fc00000);
+      }
+      return;
+    }
     if (it + 1 < ntiles) load_tile(it + 1, (it + 1) % kStagesK);
     // the chunk after next, into the buffer whose last reader was the regroup of tile it
     if (it % kKChunk == 0 && it + kKChunk < ntiles) load_chunk(it + kKChunk);

@@ -293,13 +293,24 @@ __global__ void __launch_bounds__(kPW * 32, 2)
   const int jlo = (tq >> 1) ? jmid : 0, jhi = (tq >> 1) ? p.M : jmid;
   const int r0 = warp * 16;
   for (int it = 0; it < ntiles; ++it) {
-    if (TMA) {
-      if (!mbar_wait(bar0 + 8 * (it % kPStages), (it / kPStages) & 1) && threadIdx.x == 0)
-        atomicAdd(&g_pq_tma_timeouts, 1u);
-    } else {
-      cp_async_wait<kPStages - 2>();
+    bool lost = false;
+    if (TMA) lost = !mbar_wait(bar0 + 8 * (it % kPStages), (it / kPStages) & 1);
+    else cp_async_wait<kPStages - 2>();
+    if (__syncthreads_or(lost)) {
+      // a tile copy never completed: one more bounded wait for every tile copy still in
+      // flight (none may land in shared memory after this CTA exits), then mark this CTA's
+      // partials as failed (NaN: the merged output is NaN) and count the event
+      if (threadIdx.x == 0) atomicAdd(&g_pq_tma_timeouts, 1u);
+      for (int t = it; t < min(ntiles, it + kPStages - 1); ++t) mbar_wait(bar0 + 8 * (t % kPStages), (t / kPStages) & 1);
+      if (VK != V_NONE) {
+        for (int idx = threadIdx.x; idx < nheads * D; idx += kPW * 32) {
+          const int64_t pi = (int64_t(b) * p.Hq + hk * p.G + h0 + idx / D) * p.n_splits + split;
+          p.part_o[pi * D + idx % D] = __int_as_float(0x7fc00000);
+          if (idx % D == 0) p.part_m[pi] = p.part_l[pi] = __int_as_float(0x7fc00000);
+        }
+      }
+      return;
     }
-    __syncthreads();
     {
       const int nxt = it + kPStages - 1;
       if (nxt < ntiles) load_tile(nxt, nxt % kPStages);

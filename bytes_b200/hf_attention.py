@@ -179,6 +179,17 @@ def _kivi_layer_class():
             if self.is_initialized:
                 self._batch_apply(lambda t: t[indices])
 
+        def reset(self):
+            # the base reset clears the window and the token count; the packed range and
+            # the window length must restart too, or the next prompt would be appended after
+            # (and attend over) the previous sequence's packed tokens
+            super().reset()
+            self.n_packed = 0
+            self.n_res = 0
+            if self.is_initialized:
+                for name in ("Kq", "Ks", "Km", "Vq", "Vs", "Vm"):
+                    getattr(self, name).zero_()
+
         def crop(self, max_length):
             raise NotImplementedError("KiviCache: packed tokens cannot be cropped")
 

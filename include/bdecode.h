@@ -85,8 +85,11 @@ int bd_decode_attn(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v,
  * and out), the split partials go to a fixed 4 MiB device array inside the library,
  * which every GPU that loads the library keeps until the process exits. Calls needing
  * more split scratch than that are rejected with BD_ERR_UNSUPPORTED (use
- * bd_decode_attn then); nothing is allocated. The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress): make it before any stream capture.
+ * bd_decode_attn then); nothing is allocated. Each call made outside a stream capture
+ * looks up the array's device address on the current device (cudaGetSymbolAddress), so
+ * a device reset never leaves a stale address; a call made while its stream is capturing
+ * reuses the last address looked up, so make the first call on a device before any
+ * stream capture.
  * All calls share the array, so calls that overlap on the GPU (other streams, other
  * host threads) race; serialise them. Every byte a call reads is written by that call. */
 int bd_decode_attn_noalloc(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v,

@@ -248,10 +248,17 @@ def sparse_gather_attn(q, k, v, idx, scaling, BLOCK_K=64):
     ii = idx.long()
     valid = (ii >= 0) & (ii < S)
     gi = ii.clamp(0, max(S - 1, 0))
-    kr = repeat_kv(k.float(), G)
-    vr = repeat_kv(v.float(), G)
-    ks = torch.gather(kr, 2, gi.unsqueeze(-1).expand(B, Hq, kb, D))
-    vs = torch.gather(vr, 2, gi.unsqueeze(-1).expand(B, Hq, kb, D))
+    # rows of query head h come from KV head h // G (repeat_kv's mapping); indexing the
+    # cache directly keeps the check affordable at 32K-token caches
+    bi = torch.arange(B)[:, None, None]
+    hi = (torch.arange(Hq) // G)[None, :, None]
+
+    def rows(t):
+        if t.dtype == torch.float8_e4m3fn:
+            return t.view(torch.uint8)[bi, hi, gi].view(torch.float8_e4m3fn).float()
+        return t[bi, hi, gi].float()
+
+    ks, vs = rows(k), rows(v)
     sc = (q.float()[:, :, 0, None, :] * ks).sum(-1) * scaling
     sc = torch.where(valid, sc, torch.full_like(sc, NEG_INF))
     m = sc.amax(-1, keepdim=True)

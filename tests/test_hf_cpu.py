@@ -44,3 +44,32 @@ def test_kivi_cache_window_bookkeeping(monkeypatch):
     assert layer.n_packed == 64 and layer.n_res == 8
     assert k.shape[2] == 8 and k[0, 0, :, 0].tolist() == [float(x) for x in range(64, 72)]
     assert getattr(k, "_bytes_kivi", None) is layer
+
+
+def test_kivi_cache_reset_restarts_packed_range(monkeypatch):
+    """After Cache.reset() the next prompt packs from token 0 again: no packed tokens of the
+    previous sequence stay visible to decode."""
+    pytest.importorskip("transformers")
+    from bytes_b200 import hf_attention, kivi
+    flushed = []
+    monkeypatch.setattr(kivi, "kivi_append", lambda k, v, bits, off, *caches: flushed.append((off, k.shape[2])))
+
+    class Cfg:
+        def get_text_config(self, decoder=True):
+            return self
+        num_hidden_layers = 1
+
+    cache = hf_attention.KiviCache(Cfg(), bits=2, residual=8, max_tokens=256)
+    layer = cache.layers[0]
+    tok = lambda n: torch.ones(1, 1, n, 128)
+    layer.update(tok(80), tok(80))  # 64 packed, 16 in the window
+    for _ in range(30):  # the window reaches residual + 32 at the 24th step and flushes
+        layer.update(tok(1), tok(1))
+    assert layer.n_packed == 96 and layer.n_res == 14 and layer.cumulative_length == 110
+    layer.Kq.fill_(7)
+    cache.reset()
+    assert layer.n_packed == 0 and layer.n_res == 0 and layer.cumulative_length == 0
+    assert int(layer.Kq.abs().sum()) == 0 and layer.packed_views()[0].shape[-1] == 0
+    flushed.clear()
+    layer.update(tok(45), tok(45))  # a new prompt: its first 32 tokens pack at offset 0
+    assert flushed == [(0, 32)] and layer.n_packed == 32 and layer.n_res == 13

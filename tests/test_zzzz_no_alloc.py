@@ -60,8 +60,12 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
 
 def test_noalloc_scratch_covers_every_plan_on_this_device(cuda):
     """The split plan targets two CTAs per SM, so a plan that splits at all needs at most
-    ~16 heads x 2 x SMs x (D+2) floats of scratch (about 2.5 MB on a 148-SM part): the
-    4 MiB static array holds every such plan on this device."""
+    16 heads x 2 x SMs x (D+2) floats of scratch plus 256 bytes of alignment slack, i.e.
+    16,640 bytes per SM (about 2.5 MB on a 148-SM part): the 4 MiB static array holds every
+    such plan on parts with up to 252 SMs, this device included. (Larger plans are rejected
+    with BD_ERR_UNSUPPORTED before any launch; no device this test runs on reaches that.)"""
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    assert 16640 * sms + 256 <= 4 << 20
     lib = N.lib()
     f = lib.bd_decode_attn_workspace
     f.restype = ctypes.c_size_t
