@@ -63,14 +63,17 @@ __device__ __forceinline__ float h16_to_f(uint16_t u, int is_bf16) {
   return is_bf16 ? __uint_as_float(uint32_t(u) << 16) : __half2float(__ushort_as_half(u));
 }
 
-template <int KT, int D, int NT>
+// GS: group size of packed keys (compile-time, so every per-group accumulator index is
+// static and the accumulators stay in registers); 0 for bf16 / fp8 keys.
+template <int KT, int D, int NT, int GS>
 __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p) {
   griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
   griddep_launch_dependents();
   using L = SL<KT, D>;
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int KSTEPS = D / 16;
-  constexpr int NGMAX = D / 16;  // max groups (gs >= 16)
+  constexpr int NGMAX = GS > 0 ? D / GS : 1;  // groups per token row
+  static_assert(KT == 16 || KT == 8 || (GS >= 16 && D % GS == 0), "packed keys need a group size");
   const int split = blockIdx.x;
   const int hk = blockIdx.y / p.head_chunks;
   const int chunk = blockIdx.y % p.head_chunks;
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
           v += __shfl_xor_sync(0xffffffffu, v, 2);
           part[kk][nt] = v;  // sum over the 16 channels of k-step kk, head g (+nt*8)
         }
-      const int kpg = p.gs / 16;  // k-steps per group
+      constexpr int kpg = GS > 0 ? GS / 16 : 1;  // k-steps per group
 #pragma unroll
       for (int gi = 0; gi < NGMAX; ++gi)
 #pragma unroll
@@ -160,7 +163,7 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
     }
   }
 
-  const int ngroups = (KT == 2 || KT == 4) ? D / p.gs : 0;
+  constexpr int ngroups = (KT == 2 || KT == 4) ? NGMAX : 0;
   const uint8_t* scb = (KT == 2 || KT == 4)
       ? reinterpret_cast<const uint8_t*>(p.sc + int64_t(b) * p.sc_sb + int64_t(hk) * p.sc_sh) : nullptr;
   const uint8_t* zrb = (KT == 2 || KT == 4)
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
           wa[4 * w4] = x.x; wa[4 * w4 + 1] = x.y; wa[4 * w4 + 2] = x.z; wa[4 * w4 + 3] = x.w;
           wb[4 * w4] = y.x; wb[4 * w4 + 1] = y.y; wb[4 * w4 + 2] = y.z; wb[4 * w4 + 3] = y.w;
         }
-        const int kpg = p.gs / 16;
+        constexpr int kpg = GS > 0 ? GS / 16 : 1;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
           uint32_t a0, a1, a2, a3;
@@ -323,11 +326,11 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
   }
 }
 
-template <int KT, int D, int NT>
+template <int KT, int D, int NT, int GS>
 int launch_score(const ScoreParams& p, int n_splits, cudaStream_t st) {
   using L = SL<KT, D>;
   const size_t smem = size_t(kSStages) * L::STAGE;
-  auto kern = score_kernel<KT, D, NT>;
+  auto kern = score_kernel<KT, D, NT, GS>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -341,9 +344,23 @@ int launch_score(const ScoreParams& p, int n_splits, cudaStream_t st) {
   return launch_programmatic(kern, grid, dim3(kSW * 32), smem, st, p, "score_kernel launch");
 }
 
+template <int KT, int D, int GS>
+int launch_score_gs(const ScoreParams& p, int nt, int n_splits, cudaStream_t st) {
+  return nt == 1 ? launch_score<KT, D, 1, GS>(p, n_splits, st) : launch_score<KT, D, 2, GS>(p, n_splits, st);
+}
+
 template <int KT, int D>
 int launch_score_nt(const ScoreParams& p, int nt, int n_splits, cudaStream_t st) {
-  return nt == 1 ? launch_score<KT, D, 1>(p, n_splits, st) : launch_score<KT, D, 2>(p, n_splits, st);
+  if constexpr (KT == 16 || KT == 8) {
+    return launch_score_gs<KT, D, 0>(p, nt, n_splits, st);
+  } else {
+    switch (p.gs) {
+      case 16: return launch_score_gs<KT, D, 16>(p, nt, n_splits, st);
+      case 32: return launch_score_gs<KT, D, 32>(p, nt, n_splits, st);
+      case 64: return launch_score_gs<KT, D, 64>(p, nt, n_splits, st);
+      default: return launch_score_gs<KT, D, (D >= 128 ? 128 : 64)>(p, nt, n_splits, st);
+    }
+  }
 }
 
 int tile_tokens(int kt) { return 16 * kSW * (kt == 16 ? 1 : (kt == 8 ? 2 : 4)); }
