@@ -24,6 +24,10 @@ def decode_attn_bf16(q, k, v):
     -> [B,H_q,1,D] in q.dtype. A non-bf16 query is rounded to bf16 for the
     tensor-core contraction.
     """
+    if q.is_cuda and q.dtype == torch.bfloat16:
+        rc, out = _ops.N.glue().decode_attn_nq(q, k, v)
+        if rc == 0:
+            return out
     q3 = _squeeze_q(q)
     if q3.dtype != torch.bfloat16:
         q3 = q3.to(torch.bfloat16)
@@ -34,6 +38,10 @@ def decode_attn_bf16(q, k, v):
 
 def decode_attn_fp8(q, k, v):
     """decode_attn_bf16 over an fp8 e4m3 KV cache. ref: src/attention_kernels.py:156-182."""
+    if q.is_cuda:
+        rc, out = _ops.N.glue().decode_attn_nq(q, k, v)
+        if rc == 0:
+            return out
     q3 = _squeeze_q(q)
     out = torch.empty(q3.shape, dtype=q.dtype, device=q.device)
     _ops.decode_attn(q3, k, v, 1.0, out)

@@ -93,7 +93,11 @@ struct KL {
   static constexpr int T_GROUP = 4 * T_COL;
   static constexpr int T_BYTES = 8 * T_GROUP;
   static constexpr int OFF_T = OFF_KC + 2 * KC_BYTES;  // two buffers: tile it and tile it + 1
-  static constexpr int OFF_BAR = OFF_T + 2 * T_BYTES;  // TMA: one mbarrier per stage
+  // 2-bit: each warp's value scales / minima of its 32 tokens as (token, token + 4) operand
+  // pairs: [scale, min][4 groups][4 lane columns tq][(rb, e) = 4 pairs] half2
+  static constexpr int VP_WARP = 2 * 4 * 4 * 4 * 4;
+  static constexpr int OFF_VP = OFF_T + 2 * T_BYTES;
+  static constexpr int OFF_BAR = OFF_VP + (BITS == 2 ? 4 * VP_WARP : 0);  // TMA: one mbarrier per stage
   static constexpr int SMEM = OFF_BAR + kStagesK * 8;
   static constexpr uint32_t TMA_BYTES = 128 * 32 + kTile * 32 + 2 * kTile * 8;  // K, V codes, V scale, V min
   static_assert(!TMA || (BITS == 2 && STAGE % 1024 == 0), "TMA stages hold the 2-bit tile at 1024-byte alignment");
@@ -305,17 +309,19 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
     const uint8_t* kc = smem + L::OFF_KC + ((tile / kKChunk) & 1) * L::KC_BYTES + threadIdx.x * L::KC_ROW +
                         (tile % kKChunk) * 8;
     const uint2 s4 = *reinterpret_cast<const uint2*>(kc);
-    const uint2 m4 = *reinterpret_cast<const uint2*>(kc + 128 * L::KC_ROW);
     uint8_t* ts = tsm + (tile & 1) * L::T_BYTES + t_slot;
     *reinterpret_cast<uint16_t*>(ts + 0 * L::T_GROUP) = uint16_t(s4.x);
     *reinterpret_cast<uint16_t*>(ts + 1 * L::T_GROUP) = uint16_t(s4.x >> 16);
     *reinterpret_cast<uint16_t*>(ts + 2 * L::T_GROUP) = uint16_t(s4.y);
     *reinterpret_cast<uint16_t*>(ts + 3 * L::T_GROUP) = uint16_t(s4.y >> 16);
-    *reinterpret_cast<uint16_t*>(ts + 4 * L::T_GROUP) = uint16_t(m4.x);
-    *reinterpret_cast<uint16_t*>(ts + 5 * L::T_GROUP) = uint16_t(m4.x >> 16);
-    *reinterpret_cast<uint16_t*>(ts + 6 * L::T_GROUP) = uint16_t(m4.y);
-    *reinterpret_cast<uint16_t*>(ts + 7 * L::T_GROUP) = uint16_t(m4.y >> 16);
   };
+  // ldmatrix.trans rows of a chunk's key minima for the per-chunk bias MMA: matrix lane >> 3
+  // = (channel half lane >> 4, group half (lane >> 3) & 1)
+  const uint32_t lm_off = uint32_t(((lane >> 4) * 8 + (lane & 7)) * L::KC_ROW + ((lane >> 3) & 1) * 16);
+  float bacc[4] = {0.f, 0.f, 0.f, 0.f};  // key bias of the chunk's 16 groups (rows), heads 2tq, 2tq+1
+  // 2-bit: this lane's slot in its warp's value operand pairs (lane = token 32 warp + lane)
+  uint8_t* vp_warp = smem + L::OFF_VP + warp * L::VP_WARP;
+  const uint32_t vp_tok = ((((lane >> 3) * 4 + ((lane & 7) >> 1 & 1) * 2 + (lane & 1)) * 4) + ((lane & 7) >> 2) * 2);
 
   // prologue: tile 0 and the first key scale/min chunk in flight
   if (ntiles > 0) {
@@ -414,28 +420,39 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
     const int tb = t_begin + it * kTile + 32 * warp;  // first token of this warp's group
     if (tb >= t_end) continue;
 
-    // ---- Q' = q * s_k (f16) and bias = sum_c q_c m_c on the tensor cores. One 16-byte
-    // read {m(2k, h0), m(2k+1, h0), m(2k, h1), m(2k+1, h1)} is the A operand of both
-    // k-steps: with B = q of step 2k the A rows g carry step 2k, with B = q of step 2k+1 the
-    // rows g+8 carry step 2k+1, each row holding the bias of the lane's two heads.
-    uint32_t qb[8][2];
+    // ---- key bias sum_c q_c m_c of all 16 groups of a 4-tile chunk, once per chunk: the
+    // chunk's minima [16 groups x 16 channels] per k-step are the A operand (ldmatrix.trans
+    // of the channel-major chunk buffer), accumulator rows = groups, columns = heads
+    if (it % kKChunk == 0) {
+      const uint32_t mb =
+          smem_u32(smem + L::OFF_KC + ((it / kKChunk) & 1) * L::KC_BYTES + 128 * L::KC_ROW) + lm_off;
+      bacc[0] = bacc[1] = bacc[2] = bacc[3] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(a0, a1, a2, a3, mb + 16 * j * L::KC_ROW);
+        mma_f16(bacc, a0, a1, a2, a3, qh[j][0], qh[j][1]);
+      }
+    }
     float bias[2];
     {
+      const int r = 4 * (it % kKChunk) + warp;  // this warp's group within the chunk
+      const int src = ((r & 7) << 2) | tq;
+      bias[0] = __shfl_sync(0xffffffffu, r < 8 ? bacc[0] : bacc[2], src) * score_mul;
+      bias[1] = __shfl_sync(0xffffffffu, r < 8 ? bacc[1] : bacc[3], src) * score_mul;
+    }
+    // ---- Q' = q * s_k (f16) from the regrouped key scales
+    uint32_t qb[8][2];
+    {
       const uint4* tsr = reinterpret_cast<const uint4*>(tsc + warp * L::T_GROUP + tq * L::T_COL);
-      const uint4* tmr = reinterpret_cast<const uint4*>(tsc + (4 + warp) * L::T_GROUP + tq * L::T_COL);
-      float be[4] = {0.f, 0.f, 0.f, 0.f}, bo[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint4 sc = tsr[k], mn = tmr[k];
+        const uint4 sc = tsr[k];
         qb[2 * k][0] = h2u(__hmul2(u2h(qh[2 * k][0]), u2h(sc.x)));
         qb[2 * k][1] = h2u(__hmul2(u2h(qh[2 * k][1]), u2h(sc.z)));
         qb[2 * k + 1][0] = h2u(__hmul2(u2h(qh[2 * k + 1][0]), u2h(sc.y)));
         qb[2 * k + 1][1] = h2u(__hmul2(u2h(qh[2 * k + 1][1]), u2h(sc.w)));
-        mma_f16(be, mn.x, mn.y, mn.z, mn.w, qh[2 * k][0], qh[2 * k][1]);
-        mma_f16(bo, mn.x, mn.y, mn.z, mn.w, qh[2 * k + 1][0], qh[2 * k + 1][1]);
       }
-      bias[0] = (be[0] + bo[2]) * score_mul;
-      bias[1] = (be[1] + bo[3]) * score_mul;
     }
 
     // ---- S^T (each row scaled by 2^(pos-24)) for the warp's two 16-token row blocks
@@ -543,12 +560,38 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
 
     // ---- P' = P * s_v per group; PV and the value-minimum term on the tensor cores
     const int tw = 32 * warp;  // tile-local first token of the warp's group
+    if (BITS == 2) {
+      // the warp's value scales / minima as operand pairs (token, token + 4): lane = token
+      const uint2 sv = *reinterpret_cast<const uint2*>(st + L::OFF_VS + (tw + lane) * 8);
+      const uint2 mv = *reinterpret_cast<const uint2*>(st + L::OFF_VM + (tw + lane) * 8);
+      const uint32_t svw[2] = {sv.x, sv.y}, mvw[2] = {mv.x, mv.y};
+#pragma unroll
+      for (int gr = 0; gr < 4; ++gr) {
+        *reinterpret_cast<uint16_t*>(vp_warp + gr * 64 + vp_tok) = uint16_t(svw[gr >> 1] >> (16 * (gr & 1)));
+        *reinterpret_cast<uint16_t*>(vp_warp + 256 + gr * 64 + vp_tok) = uint16_t(mvw[gr >> 1] >> (16 * (gr & 1)));
+      }
+      __syncwarp();
+    }
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) {
       uint32_t pb[4][2];
       const uint32_t hp0 = pack_f16x2(pv[rb][0], pv[rb][1]);
       const uint32_t hp1 = pack_f16x2(pv[rb][2], pv[rb][3]);
-      {
+      if (BITS == 2) {
+        // P transposed once into the PV B layout: k pairs (2tq, 2tq+1) / (2tq+8, 2tq+9) are the
+        // tokens (T0, T0+4) / (T0+1, T0+5), T0 = 8tq + 2rb; then one scale pair per group
+        const uint32_t pt0 = movmatrix_trans(hp0), pt1 = movmatrix_trans(hp1);
+#pragma unroll
+        for (int gr = 0; gr < 4; ++gr) {
+          const uint2 sp = *reinterpret_cast<const uint2*>(vp_warp + gr * 64 + tq * 16 + rb * 8);
+          pb[gr][0] = h2u(__hmul2(u2h(pt0), u2h(sp.x)));
+          pb[gr][1] = h2u(__hmul2(u2h(pt1), u2h(sp.y)));
+        }
+        // value minima: A rows g < 4 = groups, the same token pairs
+        const uint2 mp = *reinterpret_cast<const uint2*>(vp_warp + 256 + (g & 3) * 64 + tq * 16 + rb * 8);
+        const uint32_t keep = g < 4 ? 0xffffffffu : 0u;
+        mma_f16(cacc, mp.x & keep, 0u, mp.y & keep, 0u, pt0, pt1);
+      } else {
         // value scales of the tokens of rows g and g+8 (adjacent tokens in the 2-bit form)
         const int tr = tw + row_token(rb);
         uint32_t s0w[2], s1w[2];
@@ -567,7 +610,6 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
           pb[gr][0] = movmatrix_trans(h2u(__hmul2(u2h(hp0), sa)));
           pb[gr][1] = movmatrix_trans(h2u(__hmul2(u2h(hp1), sb)));
         }
-      }
       // After the transpose, MMA k index kappa (0..15) of this row block is accumulator row
       // kappa: lane tq's k pairs (2tq, 2tq+1) and (2tq+8, 2tq+9) are the tokens
       //  2-bit: tq8 + {0, 4} and tq8 + {1, 5}, tq8 = 8tq + 2rb;
@@ -582,6 +624,7 @@ __global__ void __launch_bounds__(kWarpsK * 32, MINB)
         const uint32_t a0 = (lds_u16(vmr) | (lds_u16(vmr + kd1 * 8) << 16)) & keep;
         const uint32_t a2 = (lds_u16(vmr + kd2 * 8) | (lds_u16(vmr + kd3 * 8) << 16)) & keep;
         mma_f16(cacc, a0, 0u, a2, 0u, pt0, pt1);
+      }
       }
       if (BITS == 2) {
         // tokens tw + kt0 + {0, 4, 1, 5} sit at interleaved rows (kt0 + d) * 16 + tq + 4 warp

@@ -11,7 +11,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cmath>
 #include <stdexcept>
+#include <tuple>
 
 #include "bdecode.h"
 
@@ -75,10 +77,63 @@ int64_t decode_attn(const at::Tensor& q3, const at::Tensor& k, const at::Tensor&
                         at::cuda::getCurrentCUDAStream(dev).stream());
 }
 
+// Descriptor of a [B, H, 1, D] tensor viewed as [B, H, D] (the reference's decode query and
+// output layout), without creating the view.
+bd_tensor desc_drop2(const at::Tensor& t, int device) {
+  bd_tensor d = desc(t, device);
+  d.ndim = 3;
+  d.shape[2] = t.size(3);
+  d.stride[2] = t.stride(3);
+  return d;
+}
+
+// kivi_decode_attn(Q [B,Hq,1,D], packed caches, bits, group_size) -> (status, out [B,Hq,1,D]).
+// The whole drop-in call in C++: output allocation, descriptors, workspace and the two
+// launches. A non-zero status leaves the caller to take its general path (re-laid-out
+// copies, or the error).
+std::tuple<int64_t, at::Tensor> kivi_decode_attn(const at::Tensor& Q, const at::Tensor& Kq, const at::Tensor& Ks,
+                                                 const at::Tensor& Km, const at::Tensor& Kr, const at::Tensor& Vq,
+                                                 const at::Tensor& Vs, const at::Tensor& Vm, const at::Tensor& Vr,
+                                                 int64_t bits, int64_t group_size) {
+  if (Q.dim() != 4 || Q.size(2) != 1 || Kr.scalar_type() != at::kBFloat16 || Vr.scalar_type() != at::kBFloat16 ||
+      Ks.scalar_type() != at::kHalf || Km.scalar_type() != at::kHalf || Vs.scalar_type() != at::kHalf ||
+      Vm.scalar_type() != at::kHalf || (Q.scalar_type() != at::kBFloat16 && Kr.size(2) > 0))
+    return {BD_ERR_DTYPE, at::Tensor()};
+  const int dev = Q.get_device();
+  at::Tensor out = at::empty({Q.size(0), Q.size(1), 1, Q.size(3)}, Q.options());
+  const bd_tensor dq = desc_drop2(Q, dev), dkq = desc(Kq, dev), dks = desc(Ks, dev), dkm = desc(Km, dev),
+                  dkr = desc(Kr, dev), dvq = desc(Vq, dev), dvs = desc(Vs, dev), dvm = desc(Vm, dev),
+                  dvr = desc(Vr, dev), dout = desc_drop2(out, dev);
+  const c10::cuda::CUDAGuard guard(Q.device());
+  const size_t nws = bd_kivi_decode_attn_workspace(&dq, &dkq, &dkr, int(bits));
+  const at::Tensor ws = workspace(nws, Q);
+  const int rc = bd_kivi_decode_attn_stages(&dq, &dkq, &dks, &dkm, &dkr, &dvq, &dvs, &dvm, &dvr, int(bits),
+                                            int(group_size), float(1.0 / std::sqrt(double(Q.size(3)))), &dout,
+                                            ws.data_ptr(), nws, 7, at::cuda::getCurrentCUDAStream(dev).stream());
+  return {rc, out};
+}
+
+// decode_attn_bf16 / decode_attn_fp8 (no scale) -> (status, out [B,Hq,1,D] in q's dtype).
+std::tuple<int64_t, at::Tensor> decode_attn_nq(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
+  if (q.dim() != 4 || q.size(2) != 1) return {BD_ERR_SHAPE, at::Tensor()};
+  if (k.scalar_type() == at::kBFloat16 && q.scalar_type() != at::kBFloat16) return {BD_ERR_DTYPE, at::Tensor()};
+  const int dev = q.get_device();
+  at::Tensor out = at::empty({q.size(0), q.size(1), 1, q.size(3)}, q.options());
+  const bd_tensor dq = desc_drop2(q, dev), dk = desc(k, dev), dv = desc(v, dev), dout = desc_drop2(out, dev);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const size_t nws = bd_decode_attn_workspace(&dq, &dk);
+  const at::Tensor ws = workspace(nws, q);
+  const int rc = bd_decode_attn(&dq, &dk, &dv, &dout, 1.0f, ws.data_ptr(), nws,
+                                at::cuda::getCurrentCUDAStream(dev).stream());
+  return {rc, out};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "C++ descriptor glue for the bytes_b200 decode entry points";
   m.def("kivi_decode", &kivi_decode, "bd_kivi_decode_attn_stages on the current CUDA stream");
   m.def("decode_attn", &decode_attn, "bd_decode_attn on the current CUDA stream");
+  m.def("kivi_decode_attn", &kivi_decode_attn, "the drop-in KIVI decode step: (status, out [B,Hq,1,D])");
+  m.def("decode_attn_nq", &decode_attn_nq, "decode_attn_bf16 / decode_attn_fp8: (status, out [B,Hq,1,D])");
 }

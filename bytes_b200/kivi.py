@@ -19,6 +19,11 @@ def kivi_decode_attn(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_resi
     cache, then one over the residual window that also merges the split partials (the
     reference issues 6+ launches and materialises the scores).
     """
+    if Q.is_cuda:
+        rc, out = _ops.N.glue().kivi_decode_attn(Q, Kq, K_scale, K_mn, K_residual, Vq, V_scale, V_mn, V_residual,
+                                                 int(bits), int(group_size))
+        if rc == 0:
+            return out
     if Q.dim() != 4 or Q.shape[2] != 1:
         raise ValueError("Q must be [B, H_q, 1, D]")
     Q3 = Q[:, :, 0, :]
