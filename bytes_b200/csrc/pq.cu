@@ -57,6 +57,9 @@ struct PqParams {
   int B, Hq, Hk, G, S, M, K, D;
   int head_chunks, ntiles, n_splits;  // split s owns tiles [s*ntiles/n_splits, (s+1)*ntiles/n_splits)
   float* scores_out; int64_t so_sb, so_sh;  // V_NONE mode
+  // M = 16, K = 256: the LUT re-laid out per (batch, KV head, head chunk) as [K][M][4 heads]
+  // (pq_lut_regroup_kernel), so one 16-byte read returns the four heads of a lookup
+  const float4* lut_t;
   float* part_m; float* part_l; float* part_o;
 };
 
@@ -109,6 +112,15 @@ __host__ __device__ inline PqSmem pq_smem(int vk, int M, int K, int C, int D, in
 // TMA waits that ran past their iteration limit (a non-zero count means a result is wrong)
 __device__ unsigned int g_pq_tma_timeouts = 0;
 
+// (a.x + b.x, a.y + b.y), both rounded to nearest: one paired fp32 add
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  unsigned long long x, y, z;
+  x = (static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
+  y = (static_cast<unsigned long long>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(z) : "l"(x), "l"(y));
+  return make_float2(__uint_as_float(uint32_t(z)), __uint_as_float(uint32_t(z >> 32)));
+}
+
 __device__ __forceinline__ float ld16f(const uint16_t* p, int64_t off, int dt) {
   const uint16_t u = p[off];
   return dt == BD_BF16 ? __uint_as_float(uint32_t(u) << 16) : __half2float(__ushort_as_half(u));
@@ -150,9 +162,15 @@ __global__ void __launch_bounds__(kPW * 32, 2)
   const int t_end = min(S_b, int(int64_t(split + 1) * p.ntiles / p.n_splits) * kPRows);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kPRows - 1) / kPRows : 0;
 
-  // ---- LUT of the chunk's heads -> smem [M][K][4]; rows of a head are read four
-  // entries at a time when they are contiguous and 16-byte aligned
-  {
+  // ---- LUT of the chunk's heads -> smem: the regrouped [K][M][4] copy when there is one
+  // (one contiguous 64 KB block), else [M][K][4] from the caller's layout; rows of a head
+  // are read four entries at a time when they are contiguous and 16-byte aligned
+  if (p.lut_t) {
+    const float4* src = p.lut_t + ((int64_t(b) * p.Hk + hk) * p.head_chunks + chunk) * (256 * 16);
+    for (int i = threadIdx.x; i < 256 * 16; i += kPW * 32) cp_async16(smem_u32(lut_s) + i * 16, src + i, 16);
+    cp_async_commit();
+    cp_async_wait<0>();
+  } else {
     const int MK = p.M * p.K;
     const bool vec = p.l_sk == 1 && p.l_sm == p.K && (p.K & 3) == 0 && (p.l_sh & 3) == 0 && (p.l_sb & 3) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.lut) & 15) == 0;
@@ -340,32 +358,66 @@ __global__ void __launch_bounds__(kPW * 32, 2)
     // ---- LUT scores for tokens r0+g, r0+g+8 and heads 2hp, 2hp+1 over subspaces [jlo, jhi)
     float sc[4] = {0.f, 0.f, 0.f, 0.f};  // (row g: h0, h1), (row g+8: h0, h1)
     {
-      const uint8_t* ca = st + L.off_codes + (r0 + g) * L.codes_pitch;
-      const uint8_t* cb = st + L.off_codes + (r0 + g + 8) * L.codes_pitch;
-      const float* lj = lut_s + jlo * p.K * kHC + 2 * hp;  // LUT rows of subspace j, stepped per j
-      const int jstep = p.K * kHC;
-      if (p.M == 16) {
-        // the lane's 8 subspaces of both tokens as one 8-byte load each
-        const uint2 wa = *reinterpret_cast<const uint2*>(ca + jlo), wb = *reinterpret_cast<const uint2*>(cb + jlo);
+      if (p.lut_t) {
+        // regrouped LUT [code][subspace][4 heads]: lane = (token lane >> 1, subspace half
+        // lane & 1); step s looks up subspace 8(lane & 1) + ((s + lane) & 7) with one 16-byte
+        // read of all four heads. The 16-byte unit of (code, j) sits in bank group j & 7, so
+        // the 8 lanes of a quarter-warp (distinct (s + lane) & 7) never share a bank group.
+        const uint2 w = *reinterpret_cast<const uint2*>(st + L.off_codes + (r0 + (lane >> 1)) * L.codes_pitch +
+                                                        8 * (lane & 1));
+        float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+        const uint8_t* lb = reinterpret_cast<const uint8_t*>(lut_s);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t xa = ((j < 4 ? wa.x : wa.y) >> (8 * (j & 3))) & 0xffu;
-          const uint32_t xb = ((j < 4 ? wb.x : wb.y) >> (8 * (j & 3))) & 0xffu;
-          const float2 a = *reinterpret_cast<const float2*>(lj + xa * kHC);
-          const float2 c = *reinterpret_cast<const float2*>(lj + xb * kHC);
-          sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
-          lj += jstep;
+        for (int s2 = 0; s2 < 8; ++s2) {
+          // byte 0: which of the lane's 8 code bytes; byte 2: the subspace's offset j * 16
+          const uint32_t r = uint32_t(s2 + lane) & 7u;
+          const uint32_t rs = r | (((8u * uint32_t(lane & 1) + r) * 16u) << 16);
+          const uint32_t code = prmt(w.x, w.y, rs);    // byte 0 = the code
+          const uint32_t off = prmt(code, rs, 0x7706);  // [j * 16, code, 0, 0] = code * 256 + j * 16
+          const float4 e = *reinterpret_cast<const float4*>(lb + off);
+          a01 = add_f32x2(a01, make_float2(e.x, e.y));
+          a23 = add_f32x2(a23, make_float2(e.z, e.w));
         }
+        // the two subspace halves of a token are neighbouring lanes
+        a01.x += __shfl_xor_sync(0xffffffffu, a01.x, 1);
+        a01.y += __shfl_xor_sync(0xffffffffu, a01.y, 1);
+        a23.x += __shfl_xor_sync(0xffffffffu, a23.x, 1);
+        a23.y += __shfl_xor_sync(0xffffffffu, a23.y, 1);
+        // into the accumulator layout: lane (g, tq) takes heads 2hp, 2hp+1 of tokens g and
+        // g + 8 from lanes 2g + hp and 2g + 16 + hp (odd lanes hold heads 2, 3)
+        const float2 pr = (lane & 1) ? a23 : a01;
+        sc[0] = __shfl_sync(0xffffffffu, pr.x, 2 * g + hp);
+        sc[1] = __shfl_sync(0xffffffffu, pr.y, 2 * g + hp);
+        sc[2] = __shfl_sync(0xffffffffu, pr.x, 2 * g + 16 + hp);
+        sc[3] = __shfl_sync(0xffffffffu, pr.y, 2 * g + 16 + hp);
       } else {
-        for (int j = jlo; j < jhi; ++j) {
-          const float2 a = *reinterpret_cast<const float2*>(lj + ca[j] * kHC);
-          const float2 c = *reinterpret_cast<const float2*>(lj + cb[j] * kHC);
-          sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
-          lj += jstep;
-        }
-      }
+        const uint8_t* ca = st + L.off_codes + (r0 + g) * L.codes_pitch;
+        const uint8_t* cb = st + L.off_codes + (r0 + g + 8) * L.codes_pitch;
+        const float* lj = lut_s + jlo * p.K * kHC + 2 * hp;  // LUT rows of subspace j, stepped per j
+        const int jstep = p.K * kHC;
+        if (p.M == 16) {
+          // the lane's 8 subspaces of both tokens as one 8-byte load each
+          const uint2 wa = *reinterpret_cast<const uint2*>(ca + jlo), wb = *reinterpret_cast<const uint2*>(cb + jlo);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t xa = ((j < 4 ? wa.x : wa.y) >> (8 * (j & 3))) & 0xffu;
+            const uint32_t xb = ((j < 4 ? wb.x : wb.y) >> (8 * (j & 3))) & 0xffu;
+            const float2 a = *reinterpret_cast<const float2*>(lj + xa * kHC);
+            const float2 c = *reinterpret_cast<const float2*>(lj + xb * kHC);
+            sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
+            lj += jstep;
+          }
+        } else {
+          for (int j = jlo; j < jhi; ++j) {
+            const float2 a = *reinterpret_cast<const float2*>(lj + ca[j] * kHC);
+            const float2 c = *reinterpret_cast<const float2*>(lj + cb[j] * kHC);
+            sc[0] += a.x; sc[1] += a.y; sc[2] += c.x; sc[3] += c.y;
+            lj += jstep;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
+      }
       if (OUTL) {
         const uint16_t* ka = reinterpret_cast<const uint16_t*>(st + L.off_kout + (r0 + g) * L.kout_pitch);
         const uint16_t* kb = reinterpret_cast<const uint16_t*>(st + L.off_kout + (r0 + g + 8) * L.kout_pitch);
@@ -618,6 +670,23 @@ __global__ void pq_encode_kernel(const void* x, int x_dtype, int64_t x_sn, const
   else reinterpret_cast<uint8_t*>(codes)[n * M + j] = uint8_t(bi);
 }
 
+// LUT [B,Hq,16,256] fp32 (any strides) -> one block per (batch, KV head, head chunk) of
+// [256 codes][16 subspaces][4 heads], heads past the group zero. Grid (B*Hk*chunks, 16),
+// 256 threads (thread = code): reads are coalesced along the codes.
+__global__ void pq_lut_regroup_kernel(const float* __restrict__ lut, int64_t l_sb, int64_t l_sh, int64_t l_sm,
+                                      int64_t l_sk, int Hk, int G, int head_chunks, float4* __restrict__ out) {
+  const int bc = blockIdx.x, j = blockIdx.y, code = threadIdx.x;
+  const int chunk = bc % head_chunks, bh = bc / head_chunks;
+  const int hk = bh % Hk, b = bh / Hk;
+  const int h0 = chunk * kHC, nheads = min(kHC, G - h0);
+  float v[kHC];
+#pragma unroll
+  for (int h = 0; h < kHC; ++h)
+    v[h] = h < nheads ? lut[int64_t(b) * l_sb + int64_t(hk * G + h0 + h) * l_sh + int64_t(j) * l_sm + int64_t(code) * l_sk]
+                      : 0.f;
+  out[int64_t(bc) * (256 * 16) + code * 16 + j] = make_float4(v[0], v[1], v[2], v[3]);
+}
+
 // Dynamic shared memory of one CTA (the TMA form adds its alignment slack and barriers).
 inline size_t pq_cta_smem(const PqSmem& L, int D, bool tma) {
   const size_t body = size_t(L.off_stages) + size_t(kPStages) * L.stage + L.recon_bytes + (tma ? 16 + 1024 : 0);
@@ -798,7 +867,12 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
   const int64_t slots = per_sm * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / pairs;
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
-  const size_t need = scores_only ? 0 : partials_bytes(size_t(B * Hq), int(splits), int(D));
+  // M = 16, K = 256 (the usual codebook): the LUT is regrouped per call into the workspace
+  // behind the partials, so the decode CTAs read it as one contiguous block
+  const bool fast_lut = !scores_only && M == 16 && K == 256;
+  const size_t part_bytes = scores_only ? 0 : partials_bytes(size_t(B * Hq), int(splits), int(D));
+  const size_t lut_bytes = fast_lut ? size_t(B * Hk * head_chunks) * 256 * 16 * 16 : 0;
+  const size_t need = part_bytes + (fast_lut ? lut_bytes + 256 : 0);
   if (ws_query) { *ws_query = need; return BD_OK; }
   if (!out_or_scores) return fail(BD_ERR_NULL, "output descriptor is NULL");
   if (!scores_only && (!workspace || workspace_bytes < need))
@@ -848,6 +922,13 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
   }
   Partials part = carve_partials(workspace, size_t(B * Hq), int(splits), int(D));
   p.part_m = part.m; p.part_l = part.l; p.part_o = part.o;
+  if (fast_lut) {
+    const uintptr_t lut_at = (reinterpret_cast<uintptr_t>(part.l + size_t(B * Hq) * splits) + 255) & ~uintptr_t(255);
+    p.lut_t = reinterpret_cast<const float4*>(lut_at);
+    pq_lut_regroup_kernel<<<dim3(unsigned(B * Hk * head_chunks), 16), 256, 0, st>>>(
+        p.lut, p.l_sb, p.l_sh, p.l_sm, p.l_sk, int(Hk), int(Hq / Hk), head_chunks, reinterpret_cast<float4*>(lut_at));
+    if ((rc = cuda_check(cudaGetLastError(), "pq_lut_regroup_kernel launch"))) return rc;
+  }
   if ((rc = dispatch_pq(p, vk, paged, outl, st))) return rc;
   return launch_combine(part, int(B), int(Hq), int(D), out_or_scores, st, true);
 }
