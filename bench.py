@@ -24,9 +24,11 @@ cpu_baseline / --impl reference: the reference's own CPU-runnable KIVI path
            the installed reference in baseline/_ref), else the fp32 torch restatement of it
            in oracle/, on the host cores.
 split_kv   (every N) one 1M-token bf16 sequence split across the N ranks: per-rank split-KV
-           partial, one NCCL all-gather of the (max, sum, numerator) partials and the
-           log-sum-exp combine inside the timed step; the result is checked against
-           single-GPU decode of the whole sequence before timing (parity_ok).
+           partial, the exchange of the (max, sum, numerator) partials and the log-sum-exp
+           combine inside the timed step; at N > 1 the exchange is NVLink peer stores fused
+           with the combine (one kernel), with the NCCL all-gather step timed beside it. The
+           result is checked against single-GPU decode of the whole sequence before timing
+           (parity_ok).
 """
 import argparse
 import hashlib
@@ -566,10 +568,13 @@ def _split_shard(dev, i, n, Hk, D):
 def split_kv_bench(dev, rank, world, dist, steps, warmup, peak):
     """One 1M-token bf16 sequence (28/4 heads, D=128) split along its tokens across the ranks.
 
-    Step = this rank's split-KV partial over its shard (CUDA graph), one all-gather of the
-    packed (max, sum, numerator) partials of every rank (NCCL), and the log-sum-exp combine
-    (CUDA graph). Before timing, every rank checks the combined output against single-GPU
-    decode of the whole sequence; the ranks agree on the verdict through an all-reduce."""
+    Step = this rank's split-KV partial over its shard, then the exchange of the (max, sum,
+    numerator) partials and their log-sum-exp combine. Two exchanges are timed: the split
+    pass followed by one kernel that merges the splits, stores the merged partials into every
+    rank's buffer over NVLink and combines (bytes_b200.distributed.PeerExchange.decode; one
+    CUDA graph per step), and NCCL's all-gather between the partial and combine graphs.
+    Before timing, every rank checks each combined output against single-GPU decode of the
+    whole sequence; the ranks agree on the verdict through an all-reduce."""
     from bytes_b200 import _ops, attention_kernels as ak
     Hq, Hk, D = 28, 4, 128
     scal = 1.0 / math.sqrt(D)
@@ -605,8 +610,34 @@ def split_kv_bench(dev, rank, world, dist, steps, warmup, peak):
         exchange()
         g_comb.replay()
 
+    # the peer exchange (N > 1 with symmetric memory): partial + exchange + combine, one graph
+    peer, peer_note = None, None
+    if dist is not None:
+        ok = 1.0
+        try:
+            from bytes_b200.distributed import PeerExchange
+            peer = PeerExchange(1, Hq, D, dev)
+        except Exception as e:  # symmetric memory unavailable: NCCL only
+            peer_note = f"{type(e).__name__}: {e}"[:160]
+            ok = 0.0
+        t = torch.tensor([ok], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        if t.item() < 1.0:
+            peer = None
+    out_peer = torch.empty(1, Hq, D, dtype=torch.bfloat16, device=dev)
+
+    def peer_step():
+        out_peer.copy_(peer.decode(q3, k_sh, v_sh, scal, torch.bfloat16))
+
+    g_peer = graph_of([peer_step]) if peer is not None else None
+    if peer is not None:  # the exchange kernel alone, on fixed partials
+        part_fixed = _ops.decode_attn_partial(q3, k_sh, v_sh, scal)
+        g_ex = graph_of([lambda: peer(*part_fixed, torch.bfloat16)])
+
     # parity: the split result against single-GPU decode of the whole sequence
     step()
+    if g_peer is not None:
+        g_peer.replay()
     torch.cuda.synchronize()
     parts = [_split_shard(dev, i, world, Hk, D) for i in range(world)]
     k_full = torch.cat([p[0] for p in parts], 2)
@@ -617,10 +648,13 @@ def split_kv_bench(dev, rank, world, dist, steps, warmup, peak):
     ref32 = torch.softmax((k_full[0].float() @ (q3[0].float().view(Hk, Hq // Hk, D).transpose(1, 2)) * scal)
                           .transpose(1, 2), -1) @ v_full[0].float()
     del k_full, v_full
-    d = (out[0].float() - ref32.reshape(Hq, D)).abs()
-    d2 = (out.float() - ref.float()).abs()
-    ok = bool(torch.isfinite(out.float()).all().item() and d.max().item() <= 2e-2 and d.mean().item() <= 1e-3
-              and d2.max().item() <= 2e-2)
+    def agrees(x):
+        d = (x[0].float() - ref32.reshape(Hq, D)).abs()
+        d2 = (x.float() - ref.float()).abs()
+        return bool(torch.isfinite(x.float()).all().item() and d.max().item() <= 2e-2 and d.mean().item() <= 1e-3
+                    and d2.max().item() <= 2e-2)
+
+    ok = agrees(out) and (g_peer is None or agrees(out_peer))
     flag = torch.tensor([1.0 if ok else 0.0], device=dev)
     if dist is not None:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
@@ -650,19 +684,56 @@ def split_kv_bench(dev, rank, world, dist, steps, warmup, peak):
     e1.record(st)
     e1.synchronize()
     us_ag = e0.elapsed_time(e1) * 1e3 / steps
-    t = torch.tensor([us_step, us_ag], device=dev)
+    # the peer-exchange step, and the partial alone (to attribute the exchange's share)
+    us_peer = us_part = us_ex = 0.0
+    if g_peer is not None:
+        for gr in (g_peer, g_ex):
+            for _ in range(max(warmup, 3)):
+                gr.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(st)
+            for _ in range(steps):
+                gr.replay()
+            e1.record(st)
+            e1.synchronize()
+            if gr is g_peer:
+                us_peer = e0.elapsed_time(e1) * 1e3 / steps
+            else:
+                us_ex = e0.elapsed_time(e1) * 1e3 / steps
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(steps):
+        g_part.replay()
+    e1.record(st)
+    e1.synchronize()
+    us_part = e0.elapsed_time(e1) * 1e3 / steps
+    t = torch.tensor([us_step, us_ag, us_peer, us_part, us_ex], device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    us_step, us_ag = float(t[0].item()), float(t[1].item())
+    us_nccl, us_ag, us_peer, us_part, us_ex = (float(x) for x in t.tolist())
+    us_best = us_peer if g_peer is not None else us_nccl
     shard_bytes = nbytes(k_sh, v_sh)
-    del g_part, g_comb
-    return {"tokens": SPLIT_TOKENS, "ranks": world, "shard_tokens": SPLIT_TOKENS // world, "us": round(us_step, 2),
-            "allgather_us": round(us_ag, 2), "allgather_share": round(us_ag / us_step, 3),
-            "exchange_bytes_per_rank": width * 4, "tokens_per_s": round(1e6 / us_step, 1),
-            "shard_GBps": round(shard_bytes / us_step / 1e3, 1),
-            "shard_frac": round(shard_bytes / us_step / 1e3 / peak, 3), "parity_ok": parity_ok,
-            "steps": steps, "timing": "partial and combine as CUDA graphs, NCCL all-gather between, CUDA events, "
+    used_peer = g_peer is not None
+    del g_part, g_comb, g_peer
+    if used_peer:
+        del g_ex
+    line = {"tokens": SPLIT_TOKENS, "ranks": world, "shard_tokens": SPLIT_TOKENS // world, "us": round(us_best, 2),
+            "exchange": "split merge + nvlink peer stores + combine, one kernel behind the split pass"
+                        if used_peer else ("nccl all-gather" if dist is not None else "none (one rank)"),
+            "partial_us": round(us_part, 2), "exchange_share": round(max(0.0, us_best - us_part) / us_best, 3),
+            "peer_exchange_alone_us": round(us_ex, 2) if used_peer else None,
+            "nccl_step_us": round(us_nccl, 2), "nccl_allgather_us": round(us_ag, 2),
+            "exchange_bytes_per_rank": width * 4 * max(1, world - 1), "tokens_per_s": round(1e6 / us_best, 1),
+            "shard_GBps": round(shard_bytes / us_best / 1e3, 1),
+            "shard_frac": round(shard_bytes / us_best / 1e3 / peak, 3), "parity_ok": parity_ok,
+            "steps": steps, "timing": "CUDA graphs (the NCCL all-gather eager between two), CUDA events, "
                                       "max over ranks"}
+    if peer_note:
+        line["peer_exchange_unavailable"] = peer_note
+    if peer is not None:
+        peer.buf = None
+    return line
 
 
 # ----------------------------------------------------------------------------- main

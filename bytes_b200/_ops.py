@@ -114,6 +114,40 @@ def decode_attn_partial(q3, k, v, scaling):
     return m, l, o
 
 
+def peer_exchange_combine(m, l, o, peers_dev, rank, world, out_dtype=torch.bfloat16):
+    """bd_peer_exchange_combine: this rank's m,l [B,Hq], o [B,Hq,D] fp32 -> [B,Hq,D] over all ranks.
+    peers_dev: device address of the [world] table of exchange-buffer bases."""
+    N.require_cuda(m, l, o)
+    m, l, o = m.contiguous(), l.contiguous(), o.contiguous()
+    B, Hq, D = o.shape
+    out = torch.empty(B, Hq, D, dtype=out_dtype, device=o.device)
+    dm, dl, do_, dout = N.desc(m), N.desc(l), N.desc(o), N.desc(out)
+    rc = _fn("bd_peer_exchange_combine", [P, P, P, VP, I, I, P, VP])(
+        ctypes.byref(dm), ctypes.byref(dl), ctypes.byref(do_), VP(peers_dev), int(rank), int(world),
+        ctypes.byref(dout), N.stream_of(o))
+    N.check(rc, "bd_peer_exchange_combine")
+    return out
+
+
+def split_kv_decode_peer(q3, k, v, scaling, peers_dev, rank, world, out_dtype=torch.bfloat16):
+    """bd_split_kv_decode_peer: dense split pass over this rank's token shard k,v and the
+    fused NVLink exchange + combine -> [B,Hq,D] over all ranks' shards."""
+    N.require_cuda(q3, k, v)
+    k = rows_aligned(k)
+    v = rows_aligned(v)
+    q3 = inner_contig(q3)
+    B, Hq, D = q3.shape
+    out = torch.empty(B, Hq, D, dtype=out_dtype, device=q3.device)
+    dq, dk, dv, dout = N.desc(q3), N.desc(k), N.desc(v), N.desc(out)
+    nws = _fn("bd_decode_attn_workspace", [P, P], SZ)(ctypes.byref(dq), ctypes.byref(dk))
+    buf, nb = _ws(nws, q3.device)
+    rc = _fn("bd_split_kv_decode_peer", [P, P, P, F, VP, I, I, P, VP, SZ, VP])(
+        ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), float(scaling), VP(peers_dev), int(rank), int(world),
+        ctypes.byref(dout), _ptr(buf), nb, N.stream_of(q3))
+    N.check(rc, "bd_split_kv_decode_peer")
+    return out
+
+
 def lse_combine(m, l, o, out_dtype=torch.bfloat16):
     """m,l [n,B,Hq], o [n,B,Hq,D] fp32 -> [B,Hq,D]."""
     N.require_cuda(m, l, o)

@@ -122,8 +122,9 @@ int bd_abi_version(void) { return 1; }
 
 long long bd_wait_timeouts(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  const long long a = bd::kivi_wait_timeouts(), b = bd::pq_wait_timeouts(), c = bd::merge_wait_timeouts();
-  return (a < 0 || b < 0 || c < 0) ? -1 : a + b + c;
+  const long long a = bd::kivi_wait_timeouts(), b = bd::pq_wait_timeouts(), c = bd::merge_wait_timeouts(),
+                  d = bd::exchange_wait_timeouts();
+  return (a < 0 || b < 0 || c < 0 || d < 0) ? -1 : a + b + c + d;
 }
 
 const char* bd_status_name(int s) {

@@ -41,6 +41,7 @@ std::string shape_str(const bd_tensor* t);
 long long kivi_wait_timeouts();
 long long pq_wait_timeouts();
 long long merge_wait_timeouts();
+long long exchange_wait_timeouts();
 // Tiled TMA tensor map of rank 3..5 (dims[0] contiguous; strides in bytes of dims 1..rank-1),
 // encoded through the driver entry point fetched from the runtime. False if unavailable or
 // rejected.
@@ -215,6 +216,15 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Store x into element `off` of an output of dtype dt (BD_BF16, BD_F16, else f32).
+__device__ __forceinline__ void store_as(void* base, int dt, int64_t off, float x) {
+  switch (dt) {
+    case BD_BF16: reinterpret_cast<__nv_bfloat16*>(base)[off] = __float2bfloat16_rn(x); break;
+    case BD_F16: reinterpret_cast<__half*>(base)[off] = __float2half_rn(x); break;
+    default: reinterpret_cast<float*>(base)[off] = x;
+  }
 }
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);

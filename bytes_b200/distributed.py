@@ -8,7 +8,9 @@ One process per GPU (torch.distributed, NCCL over NVLink/NVSwitch).
   [r*S/n, (r+1)*S/n). Each rank computes its shard's per-head (max, sum, numerator)
   partials with one split-KV kernel, the ranks all-gather those partials (B*Hq*(D+2)
   floats per rank, ~14.6 KB for 28 heads x 128 dims), and every rank merges them with a
-  log-sum-exp combine kernel, so all ranks end with the full attention output.
+  log-sum-exp combine kernel, so all ranks end with the full attention output. The
+  all-gather is NCCL's, or (``PeerExchange``) peer stores over NVLink done by the same
+  kernel that merges this rank's splits and combines the ranks' partials.
 * Exact top-k sparse decode over such a sharded sequence: each rank scores its shard and
   keeps its own top-kb (value, global position) pairs; one all-gather of those pairs lets
   every rank pick the same global top-kb (value descending, lower position first on
@@ -44,19 +46,80 @@ def merge_partials(m_all, l_all, o_all, out_dtype=torch.bfloat16):
     return _ops.lse_combine(m_all, l_all, o_all, out_dtype).unsqueeze(2)
 
 
+class PeerExchange:
+    """Split-KV across the ranks of `group` over NVLink peer memory, for a fixed (B, Hq, D).
+
+    ``decode(q, k_shard, v_shard, scaling)`` is the whole step in two launches: the dense
+    split pass over this rank's shard, then one kernel that merges its splits, stores the
+    merged (max, sum, numerator) into every rank's buffer, raises a per-step flag on each,
+    waits (bounded) for all ranks and writes the log-sum-exp combine
+    (``bd_split_kv_decode_peer``). ``__call__(m, l, o)`` runs the exchange kernel alone on
+    partials the caller computed (``bd_peer_exchange_combine``). The buffers are one
+    symmetric allocation (``torch.distributed._symmetric_memory``) mapped on every GPU of the
+    group; building the object is collective. Every rank must make the same calls, one per
+    step, on the current stream; the step counters live in the buffer, so the calls can be
+    captured in a CUDA graph. Raises if symmetric memory is unavailable (use the NCCL
+    all-gather of ``split_kv_decode`` then).
+    """
+
+    def __init__(self, B, Hq, D, device, group=None):
+        import ctypes
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import _native as N
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.B, self.Hq, self.D = B, Hq, D
+        f = N.lib().bd_peer_exchange_buffer_bytes
+        f.restype = ctypes.c_size_t
+        f.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        nbytes = int(f(B * Hq, D, self.world))
+        if nbytes == 0:
+            raise ValueError("peer exchange needs a non-empty problem")
+        self.buf = symm_mem.empty(nbytes // 4, dtype=torch.float32, device=device)
+        self.buf.zero_()
+        grp = group if group is not None else dist.group.WORLD
+        self.hdl = symm_mem.rendezvous(self.buf, grp)
+        self.peers_dev = int(self.hdl.buffer_ptrs_dev)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's buffer is zero before any rank writes
+
+    def _check(self, B, Hq, D):
+        if (B, Hq, D) != (self.B, self.Hq, self.D):
+            raise ValueError(f"PeerExchange built for {(self.B, self.Hq, self.D)}, called with {(B, Hq, D)}")
+
+    def __call__(self, m, l, o, out_dtype=torch.bfloat16):
+        """m, l [B, Hq], o [B, Hq, D] fp32 (this rank's shard) -> [B, Hq, D] combined."""
+        self._check(*o.shape)
+        return _ops.peer_exchange_combine(m, l, o, self.peers_dev, self.rank, self.world, out_dtype)
+
+    def decode(self, q, k_shard, v_shard, scaling, out_dtype=torch.bfloat16):
+        """q [B, Hq, 1, D] or [B, Hq, D]; k, v [B, Hk, S_r, D] this rank's shard -> [B, Hq, D]."""
+        q3 = q[:, :, 0, :] if q.dim() == 4 else q
+        self._check(*q3.shape)
+        return _ops.split_kv_decode_peer(q3, k_shard, v_shard, scaling, self.peers_dev, self.rank, self.world,
+                                         out_dtype)
+
+
 def split_kv_decode(q, k_shard, v_shard, scaling, group=None, partial_fn=None, merge_fn=None,
-                    out_dtype=torch.bfloat16):
+                    out_dtype=torch.bfloat16, exchange=None):
     """Attention of q over a sequence sharded along its tokens across the ranks of `group`.
 
     Every rank passes its own contiguous token shard; every rank returns the full output
-    [B,Hq,1,D]. One all-gather of the partials is the only communication.
+    [B,Hq,1,D]. One all-gather of the partials is the only communication: NCCL, or, with
+    ``exchange`` (a PeerExchange for these shapes), NVLink peer stores fused with the split
+    merge and the combine in one kernel behind the split pass.
     `partial_fn` / `merge_fn` default to the CUDA kernels; they are parameters so the
     host-side exchange can be exercised on CPU ranks.
     """
     import torch.distributed as dist
+    if exchange is not None and partial_fn is None:
+        return exchange.decode(q, k_shard, v_shard, scaling, out_dtype).unsqueeze(2)
     partial_fn = partial_fn or split_kv_partials
     merge_fn = merge_fn or merge_partials
     m, l, o = partial_fn(q, k_shard, v_shard, scaling)
+    if exchange is not None:
+        return exchange(m, l, o, out_dtype).unsqueeze(2)
     world = dist.get_world_size(group)
     B, Hq, D = o.shape
     packed = torch.cat([m.reshape(-1), l.reshape(-1), o.reshape(-1)]).contiguous()

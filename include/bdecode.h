@@ -111,6 +111,36 @@ int bd_decode_attn_partial(const bd_tensor* q, const bd_tensor* k, const bd_tens
 int bd_lse_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o,
                    const bd_tensor* out, bd_stream_t stream);
 
+/* Split-KV across GPUs over NVLink peer memory. Each rank holds a contiguous token shard
+ * k,v [B,Hk,S_r,D] of one sequence batch; every rank ends with the attention output over
+ * all shards. `peer_buffers` is a DEVICE array of `world` pointers, entry r the base of
+ * rank r's exchange buffer as this GPU addresses it (a symmetric allocation:
+ * torch.distributed._symmetric_memory, or cuMem handles mapped on every GPU), each
+ * bd_peer_exchange_buffer_bytes(B*Hq, D, world) bytes and zeroed once before the first call
+ * (it holds the per-row step counters, so it must not be cleared between steps). Every rank
+ * calls with the same shapes, one call per step, on one stream; calls may be captured in a
+ * CUDA graph and replayed. One kernel (at most one CTA per SM, each over rows b*Hq + hq)
+ * merges this rank's split partials per row, stores the merged (max, sum, numerator) into
+ * every rank's buffer, raises a per-step flag on each, waits (at most 1 s; then the rows of
+ * that CTA are NaN and bd_wait_timeouts() counts it) for all ranks' flags and writes the
+ * log-sum-exp combine.
+ *   bd_split_kv_decode_peer: the whole step -- the dense split pass over this rank's shard
+ *     (q [B,Hq,D], k,v bf16 or fp8 e4m3 as bd_decode_attn; workspace of
+ *     bd_decode_attn_workspace(q, k) bytes) and the exchange kernel, launched as its
+ *     programmatic dependent (two launches, no separate merge kernel).
+ *   bd_peer_exchange_combine: the exchange of partials the caller computed (m, l [B,Hq],
+ *     o [B,Hq,D] f32, as bd_decode_attn_partial returns them).
+ * out [B,Hq,D] bf16/f16/f32. Needs D a multiple of 4, at most 512; world <= 64.
+ * ref: no single counterpart -- the reference is single-GPU; this is split-KV decode across
+ *      GPUs (the merge identity of src/attention_kernels.py:45-59 applied to shards). */
+size_t bd_peer_exchange_buffer_bytes(int rows, int D, int world);
+int bd_split_kv_decode_peer(const bd_tensor* q, const bd_tensor* k, const bd_tensor* v, float scaling,
+                            void* const* peer_buffers, int rank, int world, const bd_tensor* out,
+                            void* workspace, size_t workspace_bytes, bd_stream_t stream);
+int bd_peer_exchange_combine(const bd_tensor* m, const bd_tensor* l, const bd_tensor* o,
+                             void* const* peer_buffers, int rank, int world, const bd_tensor* out,
+                             bd_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * KIVI 2/4-bit KV-cache decode: a packed-cache split-KV kernel, then a bf16
  * residual-window kernel that (when the window takes one CTA per head group) also
