@@ -127,6 +127,52 @@ def test_topk_short_rows(cuda, n):
         assert torch.equal(i.cpu(), ri.sort(-1).values)
 
 
+@pytest.mark.parametrize("n", [4100, 8192, 32768])
+def test_topk_unsorted_long_rows(cuda, n):
+    """Unsorted selection of rows past the short-row kernel (the streaming kernel): heavy
+    ties, all-equal rows, signed zeros, infinities, candidate-list overflow, a sample that
+    misleads the bracket, sorted rows, k = n - 1 and n; indices in ascending order, values
+    read back from the scores."""
+    from bytes_b200 import _ops
+    g = gen(n)
+    s = torch.randint(-30, 30, (12, n), generator=g).float()
+    s[0] = 2.5
+    s[1, ::2] = -0.0
+    s[1, 1::2] = 0.0
+    s[2] = torch.randn(n, generator=g)
+    s[2, 100:200] = float("inf")
+    s[3] = float("-inf")
+    s[3, n // 2:] = -1.0
+    s[4] = torch.randn(n, generator=g) * 1e-30
+    s[5] = torch.randint(0, 2, (n,), generator=g).float()  # two values: a threshold digit of ~n/2 keys
+    s[6] = torch.randn(n, generator=g) + 100.0
+    s[6, ::16] = 0.0  # every sampled position is small: the sample's bracket misses, radix fallback
+    s[7] = torch.randn(n, generator=g)
+    s[7, ::16] += 1000.0  # only the sampled positions are large
+    s[8] = torch.arange(n).float()  # ascending
+    s[9] = -torch.arange(n).float()  # descending
+    dev = s.to(cuda)
+    for k in sorted({1, 5, 1000, 2047, 2048, 2049, n // 2, n - 1, n}):
+        v, i = _ops.topk(dev, k, sorted=False, want_values=True, idx_dtype=torch.int64)
+        _, ri = oracle.topk_lower_index(s, k)
+        assert torch.equal(i.cpu(), ri.sort(-1).values), k
+        assert torch.equal(v.cpu(), torch.gather(s, -1, i.cpu())), k
+        _, i32 = _ops.topk(dev, k, sorted=False, want_values=False, idx_dtype=torch.int32)
+        assert torch.equal(i32.cpu().long(), i.cpu())
+
+
+def test_topk_unsorted_strided_rows(cuda):
+    """Rows of a [B, H, n] view whose rows sit 8200 floats apart (16-byte aligned)."""
+    from bytes_b200 import _ops
+    g = gen(99)
+    big = torch.randn(2, 8, 8200, generator=g)
+    view = big.to(cuda)[..., :8192]
+    assert view.stride(1) == 8200
+    _, i = _ops.topk(view, 300, sorted=False, want_values=False, idx_dtype=torch.int64)
+    _, ri = oracle.topk_lower_index(big[..., :8192].contiguous(), 300)
+    assert torch.equal(i.cpu(), ri.sort(-1).values)
+
+
 def test_topk_3d_rows(cuda):
     g = gen(3)
     s = torch.randn(2, 8, 3000, generator=g)
