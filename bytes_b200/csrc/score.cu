@@ -24,6 +24,12 @@ namespace {
 
 constexpr int kSW = 4;         // warps per CTA
 constexpr int kSStages = 3;
+// packed keys (2/4 bits): the per-token unpack -> MMA chain needs more warps in flight than
+// the bf16/fp8 forms, so their tiles double-buffer and more CTAs share an SM (four at 2 bits;
+// three at 4 bits, whose 57 KB of double-buffered tiles allow no fourth)
+__host__ __device__ constexpr bool packed_kt(int kt) { return kt == 2 || kt == 4; }
+__host__ __device__ constexpr int score_stages(int kt) { return packed_kt(kt) ? 2 : kSStages; }
+__host__ __device__ constexpr int score_ctas_per_sm(int kt) { return kt == 2 ? 4 : (kt == 4 ? 3 : 2); }
 constexpr float kSub = 16777216.f;
 
 // KT: 16 = bf16 keys, 8 = fp8 keys, 4 / 2 = packed bits
@@ -62,11 +68,35 @@ __device__ __forceinline__ float load_qs(const ScoreParams& p, int64_t off) {
 __device__ __forceinline__ float h16_to_f(uint16_t u, int is_bf16) {
   return is_bf16 ? __uint_as_float(uint32_t(u) << 16) : __half2float(__ushort_as_half(u));
 }
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+// N consecutive 16-bit floats (bf16 or f16) from shared memory, one vector load (2N bytes,
+// 2N-byte aligned), widened to fp32
+template <int N>
+__device__ __forceinline__ void load_row16(const uint16_t* src, int is_bf16, float* out) {
+  uint32_t w[(N + 1) / 2];
+  if constexpr (N == 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (N == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(src);
+    w[0] = v.x; w[1] = v.y;
+  } else if constexpr (N == 2) {
+    w[0] = *reinterpret_cast<const uint32_t*>(src);
+  } else {
+    w[0] = *src;
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const uint32_t h = (w[i >> 1] >> (16 * (i & 1))) & 0xffffu;
+    out[i] = h16_to_f(uint16_t(h), is_bf16);
+  }
+}
 
 // GS: group size of packed keys (compile-time, so every per-group accumulator index is
 // static and the accumulators stay in registers); 0 for bf16 / fp8 keys.
 template <int KT, int D, int NT, int GS>
-__global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p) {
+__global__ void __launch_bounds__(kSW * 32, score_ctas_per_sm(KT)) score_kernel(const ScoreParams p) {
   griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
   griddep_launch_dependents();
   using L = SL<KT, D>;
@@ -157,9 +187,22 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
 #pragma unroll
           for (int kk = 0; kk < KSTEPS; ++kk)
             if (kk / kpg == gi) v += part[kk][nt];
-          qsum[gi][nt][0] = __shfl_sync(0xffffffffu, v, (2 * tq) * 4);
-          qsum[gi][nt][1] = __shfl_sync(0xffffffffu, v, (2 * tq + 1) * 4);
+          // 2^-24: the epilogue applies the subnormal codes' 2^24 to the whole score
+          qsum[gi][nt][0] = __shfl_sync(0xffffffffu, v, (2 * tq) * 4) * (1.f / kSub);
+          qsum[gi][nt][1] = __shfl_sync(0xffffffffu, v, (2 * tq + 1) * 4) * (1.f / kSub);
         }
+      score_mul *= kSub;
+      if (KT == 2) {
+        // the operand registers of k-slots 2tq+8, 2tq+9 keep their codes 8 bits up (an exact
+        // subnormal 2^8 larger, one mask instead of a shift and a mask): their query halves
+        // are scaled by 2^-8 to match
+        const __half2 sc8 = __float2half2_rn(1.f / 256.f);
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            qb[kk][nt][1] = h2_bits(__hmul2(bits_h2(qb[kk][nt][1]), sc8));
+      }
     }
   }
 
@@ -194,21 +237,22 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
     }
   };
 
+  constexpr int NST = score_stages(KT);
 #pragma unroll
-  for (int s = 0; s < kSStages - 1; ++s) {
+  for (int s = 0; s < NST - 1; ++s) {
     if (s < ntiles) load_tile(s, s);
     cp_async_commit();
   }
 
   for (int it = 0; it < ntiles; ++it) {
-    cp_async_wait<kSStages - 2>();
+    cp_async_wait<NST - 2>();
     __syncthreads();
     {
-      const int nxt = it + kSStages - 1;
-      if (nxt < ntiles) load_tile(nxt, nxt % kSStages);
+      const int nxt = it + NST - 1;
+      if (nxt < ntiles) load_tile(nxt, nxt % NST);
       cp_async_commit();
     }
-    const uint8_t* st = smem + (it % kSStages) * L::STAGE;
+    const uint8_t* st = smem + (it % NST) * L::STAGE;
     const uint32_t ks = smem_u32(st);
     const uint16_t* ssc = reinterpret_cast<const uint16_t*>(st + L::KBYTES);
     const uint16_t* szr = reinterpret_cast<const uint16_t*>(st + L::KBYTES + L::SZB);
@@ -263,10 +307,11 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
         for (int kk = 0; kk < KSTEPS; ++kk) {
           uint32_t a0, a1, a2, a3;
           if (KT == 2) {
-            a0 = (wa[kk] >> (2 * tq)) & 0x00030003u;
-            a1 = (wb[kk] >> (2 * tq)) & 0x00030003u;
-            a2 = (wa[kk] >> (2 * tq + 8)) & 0x00030003u;
-            a3 = (wb[kk] >> (2 * tq + 8)) & 0x00030003u;
+            const uint32_t xa = wa[kk] >> (2 * tq), xb = wb[kk] >> (2 * tq);
+            a0 = xa & 0x00030003u;
+            a1 = xb & 0x00030003u;
+            a2 = xa & 0x03000300u;  // code * 2^(8-24): see the query halves' 2^-8
+            a3 = xb & 0x03000300u;
           } else {
             a0 = (wa[2 * kk] >> (4 * tq)) & 0x000F000Fu;
             a1 = (wb[2 * kk] >> (4 * tq)) & 0x000F000Fu;
@@ -291,22 +336,22 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
       } else {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) res[nt][0] = res[nt][1] = res[nt][2] = res[nt][3] = 0.f;
+        // this token's NGMAX scales (zeros) are one 2*NGMAX-byte row of the tile
+        const int la = r0 + g, lb = r0 + g + 8;  // tile-local rows (zero-filled past the end)
+        float sa[NGMAX], za[NGMAX], sb[NGMAX], zb[NGMAX];
+        load_row16<NGMAX>(ssc + la * NGMAX, p.sz_bf16, sa);
+        load_row16<NGMAX>(szr + la * NGMAX, p.sz_bf16, za);
+        load_row16<NGMAX>(ssc + lb * NGMAX, p.sz_bf16, sb);
+        load_row16<NGMAX>(szr + lb * NGMAX, p.sz_bf16, zb);
 #pragma unroll
-        for (int gi = 0; gi < NGMAX; ++gi) {
-          if (gi >= ngroups) break;
-          const int la = r0 + g, lb = r0 + g + 8;  // tile-local rows (zero-filled past the end)
-          const float sa = h16_to_f(ssc[la * ngroups + gi], p.sz_bf16);
-          const float za = h16_to_f(szr[la * ngroups + gi], p.sz_bf16);
-          const float sb = h16_to_f(ssc[lb * ngroups + gi], p.sz_bf16);
-          const float zb = h16_to_f(szr[lb * ngroups + gi], p.sz_bf16);
+        for (int gi = 0; gi < NGMAX; ++gi)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-              res[nt][j] += fmaf(acc[gi][nt][j] * kSub, sa, qsum[gi][nt][j] * za);
-              res[nt][2 + j] += fmaf(acc[gi][nt][2 + j] * kSub, sb, qsum[gi][nt][j] * zb);
+              res[nt][j] = fmaf(qsum[gi][nt][j], za[gi], fmaf(acc[gi][nt][j], sa[gi], res[nt][j]));
+              res[nt][2 + j] = fmaf(qsum[gi][nt][j], zb[gi], fmaf(acc[gi][nt][2 + j], sb[gi], res[nt][2 + j]));
             }
-        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -329,7 +374,7 @@ __global__ void __launch_bounds__(kSW * 32, 2) score_kernel(const ScoreParams p)
 template <int KT, int D, int NT, int GS>
 int launch_score(const ScoreParams& p, int n_splits, cudaStream_t st) {
   using L = SL<KT, D>;
-  const size_t smem = size_t(kSStages) * L::STAGE;
+  const size_t smem = size_t(score_stages(KT)) * L::STAGE;
   auto kern = score_kernel<KT, D, NT, GS>;
   static bool attr[64] = {false};
   int dev = 0;
@@ -474,7 +519,7 @@ int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* sca
   const int64_t tt = tile_tokens(kt);
   const int64_t ntiles = (S + tt - 1) / tt;
   const int64_t pairs = B * Hk * p.head_chunks;
-  const int64_t slots = 2LL * num_sms();
+  const int64_t slots = int64_t(score_ctas_per_sm(kt)) * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / pairs;
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, ntiles));
   const int64_t tps = (ntiles + splits - 1) / splits;
