@@ -163,14 +163,10 @@ __global__ void __launch_bounds__(kPW * 32, 2)
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kPRows - 1) / kPRows : 0;
 
   // ---- LUT of the chunk's heads -> smem: the regrouped [K][M][4] copy when there is one
-  // (one contiguous 64 KB block), else [M][K][4] from the caller's layout; rows of a head
-  // are read four entries at a time when they are contiguous and 16-byte aligned
-  if (p.lut_t) {
-    const float4* src = p.lut_t + ((int64_t(b) * p.Hk + hk) * p.head_chunks + chunk) * (256 * 16);
-    for (int i = threadIdx.x; i < 256 * 16; i += kPW * 32) cp_async16(smem_u32(lut_s) + i * 16, src + i, 16);
-    cp_async_commit();
-    cp_async_wait<0>();
-  } else {
+  // (one contiguous 64 KB block, copied after the first tiles are in flight, below), else
+  // [M][K][4] from the caller's layout; rows of a head are read four entries at a time when
+  // they are contiguous and 16-byte aligned
+  if (!p.lut_t) {
     const int MK = p.M * p.K;
     const bool vec = p.l_sk == 1 && p.l_sm == p.K && (p.K & 3) == 0 && (p.l_sh & 3) == 0 && (p.l_sb & 3) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.lut) & 15) == 0;
@@ -304,6 +300,15 @@ __global__ void __launch_bounds__(kPW * 32, 2)
   for (int s = 0; s < kPStages - 1; ++s) {
     if (s < ntiles) load_tile(s, s);
     cp_async_commit();
+  }
+  if (p.lut_t) {
+    // the regrouped LUT is written by the kernel this grid is a programmatic dependent of:
+    // the first tiles above are already in flight while it finishes
+    griddep_wait();
+    const float4* src = p.lut_t + ((int64_t(b) * p.Hk + hk) * p.head_chunks + chunk) * (256 * 16);
+    for (int i = threadIdx.x; i < 256 * 16; i += kPW * 32) cp_async16(smem_u32(lut_s) + i * 16, src + i, 16);
+    cp_async_commit();
+    cp_async_wait<0>();
   }
   __syncthreads();  // LUT visible
 
@@ -675,6 +680,9 @@ __global__ void pq_encode_kernel(const void* x, int x_dtype, int64_t x_sn, const
 // 256 threads (thread = code): reads are coalesced along the codes.
 __global__ void pq_lut_regroup_kernel(const float* __restrict__ lut, int64_t l_sb, int64_t l_sh, int64_t l_sm,
                                       int64_t l_sk, int Hk, int G, int head_chunks, float4* __restrict__ out) {
+  // the decode kernel queued behind may start launching: it waits for this grid only
+  // before it reads the regrouped LUT
+  griddep_launch_dependents();
   const int bc = blockIdx.x, j = blockIdx.y, code = threadIdx.x;
   const int chunk = bc % head_chunks, bh = bc / head_chunks;
   const int hk = bh % Hk, b = bh / Hk;
@@ -743,6 +751,8 @@ int launch_pq_as(const PqParams& p, const CUtensorMap* maps, cudaStream_t st) {
     attr[dev & 63] = true;
   }
   dim3 grid(p.n_splits, p.Hk * p.head_chunks, p.B);
+  if (p.lut_t)  // behind the LUT regroup: a programmatic dependent (it waits before reading the LUT)
+    return launch_pdl(kern, grid, dim3(kPW * 32), smem, st, "pq_decode_kernel launch", p, maps[0], maps[1], maps[2]);
   kern<<<grid, kPW * 32, smem, st>>>(p, maps[0], maps[1], maps[2]);
   return cuda_check(cudaGetLastError(), "pq_decode_kernel launch");
 }
