@@ -16,7 +16,9 @@ value      device time per decode step (us, max over ranks): a CUDA graph of exa
            steps (both graphs uploaded to the device before either runs); the steps rotate
            over 4 input sets (416 MB > 3x L2) so no step reads its inputs from L2.
 e2e        the same K steps through the public Python API with host buffers: every step
-           copies its queries host->device from pinned memory and reads the output back.
+           copies its queries host->device from pinned memory and reads the output back,
+           the copies on their own streams so they overlap neighbouring steps' kernels
+           (events order each step's upload -> decode -> read-back).
 roofline   the packed-cache kernel alone (no residual window), algorithmic bytes per launch
            / its CUDA-event time, against MEASURED_PEAKS.json's copy bandwidth.
 cpu_baseline / --impl reference: the reference's own CPU-runnable KIVI path
@@ -841,12 +843,31 @@ def main():
     out_host = [torch.empty(c["B"], c["Hq"], 1, c["D"], dtype=torch.bfloat16).pin_memory() for _ in sets]
     q_dev = [torch.empty_like(s[0]) for s in sets]
     st = torch.cuda.current_stream()
+    # a serving loop's overlap: the copies run on their own streams, so step i's query upload
+    # and step i-1's output read-back proceed while decode kernels run; per input slot j,
+    # events order upload -> decode -> read-back and keep a slot's buffers from being reused
+    # before its read-back is done
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_up = [torch.cuda.Event() for _ in sets]
+    ev_dec = [torch.cuda.Event() for _ in sets]
+    ev_down = [torch.cuda.Event() for _ in sets]
+    for e in ev_down:
+        e.record(st)
 
     def e2e_step(i):
         j = i % NBUF
-        q_dev[j].copy_(q_host[j], non_blocking=True)
+        with torch.cuda.stream(up):
+            up.wait_event(ev_down[j])
+            q_dev[j].copy_(q_host[j], non_blocking=True)
+            ev_up[j].record(up)
+        st.wait_event(ev_up[j])
         o = kv.kivi_decode_attn(q_dev[j], *sets[j][1:], c["bits"], c["group"])
-        out_host[j].copy_(o, non_blocking=True)
+        o.record_stream(down)  # the allocator keeps it until its read-back is done
+        ev_dec[j].record(st)
+        with torch.cuda.stream(down):
+            down.wait_event(ev_dec[j])
+            out_host[j].copy_(o, non_blocking=True)
+            ev_down[j].record(down)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -855,8 +876,11 @@ def main():
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
+    up.wait_event(e0)
     for i in range(args.steps):
         e2e_step(i)
+    for j in range(NBUF):  # every read-back of the timed steps is inside the timed region
+        st.wait_event(ev_down[j])
     e1.record(st)
     e1.synchronize()
     us_e2e = e0.elapsed_time(e1) * 1e3 / args.steps
