@@ -85,8 +85,13 @@ __device__ __forceinline__ void store_out(void* base, int dt, int64_t off, float
   }
 }
 
+// CTAs per SM the split plan fills: fp8 tiles take half the shared memory of bf16 ones,
+// and a third CTA hides more of each tile's convert -> MMA chain (32K, B = 8: 59.6 -> 58.0 us;
+// four measured 60.1)
+__host__ __device__ constexpr int dense_ctas_per_sm(bool fp8) { return fp8 ? 3 : 2; }
+
 template <int D, int NT, bool FP8>
-__global__ void __launch_bounds__(kWarps * 32, 2) dense_decode_kernel(const DenseParams p) {
+__global__ void __launch_bounds__(kWarps * 32, dense_ctas_per_sm(FP8)) dense_decode_kernel(const DenseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   // a programmatic dependent queued behind this grid (the combine) may start launching;
   // it waits for this grid before reading anything
@@ -612,7 +617,7 @@ int make_plan(const bd_tensor* q, const bd_tensor* k, Plan* pl, int target_ctas 
   pl->head_chunks = (G + pl->heads_per_chunk - 1) / pl->heads_per_chunk;
   const int64_t ntiles = (S + kRows - 1) / kRows;
   const int64_t pairs = B * Hk * pl->head_chunks;
-  const int64_t slots = target_ctas > 0 ? target_ctas : 2LL * num_sms();
+  const int64_t slots = target_ctas > 0 ? target_ctas : int64_t(dense_ctas_per_sm(pl->fp8)) * num_sms();
   int64_t splits = pairs >= slots ? 1 : slots / std::max<int64_t>(pairs, 1);
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, std::max<int64_t>(ntiles, 1)));
   int64_t tps = ntiles > 0 ? (ntiles + splits - 1) / splits : 1;
@@ -778,10 +783,10 @@ int launch_combine(const Partials& part, int B, int Hq, int D, const bd_tensor* 
 // the process exits. In host code the symbol is only a stand-in, so its device address
 // is looked up with cudaGetSymbolAddress on the calling device.
 //
-// Size: a plan that splits at all targets two CTAs per SM, so it holds at most
-// 2 x SMs CTAs x 16 heads of (D + 2) floats, D <= 128, plus 256 bytes of alignment slack:
-// 16,640 bytes per SM. 4 MiB therefore covers every plan on parts with up to 252 SMs
-// (B200: 148); a larger plan is rejected with BD_ERR_UNSUPPORTED before any launch.
+// Size: a plan that splits at all targets two CTAs per SM (three for fp8 caches), so it
+// holds at most 3 x SMs CTAs x 16 heads of (D + 2) floats, D <= 128, plus 256 bytes of
+// alignment slack: 24,960 bytes per SM. 4 MiB therefore covers every plan on parts with up
+// to 168 SMs (B200: 148); a larger plan is rejected with BD_ERR_UNSUPPORTED before any launch.
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 static std::mutex g_scratch_mu;

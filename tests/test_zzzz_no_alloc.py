@@ -59,13 +59,14 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
 
 
 def test_noalloc_scratch_covers_every_plan_on_this_device(cuda):
-    """The split plan targets two CTAs per SM, so a plan that splits at all needs at most
-    16 heads x 2 x SMs x (D+2) floats of scratch plus 256 bytes of alignment slack, i.e.
-    16,640 bytes per SM (about 2.5 MB on a 148-SM part): the 4 MiB static array holds every
-    such plan on parts with up to 252 SMs, this device included. (Larger plans are rejected
-    with BD_ERR_UNSUPPORTED before any launch; no device this test runs on reaches that.)"""
+    """The split plan targets two CTAs per SM (three for fp8 caches), so a plan that splits
+    at all needs at most 16 heads x 3 x SMs x (D+2) floats of scratch plus 256 bytes of
+    alignment slack, i.e. 24,960 bytes per SM (about 3.7 MB on a 148-SM part): the 4 MiB
+    static array holds every such plan on parts with up to 168 SMs, this device included.
+    (Larger plans are rejected with BD_ERR_UNSUPPORTED before any launch; no device this
+    test runs on reaches that.)"""
     sms = torch.cuda.get_device_properties(cuda).multi_processor_count
-    assert 16640 * sms + 256 <= 4 << 20
+    assert 24960 * sms + 256 <= 4 << 20
     lib = N.lib()
     f = lib.bd_decode_attn_workspace
     f.restype = ctypes.c_size_t
@@ -83,9 +84,9 @@ def test_noalloc_scratch_covers_every_plan_on_this_device(cuda):
     for B in (1, 2, 3, 8):
         for Hk in (1, 2, 4, 8):
             for G in (1, 4, 7, 8, 9, 16, 17, 32, 64, 128):
-                for D in (64, 128):
+                for D, kdt in ((64, N.BD_BF16), (128, N.BD_BF16), (64, N.BD_F8E4M3), (128, N.BD_F8E4M3)):
                     q = fake((B, Hk * G, D))
-                    k = fake((B, Hk, 1 << 20, D))
+                    k = fake((B, Hk, 1 << 20, D), kdt)
                     ws = f(ctypes.byref(q), ctypes.byref(k))
                     splits = (ws - 256) // (B * Hk * G * (D + 2) * 4)
                     if splits > 1:  # a one-split plan writes the output directly, no scratch
