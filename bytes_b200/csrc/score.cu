@@ -25,15 +25,15 @@ namespace {
 constexpr int kSW = 4;         // warps per CTA
 constexpr int kSStages = 3;
 // packed keys (2/4 bits): the per-token unpack -> MMA chain needs more warps in flight than
-// the bf16/fp8 forms, so their tiles double-buffer and more CTAs share an SM (four at 2 bits;
-// three at 4 bits, whose 57 KB of double-buffered tiles allow no fourth)
+// the bf16/fp8 forms, so their tiles double-buffer and four CTAs share an SM (at 4 bits and
+// group size 32, 48 KB of double-buffered tiles; smaller groups fit three)
 __host__ __device__ constexpr bool packed_kt(int kt) { return kt == 2 || kt == 4; }
 __host__ __device__ constexpr int score_stages(int kt) { return packed_kt(kt) ? 2 : kSStages; }
-__host__ __device__ constexpr int score_ctas_per_sm(int kt) { return kt == 2 ? 4 : (kt == 4 ? 3 : 2); }
+__host__ __device__ constexpr int score_ctas_per_sm(int kt) { return packed_kt(kt) ? 4 : 2; }
 constexpr float kSub = 16777216.f;
 
-// KT: 16 = bf16 keys, 8 = fp8 keys, 4 / 2 = packed bits
-template <int KT, int D>
+// KT: 16 = bf16 keys, 8 = fp8 keys, 4 / 2 = packed bits; GS: group size of packed keys
+template <int KT, int D, int GS>
 struct SL {
   static constexpr int RB = KT == 16 ? 1 : (KT == 8 ? 2 : 4);  // 16-token row blocks per warp per tile
   static constexpr int TILE = 16 * kSW * RB;
@@ -41,7 +41,7 @@ struct SL {
   // packed rows are read by 8 lanes at a time with 16-byte loads: pitches chosen conflict-free
   static constexpr int PITCH = (KT == 16 || KT == 8) ? ROWB + 16 : (ROWB == 16 ? 16 : (ROWB == 32 ? 48 : 80));
   static constexpr int KBYTES = TILE * PITCH;
-  static constexpr int SZB = (KT == 16 || KT == 8) ? 0 : TILE * (D / 16) * 2;  // scale tile, worst case gs=16
+  static constexpr int SZB = (KT == 16 || KT == 8) ? 0 : TILE * (D / GS) * 2;  // scale (zero) tile: D/GS f16 per token
   static constexpr int STAGE = KBYTES + 2 * SZB;
 };
 
@@ -99,7 +99,7 @@ template <int KT, int D, int NT, int GS>
 __global__ void __launch_bounds__(kSW * 32, score_ctas_per_sm(KT)) score_kernel(const ScoreParams p) {
   griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
   griddep_launch_dependents();
-  using L = SL<KT, D>;
+  using L = SL<KT, D, GS>;
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int KSTEPS = D / 16;
   constexpr int NGMAX = GS > 0 ? D / GS : 1;  // groups per token row
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kSW * 32, score_ctas_per_sm(KT)) score_kernel(
 
 template <int KT, int D, int NT, int GS>
 int launch_score(const ScoreParams& p, int n_splits, cudaStream_t st) {
-  using L = SL<KT, D>;
+  using L = SL<KT, D, GS>;
   const size_t smem = size_t(score_stages(KT)) * L::STAGE;
   auto kern = score_kernel<KT, D, NT, GS>;
   static bool attr[64] = {false};
