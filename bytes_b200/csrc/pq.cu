@@ -543,10 +543,12 @@ __global__ void __launch_bounds__(kPW * 32, 2)
             a[2 * u] = e4m3x2_to_f16x2(prmt(xs[u], 0, 0x0020));
             a[2 * u + 1] = e4m3x2_to_f16x2(prmt(xs[u], 0, 0x0031));
           } else {
-            // int8 -> f16 halves 0x64XX, XX = x ^ 0x80: the value 1024 + x + 128 (one
-            // byte-select PRMT and one XOR per register); the 1152 comes off through oc
-            a[2 * u] = prmt(xs[u], 0x64646464u, 0x4240) ^ 0x00800080u;
-            a[2 * u + 1] = prmt(xs[u], 0x64646464u, 0x4341) ^ 0x00800080u;
+            // int8 -> f16 halves 0x64XX, XX = x ^ 0x80: the value 1024 + x + 128 (the four
+            // sign bits flipped once per word, then one byte-select PRMT per register); the
+            // 1152 comes off through oc
+            const uint32_t xo = xs[u] ^ 0x80808080u;
+            a[2 * u] = prmt(xo, 0x64646464u, 0x4240);
+            a[2 * u + 1] = prmt(xo, 0x64646464u, 0x4341);
           }
         }
         mma_f16(o[2 * m2], a[0], a[1], a[2], a[3], pb0, pb1);
