@@ -553,8 +553,81 @@ def path_c4(dev, peak, g):
     return c4_batch_shard(dev, peak, g)
 
 
+def path_ref_gpu(dev, peak, g):
+    """The reference's own Triton kernels (the installed reference in baseline/_ref,
+    unmodified) on this GPU beside this engine's kernels, on the same inputs: dense bf16 /
+    fp8 decode at 32K (B=8, 28/4) and c0, the fp8 / int4 / int2 score passes and the gather
+    at config 3's shape (B=16, 32/8, S=32768, k = 5 %), PQ-LUT decode with bf16 values at
+    config 2's shape. Each op is CUDA-graph replayed after a warm-up call (the reference's
+    own harness times ops the same way); `max_abs_diff` compares the two outputs."""
+    if not os.path.isdir(os.path.join(REF_DIR, "src")):
+        return {"ref_gpu": {"unavailable": "the reference is not installed in baseline/_ref"}}
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import src.attention_kernels as ref
+    from bytes_b200 import attention_kernels as ak
+
+    def timed(fn, reps=10):
+        fn()
+        torch.cuda.synchronize()
+        gr = graph_of([fn])
+        time_graph(gr, 2)
+        return round(time_graph(gr, reps) / reps, 2)
+
+    def both(name, f_ref, f_ours):
+        a, b = f_ref(), f_ours()
+        torch.cuda.synchronize()
+        d = (a.float() - b.float()).abs().max().item()
+        out[name] = {"ref_us": timed(f_ref), "ours_us": timed(f_ours), "max_abs_diff": d}
+        out[name]["speedup"] = round(out[name]["ref_us"] / out[name]["ours_us"], 2)
+
+    out = {}
+    D = 128
+    q = torch.randn(8, 28, 1, D, device=dev, generator=g).bfloat16()
+    k = torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16()
+    v = torch.randn(8, 4, 32768, D, device=dev, generator=g).bfloat16()
+    qs = (q.float() / math.sqrt(D)).bfloat16()
+    both("bf16_decode_32k_B8", lambda: ref.decode_attn_bf16(qs, k, v), lambda: ak.decode_attn_bf16(qs, k, v))
+    k8, v8 = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
+    both("fp8_decode_32k_B8", lambda: ref.decode_attn_fp8(qs, k8, v8), lambda: ak.decode_attn_fp8(qs, k8, v8))
+    del k, v, k8, v8
+    q0 = (torch.randn(1, 28, 1, D, device=dev, generator=g) / math.sqrt(D)).bfloat16()
+    k0 = torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16()
+    v0 = torch.randn(1, 4, 8192, D, device=dev, generator=g).bfloat16()
+    both("c0_bf16_decode", lambda: ref.decode_attn_bf16(q0, k0, v0), lambda: ak.decode_attn_bf16(q0, k0, v0))
+    torch.cuda.empty_cache()
+    B, Hq, Hk, S = 16, 32, 8, 32768
+    sc = 1 / math.sqrt(D)
+    q3 = torch.randn(B, Hq, 1, D, device=dev, generator=g).bfloat16()
+    k3 = torch.randn(B, Hk, S, D, device=dev, generator=g).bfloat16()
+    v3 = torch.randn(B, Hk, S, D, device=dev, generator=g).bfloat16()
+    k38 = k3.to(torch.float8_e4m3fn)
+    both("c3_score_fp8", lambda: ref.sparse_score_scalar(q3, k38, sc, score_bits=8),
+         lambda: ak.sparse_score_scalar(q3, k38, sc, score_bits=8))
+    del k38
+    for bits in (4, 2):
+        kp, s_, z_ = ak.quantize_and_pack_score_keys(k3, bits, 32)
+        both(f"c3_score_int{bits}", lambda: ref.sparse_score_packed(q3, kp, s_, z_, sc, score_bits=bits, group_size=32),
+             lambda: ak.sparse_score_packed(q3, kp, s_, z_, sc, score_bits=bits, group_size=32))
+        del kp, s_, z_
+    kb = max(1, int(round(0.05 * S)))
+    scores = ak.sparse_score_scalar(q3, k3, sc, score_bits=16)
+    _, idx = ak.topk(scores, kb, sorted=False)
+    del scores
+    both("c3_gather_k5pct", lambda: ref.sparse_gather_attn(q3, k3, v3, idx, sc),
+         lambda: ak.sparse_gather_attn(q3, k3, v3, idx, sc))
+    del q3, k3, v3, idx
+    torch.cuda.empty_cache()
+    lut = torch.randn(4, 32, 16, 256, device=dev, generator=g) * 0.3
+    codes = torch.randint(0, 256, (4, 8, 32768, 16), device=dev, generator=g, dtype=torch.int32).to(torch.uint8)
+    vp = torch.randn(4, 8, 32768, D, device=dev, generator=g).bfloat16()
+    both("c2_pq_lut_bf16v", lambda: ref.decode_attn_pq_lut(lut, codes, vp), lambda: ak.decode_attn_pq_lut(lut, codes, vp))
+    return {"ref_gpu": out}
+
+
 PATHS = {"c0": path_c0, "c1": path_c1, "bf16_32k": path_bf16_32k, "c2": path_c2, "c3": path_c3,
-         "sparse_published": path_sparse_published, "topk": path_topk, "c4": path_c4}
+         "sparse_published": path_sparse_published, "topk": path_topk, "c4": path_c4, "ref_gpu": path_ref_gpu}
+OPT_IN = {"ref_gpu"}  # run only when asked for by --path (it JIT-compiles the reference's Triton kernels)
 
 
 def extras(dev, peak, only=None):
@@ -563,7 +636,7 @@ def extras(dev, peak, only=None):
     out = {}
     g = torch.Generator(device=dev).manual_seed(7)
     for name, fn in PATHS.items():
-        if only is not None and name != only:
+        if (only is not None and name != only) or (only is None and name in OPT_IN):
             continue
         out.update(fn(dev, peak, g))
         gc.collect()
