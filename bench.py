@@ -558,8 +558,9 @@ def path_ref_gpu(dev, peak, g):
     unmodified) on this GPU beside this engine's kernels, on the same inputs: dense bf16 /
     fp8 decode at 32K (B=8, 28/4) and c0, the fp8 / int4 / int2 score passes and the gather
     at config 3's shape (B=16, 32/8, S=32768, k = 5 %), PQ-LUT decode with bf16 values at
-    config 2's shape. Each op is CUDA-graph replayed after a warm-up call (the reference's
-    own harness times ops the same way); `max_abs_diff` compares the two outputs."""
+    config 2's shape, and the two-pass sparse decode (fp8 / int2 scores, k = 5 %) as whole
+    chains. Each op is CUDA-graph replayed after a warm-up call (the reference's own harness
+    times ops the same way); `max_abs_diff` compares the two outputs."""
     if not os.path.isdir(os.path.join(REF_DIR, "src")):
         return {"ref_gpu": {"unavailable": "the reference is not installed in baseline/_ref"}}
     if REF_DIR not in sys.path:
@@ -610,6 +611,17 @@ def path_ref_gpu(dev, peak, g):
         both(f"c3_score_int{bits}", lambda: ref.sparse_score_packed(q3, kp, s_, z_, sc, score_bits=bits, group_size=32),
              lambda: ak.sparse_score_packed(q3, kp, s_, z_, sc, score_bits=bits, group_size=32))
         del kp, s_, z_
+    # the two-pass sparse decode at k = 5 % (scores -> top-k -> gather), whole chain
+    k38 = k3.to(torch.float8_e4m3fn)
+    both("c3_sparse_decode_fp8_k5pct",
+         lambda: ref.sparse_decode_scalar(q3, k38, None, None, k3, v3, 0.05, sc, score_bits=8),
+         lambda: ak.sparse_decode_scalar(q3, k38, None, None, k3, v3, 0.05, sc, score_bits=8))
+    del k38
+    kp, s_, z_ = ak.quantize_and_pack_score_keys(k3, 2, 32)
+    both("c3_sparse_decode_int2_k5pct",
+         lambda: ref.sparse_decode_scalar(q3, kp, s_, z_, k3, v3, 0.05, sc, score_bits=2, group_size=32),
+         lambda: ak.sparse_decode_scalar(q3, kp, s_, z_, k3, v3, 0.05, sc, score_bits=2, group_size=32))
+    del kp, s_, z_
     kb = max(1, int(round(0.05 * S)))
     scores = ak.sparse_score_scalar(q3, k3, sc, score_bits=16)
     _, idx = ak.topk(scores, kb, sorted=False)
