@@ -5,7 +5,11 @@
 //   xmin, xmax over the group axis; scale = clamp(xmax - xmin, 1e-8) / (levels - 1)
 //   q = clamp(round_half_even((x - xmin) / scale), 0, levels - 1); y = q * scale + xmin
 // Every step rounds like the reference's tensor ops in the input dtype (fp32, or bf16 /
-// f16 after each op), with no fused multiply-add, so outputs are bit-identical.
+// f16 after each op), with no fused multiply-add, so outputs are bit-identical to the
+// reference run on a CUDA device. There PyTorch divides a tensor by a Python number as a
+// multiplication by the number's fp32 reciprocal (formed on the host; for bf16 / f16 the
+// product is taken in fp32 and rounded), so the scale is range * fp32(1/(levels-1)); the
+// CPU run of the same expression divides and differs in the last bit of some scales.
 #include "common.cuh"
 
 namespace bd {
@@ -21,6 +25,7 @@ struct FqParams {
   int64_t n[5];                  // sizes
   void* y;                       // contiguous output, same logical shape
   int levels;
+  float rcp;                     // fp32 1/(levels-1), formed on the host
 };
 
 template <typename T>
@@ -42,7 +47,7 @@ __global__ void fakequant_kernel(const FqParams p) {
     hi = fmaxf(hi, v);
   }
   const float L = float(p.levels - 1);
-  const float sc = rnd<T>(__fdiv_rn(rnd<T>(fmaxf(rnd<T>(__fsub_rn(hi, lo)), rnd<T>(1e-8f))), L));
+  const float sc = rnd<T>(__fmul_rn(rnd<T>(fmaxf(rnd<T>(__fsub_rn(hi, lo)), rnd<T>(1e-8f))), p.rcp));
   for (int64_t e = 0; e < gl; ++e) {
     const float v = to_f32<T>(x[e * p.s[3]]);
     float q = rintf(rnd<T>(__fdiv_rn(rnd<T>(__fsub_rn(v, lo)), sc)));
@@ -71,6 +76,7 @@ int bd_asym_fakequant(const bd_tensor* x, int levels, const bd_tensor* y, bd_str
   }
   FqParams p{};
   p.x = x->data; p.y = y->data; p.levels = levels;
+  p.rcp = 1.0f / float(levels - 1);
   for (int i = 0; i < 5; ++i) { p.s[i] = x->stride[i]; p.n[i] = x->shape[i]; }
   const int64_t ncol = p.n[0] * p.n[1] * p.n[2] * p.n[4];
   if (ncol == 0 || p.n[3] == 0) return BD_OK;

@@ -941,7 +941,9 @@ __global__ void kivi_pack_kernel(const T* __restrict__ x, int nlead, int64_t l0,
 #pragma unroll
   for (int e = 1; e < 32; ++e) { lo = fminf(lo, v[e]); hi = fmaxf(hi, v[e]); }
   constexpr int LV = (1 << BITS) - 1;
-  const float sc = __fdiv_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), float(LV));
+  // (max-min)/(2^bits-1) as PyTorch forms it on a CUDA device: times the fp32 reciprocal
+  constexpr float kRcp = 1.0f / float(LV);
+  const float sc = __fmul_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), kRcp);
   constexpr int FPI = 32 / BITS;
   uint32_t words[32 / FPI];
 #pragma unroll
@@ -961,8 +963,8 @@ __global__ void kivi_pack_kernel(const T* __restrict__ x, int nlead, int64_t l0,
 
 // ---------------------------------------------------------------- KIVI cache append
 // Quantizes whole 32-token groups of new keys/values into existing packed caches at a
-// token offset, with the packer's arithmetic (fp32 min/max, scale = max(max-min,1e-8) /
-// (2^bits-1), round-half-even, clamp): the caches then hold exactly what packing the whole
+// token offset, with the packer's arithmetic (fp32 min/max, scale = max(max-min,1e-8) times
+// the fp32 reciprocal of 2^bits-1, round-half-even, clamp): the caches then hold exactly what packing the whole
 // sequence at once would give. Keys are quantized per channel over the group's tokens
 // (one thread per (b, hk, channel, group); a warp reads 32 consecutive channels of each
 // token), values per token over 32-channel groups (one thread per (b, hk, token, group)).
@@ -996,7 +998,8 @@ __device__ __forceinline__ void quant32(const float* v, uint32_t* words, float* 
   for (int e = 1; e < 32; ++e) { lo = fminf(lo, v[e]); hi = fmaxf(hi, v[e]); }
   constexpr int LV = (1 << BITS) - 1;
   constexpr int FPI = 32 / BITS;
-  const float sc = __fdiv_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), float(LV));
+  constexpr float kRcp = 1.0f / float(LV);
+  const float sc = __fmul_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), kRcp);
 #pragma unroll
   for (int w = 0; w < 32 / FPI; ++w) words[w] = 0u;
 #pragma unroll

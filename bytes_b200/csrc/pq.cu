@@ -643,14 +643,36 @@ __global__ void pq_lut_kernel(const void* q, int q_dtype, int64_t q_sb, int64_t 
   lut[int64_t(bh) * M * K + i] = acc;
 }
 
-// codes[n, j] = argmin_c sum_i (x[n, j*dsub+i] - cent[j,c,i])^2, first index on ties
+// codes[n, j] = argmax_c (x_h . c_h - norm_c), first index on ties: the nearest-centroid rule
+// of ProductQuantizer.quantize on a CUDA device (src/quantization.py:160-199, kernel :8-60).
+// x_h = x rounded to f16; c_h = the fp32 centroid rounded to x's dtype, then to f16; the
+// products of f16 values are exact in fp32 and summed in fp32; norm_c = 0.5 * sum(c^2) in
+// fp32, rounded to x's dtype. argmax of that score is argmin of the squared distance up to
+// the f16 rounding of the operands.
+__device__ __forceinline__ float round_as(float v, int dt) {
+  if (dt == BD_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dt == BD_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
 __global__ void pq_encode_kernel(const void* x, int x_dtype, int64_t x_sn, const float* cent, int64_t c_sm,
                                  int64_t c_sk, int64_t c_sd, int64_t N, int M, int K, int dsub, void* codes,
                                  int codes64) {
-  extern __shared__ float cs[];  // [K][dsub] of subspace j
+  extern __shared__ float cs[];  // [K][dsub] f16-rounded centroids of subspace j, then [K] norms
+  float* norms = cs + K * dsub;
   const int j = blockIdx.y;
-  for (int i = threadIdx.x; i < K * dsub; i += blockDim.x)
-    cs[i] = cent[int64_t(j) * c_sm + int64_t(i / dsub) * c_sk + int64_t(i % dsub) * c_sd];
+  for (int i = threadIdx.x; i < K * dsub; i += blockDim.x) {
+    const float c = cent[int64_t(j) * c_sm + int64_t(i / dsub) * c_sk + int64_t(i % dsub) * c_sd];
+    cs[i] = __half2float(__float2half_rn(round_as(c, x_dtype)));
+  }
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    float s2 = 0.f;
+    for (int e = 0; e < dsub; ++e) {
+      const float v = cent[int64_t(j) * c_sm + int64_t(c) * c_sk + int64_t(e) * c_sd];
+      s2 = __fadd_rn(s2, __fmul_rn(v, v));
+    }
+    norms[c] = round_as(0.5f * s2, x_dtype);
+  }
   __syncthreads();
   const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (n >= N) return;
@@ -661,17 +683,15 @@ __global__ void pq_encode_kernel(const void* x, int x_dtype, int64_t x_sn, const
     if (x_dtype == BD_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[off]);
     else if (x_dtype == BD_F16) v = __half2float(reinterpret_cast<const __half*>(x)[off]);
     else v = reinterpret_cast<const float*>(x)[off];
-    xv[e] = v;
+    xv[e] = __half2float(__float2half_rn(v));
   }
-  float best = INFINITY;
+  float best = -INFINITY;
   int bi = 0;
   for (int c = 0; c < K; ++c) {
     float d = 0.f;
-    for (int e = 0; e < dsub; ++e) {
-      const float t = xv[e] - cs[c * dsub + e];
-      d = fmaf(t, t, d);
-    }
-    if (d < best) { best = d; bi = c; }
+    for (int e = 0; e < dsub; ++e) d = __fadd_rn(d, __fmul_rn(xv[e], cs[c * dsub + e]));
+    const float sc = __fsub_rn(d, norms[c]);
+    if (sc > best) { best = sc; bi = c; }
   }
   if (codes64) reinterpret_cast<int64_t*>(codes)[n * M + j] = bi;
   else reinterpret_cast<uint8_t*>(codes)[n * M + j] = uint8_t(bi);
@@ -1019,7 +1039,7 @@ int bd_pq_encode(const bd_tensor* x, const bd_tensor* centroids, const bd_tensor
     return fail(BD_ERR_SHAPE, "codes must be contiguous [N,M]");
   if (x->stride[1] != 1) return fail(BD_ERR_STRIDE, "x rows must be contiguous");
   if (x->dtype != BD_BF16 && x->dtype != BD_F16 && x->dtype != BD_F32) return fail(BD_ERR_DTYPE, "x dtype");
-  const size_t smem = size_t(K * dsub) * sizeof(float);
+  const size_t smem = size_t(K * (dsub + 1)) * sizeof(float);
   if (smem > 200 * 1024) return fail(BD_ERR_UNSUPPORTED, "codebook too large");
   if (N * M == 0) return BD_OK;
   static bool attr[64] = {false};

@@ -430,7 +430,9 @@ __global__ void pack_score_keys_kernel(const T* __restrict__ k, int64_t rows, in
     hi = fmaxf(hi, x);
   }
   constexpr int LV = (1 << BITS) - 1;
-  const float sc = __fdiv_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), float(LV));
+  // (max-min)/(levels-1) as PyTorch forms it on a CUDA device: times the fp32 reciprocal
+  constexpr float kRcp = 1.0f / float(LV);
+  const float sc = __fmul_rn(fmaxf(__fsub_rn(hi, lo), 1e-8f), kRcp);
   constexpr int EPB = 8 / BITS;
   uint8_t* dst = packed + row * (D / EPB) + int64_t(grp) * (gs / EPB);
   for (int e0 = 0; e0 < gs; e0 += EPB) {

@@ -73,9 +73,12 @@ class KIVIQuantizer:
 class ProductQuantizer:
     """Product quantizer with a GPU nearest-centroid encoder (ref: src/quantization.py:134-226).
 
-    ``quantize`` returns int64 codes [..., M] like the reference; distances are exact fp32
-    squared distances (the reference's CPU path uses cdist; near-equal distances may pick
-    either centroid).
+    ``quantize`` returns int64 codes [..., M] like the reference and follows the reference's
+    CUDA encoder: score = f16(x) . f16(centroid) - 0.5*||centroid||^2, argmax, first index
+    on ties (the centroids are rounded to x's dtype before f16, the norms to x's dtype).
+    Only scores equal to within fp32 summation order may pick another centroid than the
+    reference's tensor-core kernel. (The reference's CPU fallback, cdist + argmin, differs
+    from its CUDA kernel wherever f16 rounding reorders two centroids.)
     """
 
     def __init__(self, d, d_sub, bits=3, device="cuda"):

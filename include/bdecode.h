@@ -309,9 +309,12 @@ int bd_pq_scores(const bd_tensor* lut, const bd_tensor* k_idx, const bd_tensor* 
  * ref: the LUT einsum of benchmarks/test_correctness.py:181-182 and the key
  *      reconstruction of decode_attn_dequant src/attention_kernels.py:267 */
 int bd_pq_build_lut(const bd_tensor* q, const bd_tensor* centroids, const bd_tensor* lut, bd_stream_t stream);
-/* codes[n,j] = argmin_c ||x[n, j*d_sub:(j+1)*d_sub] - centroids[j,c]||^2 (fp32, first
- * index on ties). x [N,D] f32/bf16/f16; codes [N,M] u8 or int64.
- * ref: ProductQuantizer.quantize  src/quantization.py:160 */
+/* codes[n,j] = argmax_c (x_h . c_h - norm_c), first index on ties: the reference's CUDA
+ * nearest-centroid rule (x and the centroids rounded to f16 -- the centroids through x's
+ * dtype first -- products summed in fp32, norm_c = 0.5*||c||^2 rounded to x's dtype).
+ * x [N,D] f32/bf16/f16; codes [N,M] u8 or int64. For d_sub > 16 the whole sub-vector is
+ * used (the reference's CUDA kernel reads its first 16 elements only).
+ * ref: ProductQuantizer.quantize  src/quantization.py:160-199 (CUDA branch) */
 int bd_pq_encode(const bd_tensor* x, const bd_tensor* centroids, const bd_tensor* codes, bd_stream_t stream);
 
 /* Asymmetric uniform fake-quant over axis 3 of a 5-d strided view x (o0,o1,o2,

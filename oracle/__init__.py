@@ -12,7 +12,10 @@ as the timed CPU baseline. The product package ``bytes_b200`` never imports it; 
 entry points run the CUDA kernels or raise.
 
 Parity pinning: the restatement is checked against golden vectors produced by
-running the reference's own CPU-runnable functions (``tests/golden/make_golden.py``).
+running the reference's own CPU-runnable functions (``tests/golden/make_golden.py``) and
+its quantizers on a CUDA device (``tests/golden/make_golden_cuda.py``): those PyTorch
+expressions round differently on the two devices, and the quantizers here take
+``rule="cuda"`` (default, what the GPU engine must match) or ``rule="cpu"``.
 The external KIVI packer (jy-yuan/KIVI @ 876b4d2d, not vendored by the reference)
 is the one piece whose bit-exact output is not pinned: its layout is pinned by the
 reference's in-tree ``unpack_tensor_last_dim`` and its quantisation formula follows

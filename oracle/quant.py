@@ -2,26 +2,51 @@
 
 References: ``src/quantization.py`` and ``src/attention_kernels.py`` of saifmb0/bytes,
 ``benchmarks/kivi_latency.py`` (in-tree KIVI unpack / dequant / reference decode).
+
+Two device rules. The reference's quantizers are PyTorch expressions, and PyTorch
+evaluates ``tensor / python_number`` differently by device: on the CPU as a true
+division, on a CUDA device as a multiplication by the fp32 reciprocal of the number
+(computed once on the host; for bf16 / f16 tensors the product is formed in fp32 and
+rounded to the tensor's type). The two differ in the last bit of about half of all
+fp32 quotients, which moves a few percent of the quantised codes. ``rule="cuda"`` (the
+default) restates what the reference computes on a GPU, the device its decode path runs
+on; ``rule="cpu"`` restates its CPU run. ``ProductQuantizer.quantize`` is a different
+algorithm on each device (a Triton f16-dot-product kernel on CUDA, cdist + argmin on the
+CPU); ``pq_encode`` restates both.
 """
 import math
 
+import numpy as np
 import torch
 
 
-def asym_uniform_fakequant(x, levels, dim):
+def div_scalar(t, n, rule="cuda"):
+    """``t / n`` for a tensor t and a Python number n, as PyTorch evaluates it on ``rule``'s
+    device: CPU = true division; CUDA = t * fp32(1/n), formed in fp32 and rounded to t's type."""
+    if rule == "cpu":
+        return t / n
+    if rule != "cuda":
+        raise ValueError(f"unknown rule {rule!r}")
+    rcp = torch.tensor(np.float32(1.0) / np.float32(n), dtype=torch.float32)
+    return (t.float() * rcp).to(t.dtype)
+
+
+def asym_uniform_fakequant(x, levels, dim, rule="cuda"):
     """Quantize-then-dequantize with the [min,max] range taken over ``dim``.
 
     src/quantization.py:432-442: scale = clamp(max-min, 1e-8)/(levels-1);
-    q = clamp(round((x-min)/scale), 0, levels-1); return q*scale + min.
+    q = clamp(round((x-min)/scale), 0, levels-1); return q*scale + min. The division by
+    levels-1 follows ``rule`` (see ``div_scalar``); (x-min)/scale is a true division on
+    both devices.
     """
     xmin = x.amin(dim=dim, keepdim=True)
     xmax = x.amax(dim=dim, keepdim=True)
-    scale = (xmax - xmin).clamp(min=1e-8) / (levels - 1)
+    scale = div_scalar((xmax - xmin).clamp(min=1e-8), levels - 1, rule)
     q = torch.clamp(torch.round((x - xmin) / scale), 0, levels - 1)
     return q * scale + xmin
 
 
-def kivi_quantize_key(k, bits=4, group_size=32, residual_length=32):
+def kivi_quantize_key(k, bits=4, group_size=32, residual_length=32, rule="cuda"):
     """KIVIQuantizer.quantize_key (src/quantization.py:468-489): per-channel scales over
     groups of ``group_size`` tokens; a ragged token tail forms one group; the last
     ``residual_length`` tokens stay exact."""
@@ -38,14 +63,14 @@ def kivi_quantize_key(k, bits=4, group_size=32, residual_length=32):
     parts = []
     if n_full > 0:
         main = k_q[:, :, :n_full * G, :].reshape(B, H, n_full, G, D)
-        parts.append(asym_uniform_fakequant(main, levels, 3).reshape(B, H, n_full * G, D))
+        parts.append(asym_uniform_fakequant(main, levels, 3, rule).reshape(B, H, n_full * G, D))
     if n_full * G < S_q:
-        parts.append(asym_uniform_fakequant(k_q[:, :, n_full * G:, :], levels, 2))
+        parts.append(asym_uniform_fakequant(k_q[:, :, n_full * G:, :], levels, 2, rule))
     k_dq = torch.cat(parts, dim=2) if len(parts) > 1 else parts[0]
     return torch.cat([k_dq.to(k.dtype), k_res], dim=2)
 
 
-def kivi_quantize_value(v, bits=4, group_size=32, residual_length=32):
+def kivi_quantize_value(v, bits=4, group_size=32, residual_length=32, rule="cuda"):
     """KIVIQuantizer.quantize_value (src/quantization.py:491-501): per-token range over
     all channels, last ``residual_length`` tokens exact."""
     levels = 2 ** bits
@@ -54,11 +79,11 @@ def kivi_quantize_value(v, bits=4, group_size=32, residual_length=32):
     S_q = S - R
     if S_q <= 0:
         return v
-    v_dq = asym_uniform_fakequant(v[:, :, :S_q, :].float(), levels, 3)
+    v_dq = asym_uniform_fakequant(v[:, :, :S_q, :].float(), levels, 3, rule)
     return torch.cat([v_dq.to(v.dtype), v[:, :, S_q:, :]], dim=2)
 
 
-def quantize_and_pack_score_keys(k, score_bits, group_size):
+def quantize_and_pack_score_keys(k, score_bits, group_size, rule="cuda"):
     """Per-token groups of ``group_size`` channels, fp32 min/max/scale, round-half-even,
     2 codes (4-bit) or 4 codes (2-bit) per byte, low bits first.
 
@@ -73,7 +98,7 @@ def quantize_and_pack_score_keys(k, score_bits, group_size):
     kr = k.reshape(B, H, S, ng, group_size).float()
     xmin = kr.amin(dim=-1, keepdim=True)
     xmax = kr.amax(dim=-1, keepdim=True)
-    scale = (xmax - xmin).clamp(min=1e-8) / (levels - 1)
+    scale = div_scalar((xmax - xmin).clamp(min=1e-8), levels - 1, rule)
     q = torch.clamp(torch.round((kr - xmin) / scale), 0, levels - 1).to(torch.uint8)
     qf = q.reshape(B, H, S, D)
     epb = 8 // score_bits
@@ -95,15 +120,16 @@ def unpack_score_keys(packed, score_bits):
     return torch.stack(cols, dim=-1).reshape(packed.shape[:-1] + (packed.shape[-1] * epb,)).to(torch.uint8)
 
 
-def kivi_pack_last_dim(x, group_size, bits):
+def kivi_pack_last_dim(x, group_size, bits, rule="cuda"):
     """Group-wise asymmetric quantize + pack along the last dim (KIVI packer contract).
 
     The packer lives in the un-vendored external KIVI checkout (call sites
     benchmarks/kivi_latency.py:123,127,208,210). Layout follows the reference's
     in-tree unpacker (benchmarks/kivi_latency.py:26-35): element e -> int32 word
     e // (32/bits), bit offset (e % (32/bits)) * bits. Quantisation follows
-    src/quantization.py:438-442 in fp32 (scale clamped at 1e-8); scale and mn are
-    stored in x.dtype. Returns (code int32 [...,N*bits/32], scale [...,N/gs], mn [...,N/gs]).
+    src/quantization.py:438-442 in fp32 (scale clamped at 1e-8; the division by 2^bits-1
+    follows ``rule``, as PyTorch evaluates the packer's scale on the device it runs on);
+    scale and mn are stored in x.dtype. Returns (code int32 [...,N*bits/32], scale [...,N/gs], mn [...,N/gs]).
     """
     N = x.shape[-1]
     fpi = 32 // bits
@@ -111,7 +137,7 @@ def kivi_pack_last_dim(x, group_size, bits):
     xf = x.float().reshape(lead + (N // group_size, group_size))
     mn = xf.amin(dim=-1, keepdim=True)
     mx = xf.amax(dim=-1, keepdim=True)
-    scale = (mx - mn).clamp(min=1e-8) / (2 ** bits - 1)
+    scale = div_scalar((mx - mn).clamp(min=1e-8), 2 ** bits - 1, rule)
     q = torch.clamp(torch.round((xf - mn) / scale), 0, 2 ** bits - 1).to(torch.int64)
     q = q.reshape(lead + (N // fpi, fpi))
     shifts = torch.arange(fpi, dtype=torch.int64) * bits
@@ -182,18 +208,44 @@ def kivi_gemv_outer(group_size, fA, qB, scales, zeros, bits):
     return torch.matmul(fA.float(), deq).to(torch.float16)
 
 
-def pq_encode(X, centroids):
-    """Nearest centroid per subspace: argmin_k ||x_j - c_{j,k}||, first index on ties.
+def pq_encode(X, centroids, rule="cuda"):
+    """Nearest centroid per subspace. X [...,D], centroids [M,K,d_sub] -> int64 [...,M].
 
-    ProductQuantizer.quantize CPU path (src/quantization.py:203-211) with the
-    distance computed directly in fp32. X [...,D], centroids [M,K,d_sub] -> int64 [...,M].
+    rule="cuda": ProductQuantizer.quantize on a CUDA device (src/quantization.py:167-199,
+    Triton kernel :8-60): score_k = f16(x) . f16(dtype_x(c_k)) summed in fp32, minus
+    dtype_x(0.5*||c_k||^2); argmax, first index on ties. (The reference's kernel reads the
+    first 16 elements of a sub-vector; this restatement, like the engine, uses all d_sub.)
+    The products of f16 values are exact in fp32 and are summed in element order.
+
+    rule="cpu": the CPU path (src/quantization.py:203-211), argmin of the fp32 squared
+    distance, first index on ties.
     """
     M, K, d_sub = centroids.shape
     lead = X.shape[:-1]
-    Xs = X.float().reshape(-1, M, d_sub)
-    c = centroids.float()
-    d2 = ((Xs[:, :, None, :] - c[None, :, :, :]) ** 2).sum(-1)  # [N,M,K]
-    return d2.argmin(dim=-1).reshape(lead + (M,))
+    if rule == "cpu":
+        Xs = X.float().reshape(-1, M, d_sub)
+        c = centroids.float()
+        d2 = ((Xs[:, :, None, :] - c[None, :, :, :]) ** 2).sum(-1)  # [N,M,K]
+        return d2.argmin(dim=-1).reshape(lead + (M,))
+    if rule != "cuda":
+        raise ValueError(f"unknown rule {rule!r}")
+    return pq_encode_scores(X, centroids).argmax(dim=-1).reshape(lead + (M,))
+
+
+def pq_encode_scores(X, centroids):
+    """The CUDA-rule scores [N,M,K] of ``pq_encode`` (higher is nearer)."""
+    M, K, d_sub = centroids.shape
+    xs = X.reshape(-1, M, d_sub).to(torch.float16).float()
+    c = centroids.to(X.dtype).to(torch.float16).float()
+    c2 = centroids.float() * centroids.float()
+    s2 = torch.zeros(M, K)
+    for e in range(d_sub):
+        s2 = s2 + c2[:, :, e]
+    norms = (0.5 * s2).to(X.dtype).float()
+    dot = torch.zeros(xs.shape[0], M, K)
+    for e in range(d_sub):
+        dot = dot + xs[:, :, None, e] * c[None, :, :, e]
+    return dot - norms[None]
 
 
 def pq_distances(X, centroids):

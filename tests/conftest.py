@@ -20,6 +20,12 @@ def golden():
 
 
 @pytest.fixture(scope="session")
+def golden_cuda():
+    """The reference's quantizers run on a CUDA device (tests/golden/make_golden_cuda.py)."""
+    return torch.load(os.path.join(ROOT, "tests", "golden", "golden_cuda.pt"))
+
+
+@pytest.fixture(scope="session")
 def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")

@@ -36,8 +36,9 @@ def test_pack_score_keys_bit_exact(cuda, dtype, bits):
     assert torch.equal(p.cpu(), rp) and torch.equal(s.cpu(), rs) and torch.equal(z.cpu(), rz)
 
 
-def test_pack_score_keys_golden(cuda, golden):
-    for c in golden["pack_score_keys"]:
+def test_pack_score_keys_golden(cuda, golden_cuda):
+    """Against the reference's packer run on a CUDA device (bit-exact)."""
+    for c in golden_cuda["pack_score_keys"]:
         p, s, z = ak.quantize_and_pack_score_keys(c["k"].to(cuda), c["bits"], c["group_size"])
         assert torch.equal(p.cpu(), c["packed"])
         assert torch.equal(s.cpu(), c["scale"])

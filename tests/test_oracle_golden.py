@@ -1,8 +1,12 @@
 """Pin the CPU oracle against golden vectors produced by the reference's own code.
 
-The fixtures come from tests/golden/make_golden.py, which imports the reference
-project and runs its CPU-runnable functions. Integer / byte / index outputs must be
-bit-exact; floating outputs agree to fp32 summation-order noise.
+``golden.pt`` comes from tests/golden/make_golden.py, which imports the reference project
+and runs its CPU-runnable functions; ``golden_cuda.pt`` from tests/golden/make_golden_cuda.py,
+which runs the reference's quantizers on a CUDA device, where PyTorch evaluates their
+division by levels-1 as a reciprocal multiply and ``ProductQuantizer`` encodes with its
+f16 Triton kernel. The oracle's quantizers take ``rule="cpu"`` / ``rule="cuda"`` for the
+two. Integer / byte / index outputs must be bit-exact; floating outputs agree to fp32
+summation-order noise.
 """
 import math
 
@@ -13,7 +17,7 @@ import oracle
 
 def test_pack_score_keys_bit_exact(golden):
     for c in golden["pack_score_keys"]:
-        p, s, z = oracle.quantize_and_pack_score_keys(c["k"], c["bits"], c["group_size"])
+        p, s, z = oracle.quantize_and_pack_score_keys(c["k"], c["bits"], c["group_size"], rule="cpu")
         assert torch.equal(p, c["packed"])
         assert torch.equal(s, c["scale"]) and s.dtype == c["scale"].dtype
         assert torch.equal(z, c["zero"])
@@ -23,14 +27,14 @@ def test_pack_score_keys_bit_exact(golden):
 
 def test_fakequant_bit_exact(golden):
     for c in golden["fakequant"]:
-        y = oracle.asym_uniform_fakequant(c["x"], c["levels"], c["dim"])
+        y = oracle.asym_uniform_fakequant(c["x"], c["levels"], c["dim"], rule="cpu")
         assert torch.equal(y, c["y"])
 
 
 def test_kivi_quantizer_bit_exact(golden):
     for c in golden["kivi_quantizer"]:
-        kf = oracle.kivi_quantize_key(c["k"], c["bits"], c["group_size"], c["residual_length"])
-        vf = oracle.kivi_quantize_value(c["v"], c["bits"], c["group_size"], c["residual_length"])
+        kf = oracle.kivi_quantize_key(c["k"], c["bits"], c["group_size"], c["residual_length"], rule="cpu")
+        vf = oracle.kivi_quantize_value(c["v"], c["bits"], c["group_size"], c["residual_length"], rule="cpu")
         assert torch.equal(kf, c["k_fq"])
         assert torch.equal(vf, c["v_fq"])
 
@@ -39,7 +43,7 @@ def test_pq_encode_matches_reference_cpu_path(golden):
     """cdist+argmin (reference) vs direct fp32 distances (oracle): equal codes, except
     where the two candidates' distances tie within float noise."""
     for c in golden["pq_encode"]:
-        codes = oracle.pq_encode(c["X"], c["centroids"])
+        codes = oracle.pq_encode(c["X"], c["centroids"], rule="cpu")
         ref = c["codes"]
         diff = codes != ref
         if diff.any():
@@ -48,6 +52,47 @@ def test_pq_encode_matches_reference_cpu_path(golden):
             b = d2.gather(-1, ref.unsqueeze(-1)).squeeze(-1)[diff]
             assert torch.allclose(a, b, rtol=1e-5, atol=1e-5)
         assert diff.float().mean() < 1e-3
+
+
+def test_quantizers_match_reference_on_cuda(golden_cuda):
+    """rule="cuda" reproduces the reference's quantizers run on a GPU bit for bit, and the
+    fixture separates the device rules (the CPU rule misses some of its bytes)."""
+    cpu_miss = 0
+    for c in golden_cuda["pack_score_keys"]:
+        out = oracle.quantize_and_pack_score_keys(c["k"], c["bits"], c["group_size"])
+        for a, b in zip(out, (c["packed"], c["scale"], c["zero"])):
+            assert a.dtype == b.dtype and torch.equal(a, b)
+        cpu = oracle.quantize_and_pack_score_keys(c["k"], c["bits"], c["group_size"], rule="cpu")
+        n = sum(int((a != b).sum()) for a, b in zip(cpu, (c["packed"], c["scale"], c["zero"])))
+        assert n == c["cpu_differs"]
+        cpu_miss += n
+    for c in golden_cuda["fakequant"]:
+        assert torch.equal(oracle.asym_uniform_fakequant(c["x"], c["levels"], c["dim"]), c["y"])
+        cpu = oracle.asym_uniform_fakequant(c["x"], c["levels"], c["dim"], rule="cpu")
+        assert int((cpu != c["y"]).sum()) == c["cpu_differs"]
+        cpu_miss += c["cpu_differs"]
+    for c in golden_cuda["kivi_quantizer"]:
+        args = (c["bits"], c["group_size"], c["residual_length"])
+        assert torch.equal(oracle.kivi_quantize_key(c["k"], *args), c["k_fq"])
+        assert torch.equal(oracle.kivi_quantize_value(c["v"], *args), c["v_fq"])
+    assert cpu_miss > 0
+
+
+def test_pq_encode_matches_reference_cuda_kernel(golden_cuda):
+    """rule="cuda" (f16 dot products minus norms, argmax) against the reference's Triton
+    encoder: equal codes except between centroids whose scores agree to fp32 summation
+    order; its CPU path (rule="cpu") differs on more codes."""
+    for c in golden_cuda["pq_encode"]:
+        codes = oracle.pq_encode(c["X"], c["centroids"])
+        ref = c["codes"]
+        diff = codes != ref
+        if diff.any():
+            sc = oracle.quant.pq_encode_scores(c["X"], c["centroids"])
+            a = sc.gather(-1, codes.unsqueeze(-1)).squeeze(-1)[diff]
+            b = sc.gather(-1, ref.unsqueeze(-1)).squeeze(-1)[diff]
+            assert torch.allclose(a, b, rtol=1e-5, atol=1e-5)
+        assert diff.float().mean() < 1e-3
+    assert sum(c["cpu_differs"] for c in golden_cuda["pq_encode"]) > 0
 
 
 def test_select_topk_exact_matches_reference(golden):
