@@ -377,11 +377,18 @@ def quest_page_minmax_into(k, page, kmin, kmax):
     N.check(rc, "bd_quest_page_minmax")
 
 
+def _page_meta(t):
+    """Quest page metadata as the kernels read it: bf16 / f16 / fp32 as given (other float
+    dtypes widened to fp32), rows on 16-byte boundaries."""
+    if t.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        t = t.float()
+    return rows_aligned(t)
+
+
 def quest_page_bounds(q3, kmin, kmax, scaling, force_from_page=None):
     N.require_cuda(q3, kmin, kmax)
     q3 = inner_contig(q3)
-    kmin = rows_aligned(kmin.to(torch.bfloat16))
-    kmax = rows_aligned(kmax.to(torch.bfloat16))
+    kmin, kmax = _page_meta(kmin), _page_meta(kmax)
     B, Hq, _ = q3.shape
     np_ = kmin.shape[2]
     bounds = torch.empty(B, Hq, np_, dtype=torch.float32, device=q3.device)
@@ -397,8 +404,7 @@ def quest_page_bounds(q3, kmin, kmax, scaling, force_from_page=None):
 def quest_select(q3, kmin, kmax, S, kb, page, scaling, force_from_page=None, idx_dtype=torch.int64):
     N.require_cuda(q3, kmin, kmax)
     q3 = inner_contig(q3)
-    kmin = rows_aligned(kmin.to(torch.bfloat16))
-    kmax = rows_aligned(kmax.to(torch.bfloat16))
+    kmin, kmax = _page_meta(kmin), _page_meta(kmax)
     B, Hq, _ = q3.shape
     np_ = kmin.shape[2]
     npick = min(max(1, (kb + page - 1) // page), np_)

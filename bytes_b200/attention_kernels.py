@@ -49,22 +49,23 @@ def decode_attn_fp8(q, k, v):
 
 
 def sparse_score_scalar(q, k_score, scaling, *, score_bits=16, BLOCK_N=128):
-    """Pass-1 exact scores [B,H_q,S] fp32 = scaling * q.k over bf16 (16) or fp8 (8) keys.
+    """Pass-1 exact scores [B,H_q,S] fp32 = scaling * q.k.
 
-    ref: src/attention_kernels.py:1113-1133.
+    ref: src/attention_kernels.py:1113-1133. Like the reference, the key dtype decides the
+    arithmetic and ``score_bits`` is a label: fp8 e4m3 keys, or bf16 / f16 / fp32 keys
+    (bf16 query and keys on the tensor cores, where every product is exact in fp32; other
+    combinations in fp32 on the CUDA cores, unrounded). Other float dtypes are read as fp32.
     """
     q3 = _squeeze_q(q)
-    if score_bits == 16:
-        if k_score.dtype != torch.bfloat16:
-            raise ValueError("score_bits=16 expects bf16 keys")
-        if q3.dtype != torch.bfloat16:
-            q3 = q3.to(torch.bfloat16)
-    elif score_bits == 8:
-        if k_score.dtype != torch.float8_e4m3fn:
-            raise ValueError("score_bits=8 expects fp8 e4m3 keys")
+    if q3.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        q3 = q3.float()
+    if k_score.dtype == torch.float8_e4m3fn:
+        bits = 8
     else:
-        raise ValueError("Unsupported score_bits")
-    return _ops.sparse_score(q3, k_score, None, None, scaling, score_bits, 32)
+        bits = 16
+        if k_score.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            k_score = k_score.float()
+    return _ops.sparse_score(q3, k_score, None, None, scaling, bits, 32)
 
 
 def sparse_score_packed(q, k_packed, scale, zero, scaling, *, score_bits=4, group_size=32, BLOCK_N=128):
@@ -80,8 +81,9 @@ def sparse_score_packed(q, k_packed, scale, zero, scaling, *, score_bits=4, grou
 def quantize_and_pack_score_keys(k, score_bits, group_size):
     """Per-token groups of `group_size` channels -> (packed uint8, scale, zero) in k.dtype.
 
-    ref: src/attention_kernels.py:1225-1249 (bit-exact: fp32 min/max, IEEE divide,
-    round-half-even, low bits first).
+    ref: src/attention_kernels.py:1225-1249, bit-exact with the reference run on a CUDA
+    device: fp32 min/max, scale = range times the fp32 reciprocal of levels-1 (PyTorch's
+    CUDA division by a number), codes by IEEE division, round-half-even, low bits first.
     """
     if score_bits not in (2, 4):
         raise ValueError("Unsupported score_bits")
@@ -96,9 +98,14 @@ def sparse_gather_attn(q, k, v, idx, scaling, BLOCK_K=64):
     """
     q3 = _squeeze_q(q)
     out_dtype = torch.bfloat16 if v.dtype == torch.float8_e4m3fn else v.dtype
-    out = torch.empty(q3.shape, dtype=out_dtype, device=q.device)
+    if k.dtype not in (torch.bfloat16, torch.float16, torch.float32, torch.float8_e4m3fn) or k.dtype != v.dtype:
+        k, v = k.float(), v.float()
+    if q3.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        q3 = q3.float()
+    out = torch.empty(q3.shape, dtype=out_dtype if out_dtype in (torch.bfloat16, torch.float16, torch.float32)
+                      else torch.float32, device=q.device)
     _ops.gather_attn(q3, k, v, idx, scaling, out)
-    return out.unsqueeze(2)
+    return out.to(out_dtype).unsqueeze(2)
 
 
 def _budget(frac, S):

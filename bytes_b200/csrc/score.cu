@@ -410,6 +410,78 @@ int launch_score_nt(const ScoreParams& p, int nt, int n_splits, cudaStream_t st)
 
 int tile_tokens(int kt) { return 16 * kSW * (kt == 16 ? 1 : (kt == 8 ? 2 : 4)); }
 
+// ------------------------------------------------------------ full-precision scores
+// CUDA-core fp32 form of the same scores for the inputs the tensor-core tiles would have
+// to round: an fp32 query (the MMA operands are bf16 / f16), an f16 query against bf16
+// keys, and f16 / fp32 keys. Every key element is widened to fp32 (packed codes
+// dequantised as code * scale + zero, the reference's per-element form,
+// src/attention_kernels.py:1175-1190); score = scaling * sum_d q_d * k_d, like the
+// reference's fp32 Triton blocks (:1098-1110, :1169-1196) up to summation order.
+// One CTA: 64 tokens of one (batch, KV head), the group's heads 16 at a time; the key tile
+// sits in shared memory with a padded pitch (conflict-free column reads), each thread owns
+// one token and 8 heads.
+enum GenericKey { kGkBf16 = 0, kGkF16, kGkF32, kGkFp8, kGkPack4, kGkPack2 };
+constexpr int kGenTok = 64;
+
+template <int KIND, int D>
+__global__ void __launch_bounds__(128) score_generic_kernel(const ScoreParams p) {
+  __shared__ float ks[kGenTok][D + 1];
+  __shared__ float qs[16][D];
+  const int t0 = blockIdx.x * kGenTok, hk = blockIdx.y, b = blockIdx.z;
+  const int nt = min(kGenTok, p.S - t0);
+  for (int i = threadIdx.x; i < kGenTok * D; i += 128) {
+    const int t = i / D, d = i % D;
+    float x = 0.f;
+    if (t < nt) {
+      const int64_t tok = int64_t(b) * p.k_sb + int64_t(hk) * p.k_sh + int64_t(t0 + t) * p.k_ss;
+      if (KIND == kGkBf16) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.k)[tok + d]);
+      else if (KIND == kGkF16) x = __half2float(reinterpret_cast<const __half*>(p.k)[tok + d]);
+      else if (KIND == kGkF32) x = reinterpret_cast<const float*>(p.k)[tok + d];
+      else if (KIND == kGkFp8) x = float(reinterpret_cast<const __nv_fp8_e4m3*>(p.k)[tok + d]);
+      else {
+        constexpr int BITS = KIND == kGkPack4 ? 4 : 2, EPB = 8 / BITS;
+        const uint32_t code = (uint32_t(p.k[tok + d / EPB]) >> ((d % EPB) * BITS)) & ((1u << BITS) - 1);
+        const int g = d / p.gs;
+        const float sc = h16_to_f(p.sc[int64_t(b) * p.sc_sb + int64_t(hk) * p.sc_sh + int64_t(t0 + t) * p.sc_ss + g], p.sz_bf16);
+        const float zr = h16_to_f(p.zr[int64_t(b) * p.zr_sb + int64_t(hk) * p.zr_sh + int64_t(t0 + t) * p.zr_ss + g], p.sz_bf16);
+        x = fmaf(float(code), sc, zr);
+      }
+    }
+    ks[t][d] = x;
+  }
+  const int t = threadIdx.x % kGenTok, hsel = threadIdx.x / kGenTok;  // 2 head lanes
+  for (int h0 = 0; h0 < p.G; h0 += 16) {
+    const int nh = min(16, p.G - h0);
+    __syncthreads();  // the key tile is written / the previous head chunk's readers are done
+    for (int i = threadIdx.x; i < nh * D; i += 128) {
+      const int h = i / D, d = i % D;
+      qs[h][d] = load_qs(p, int64_t(b) * p.q_sb + int64_t(hk * p.G + h0 + h) * p.q_sh + d);
+    }
+    __syncthreads();
+    if (t >= nt) continue;
+    for (int h = hsel; h < nh; h += 2) {
+      float acc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < D; ++d) acc = fmaf(qs[h][d], ks[t][d], acc);
+      p.out[int64_t(b) * p.o_sb + int64_t(hk * p.G + h0 + h) * p.o_sh + t0 + t] = acc * p.scaling;
+    }
+  }
+}
+
+template <int D>
+int launch_score_generic(const ScoreParams& p, int kind, cudaStream_t st) {
+  dim3 grid(unsigned((p.S + kGenTok - 1) / kGenTok), unsigned(p.Hk), unsigned(p.B));
+  switch (kind) {
+    case kGkBf16: score_generic_kernel<kGkBf16, D><<<grid, 128, 0, st>>>(p); break;
+    case kGkF16: score_generic_kernel<kGkF16, D><<<grid, 128, 0, st>>>(p); break;
+    case kGkF32: score_generic_kernel<kGkF32, D><<<grid, 128, 0, st>>>(p); break;
+    case kGkFp8: score_generic_kernel<kGkFp8, D><<<grid, 128, 0, st>>>(p); break;
+    case kGkPack4: score_generic_kernel<kGkPack4, D><<<grid, 128, 0, st>>>(p); break;
+    default: score_generic_kernel<kGkPack2, D><<<grid, 128, 0, st>>>(p); break;
+  }
+  return cuda_check(cudaGetLastError(), "score_generic_kernel launch");
+}
+
 // ------------------------------------------------------------ score-key pack
 template <typename T, int BITS>
 __global__ void pack_score_keys_kernel(const T* __restrict__ k, int64_t rows, int64_t r_h, int64_t s_b, int64_t s_h,
@@ -468,8 +540,8 @@ int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* sca
   if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
   int kt;
   if (score_bits == 16) {
-    if (k->dtype != BD_BF16 || k->shape[3] != D) return fail(BD_ERR_DTYPE, "score_bits=16 needs bf16 k [B,Hk,S,D]");
-    if (q->dtype != BD_BF16) return fail(BD_ERR_DTYPE, "score_bits=16 needs a bf16 query");
+    if ((k->dtype != BD_BF16 && k->dtype != BD_F16 && k->dtype != BD_F32) || k->shape[3] != D)
+      return fail(BD_ERR_DTYPE, "score_bits=16 needs bf16, f16 or f32 k [B,Hk,S,D]");
     kt = 16;
   } else if (score_bits == 8) {
     if (k->dtype != BD_F8E4M3 || k->shape[3] != D) return fail(BD_ERR_DTYPE, "score_bits=8 needs fp8 e4m3 k [B,Hk,S,D]");
@@ -518,6 +590,15 @@ int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* sca
   p.heads_per_chunk = 8 * nt;
   p.head_chunks = (p.G + p.heads_per_chunk - 1) / p.heads_per_chunk;
   p.scaling = scaling;
+  // inputs the tensor-core operands would round (fp32 query; f16 query against bf16 keys;
+  // f16 / fp32 keys) take the fp32 CUDA-core kernel
+  const bool generic = q->dtype == BD_F32 || (kt == 16 && (k->dtype != BD_BF16 || q->dtype != BD_BF16));
+  if (generic) {
+    const int kind = kt == 16 ? (k->dtype == BD_BF16 ? kGkBf16 : k->dtype == BD_F16 ? kGkF16 : kGkF32)
+                              : kt == 8 ? kGkFp8 : kt == 4 ? kGkPack4 : kGkPack2;
+    cudaStream_t gst = reinterpret_cast<cudaStream_t>(stream);
+    return D == 128 ? launch_score_generic<128>(p, kind, gst) : launch_score_generic<64>(p, kind, gst);
+  }
   const int64_t tt = tile_tokens(kt);
   const int64_t ntiles = (S + tt - 1) / tt;
   const int64_t pairs = B * Hk * p.head_chunks;

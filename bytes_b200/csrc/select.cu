@@ -22,6 +22,7 @@
 #include "decode_shared.cuh"
 
 #include <algorithm>
+#include <type_traits>
 #include <cmath>
 
 namespace bd {
@@ -820,12 +821,16 @@ struct GatherParams {
   void* out; int out_dtype; int64_t o_sb, o_sh;  // one split and a final output: written directly
 };
 
-template <int D, bool FP8>
+// key/value element kinds of the gather (fp8 e4m3, bf16, f16, fp32), widened to fp32
+enum GatherKv { kGvBf16 = 0, kGvFp8, kGvF16, kGvF32 };
+
+template <int D, int KV>
 __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) {
+  constexpr bool FP8 = KV == kGvFp8;
   griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
   griddep_launch_dependents();  // the combine queued behind may start launching (it waits for this grid)
   constexpr int CPL = D / 8;  // channels per lane (8 lanes per row)
-  constexpr int ELT = FP8 ? 1 : 2;
+  constexpr int ELT = FP8 ? 1 : (KV == kGvF32 ? 4 : 2);
   __shared__ float red_m[16], red_l[16];
   __shared__ float red_o[16][D];
   const int split = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
@@ -893,6 +898,14 @@ __global__ void __launch_bounds__(128) gather_attn_kernel(const GatherParams p) 
         const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v23));
         kf[4 * w] = a.x; kf[4 * w + 1] = a.y; kf[4 * w + 2] = c.x; kf[4 * w + 3] = c.y;
         vf[4 * w] = d.x; vf[4 * w + 1] = d.y; vf[4 * w + 2] = e.x; vf[4 * w + 3] = e.y;
+      } else if (KV == kGvF32) {
+        kf[w] = __uint_as_float(kw[w]);
+        vf[w] = __uint_as_float(vw[w]);
+      } else if (KV == kGvF16) {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&kw[w]));
+        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&vw[w]));
+        kf[2 * w] = a.x; kf[2 * w + 1] = a.y;
+        vf[2 * w] = c.x; vf[2 * w + 1] = c.y;
       } else {
         kf[2 * w] = __uint_as_float(kw[w] << 16);
         kf[2 * w + 1] = __uint_as_float(kw[w] & 0xffff0000u);
@@ -1003,24 +1016,35 @@ __global__ void quest_minmax_kernel(const T* __restrict__ k, int64_t s_b, int64_
 }
 
 // bound[b,hq,p] = scaling * sum_d max(q_d*kmin_pd, q_d*kmax_pd); pages >= force_from -> +inf
-constexpr int kQPages = 64;  // pages per CTA (one thread each)
+// (the reference's fp32 bound, benchmarks/sparse_attention.py:342-345). Page metadata MT is
+// bf16, f16 or fp32 (the key dtype), read unrounded; 64 pages per CTA (32 for fp32 rows).
+constexpr int kQPages = 64;  // pages per CTA (one thread each) for 16-bit metadata
 
-template <int D>
+template <typename MT>
+__device__ __forceinline__ float meta_f32(const uint8_t* p) {
+  if constexpr (sizeof(MT) == 4) return *reinterpret_cast<const float*>(p);
+  else return to_f32<MT>(*reinterpret_cast<const MT*>(p));
+}
+
+template <int D, typename MT>
 __global__ void __launch_bounds__(kQPages) quest_bounds_kernel(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh,
-                                                         const __nv_bfloat16* kmin, const __nv_bfloat16* kmax,
+                                                         const MT* kmin, const MT* kmax,
                                                          int64_t m_sb, int64_t m_sh, int64_t m_sp, int Hq, int Hk,
                                                          int np, float scaling, int force_from, float* bounds) {
   griddep_wait();  // programmatic launch: the previous kernel's results are complete past here
   griddep_launch_dependents();
-  constexpr int PITCH = D * 2 + 16;
-  __shared__ __align__(16) uint8_t sm[2][kQPages * PITCH];
-  const int b = blockIdx.z, hk = blockIdx.y, p0 = blockIdx.x * kQPages;
+  constexpr int ES = int(sizeof(MT));
+  constexpr int NP = ES == 4 ? kQPages / 2 : kQPages;  // pages per CTA
+  constexpr int PITCH = D * ES + 16;
+  constexpr int EPC = 16 / ES;  // elements per 16-byte chunk
+  __shared__ __align__(16) uint8_t sm[2][NP * PITCH];
+  const int b = blockIdx.z, hk = blockIdx.y, p0 = blockIdx.x * NP;
   const int G = Hq / Hk;
-  const int npg = min(kQPages, np - p0);
+  const int npg = min(NP, np - p0);
   // stage the pages' min and max rows (padded pitch: conflict-free 16-byte reads)
-  for (int c = threadIdx.x; c < npg * (D / 8); c += kQPages) {
-    const int r = c / (D / 8), cc = c % (D / 8);
-    const int64_t go = int64_t(b) * m_sb + int64_t(hk) * m_sh + int64_t(p0 + r) * m_sp + cc * 8;
+  for (int c = threadIdx.x; c < npg * (D / EPC); c += NP) {
+    const int r = c / (D / EPC), cc = c % (D / EPC);
+    const int64_t go = int64_t(b) * m_sb + int64_t(hk) * m_sh + int64_t(p0 + r) * m_sp + cc * EPC;
     cp_async16(smem_u32(&sm[0][r * PITCH + cc * 16]), kmin + go, 16);
     cp_async16(smem_u32(&sm[1][r * PITCH + cc * 16]), kmax + go, 16);
   }
@@ -1032,28 +1056,18 @@ __global__ void __launch_bounds__(kQPages) quest_bounds_kernel(const void* q, in
   const int pg = p0 + r;
   for (int h0 = 0; h0 < G; h0 += 4) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c8 = 0; c8 < D / 8; ++c8) {
-      const uint4 lo4 = *reinterpret_cast<const uint4*>(&sm[0][r * PITCH + c8 * 16]);
-      const uint4 hi4 = *reinterpret_cast<const uint4*>(&sm[1][r * PITCH + c8 * 16]);
-      const uint32_t lw[4] = {lo4.x, lo4.y, lo4.z, lo4.w}, hw[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+    for (int d = 0; d < D; ++d) {
+      const float mnv = meta_f32<MT>(&sm[0][r * PITCH + d * ES]);
+      const float mxv = meta_f32<MT>(&sm[1][r * PITCH + d * ES]);
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {
         if (h0 + hh >= G) break;
-        const int64_t qo = int64_t(b) * q_sb + int64_t(hk * G + h0 + hh) * q_sh + c8 * 8;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float mnv = __uint_as_float(e ? (lw[w] & 0xffff0000u) : (lw[w] << 16));
-            const float mxv = __uint_as_float(e ? (hw[w] & 0xffff0000u) : (hw[w] << 16));
-            float qd;
-            const int64_t qi = qo + 2 * w + e;
-            if (q_dtype == BD_BF16) qd = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(q)[qi]);
-            else if (q_dtype == BD_F16) qd = __half2float(reinterpret_cast<const __half*>(q)[qi]);
-            else qd = reinterpret_cast<const float*>(q)[qi];
-            acc[hh] += fmaxf(qd * mnv, qd * mxv);
-          }
-        }
+        const int64_t qi = int64_t(b) * q_sb + int64_t(hk * G + h0 + hh) * q_sh + d;
+        float qd;
+        if (q_dtype == BD_BF16) qd = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(q)[qi]);
+        else if (q_dtype == BD_F16) qd = __half2float(reinterpret_cast<const __half*>(q)[qi]);
+        else qd = reinterpret_cast<const float*>(q)[qi];
+        acc[hh] += fmaxf(__fmul_rn(qd, mnv), __fmul_rn(qd, mxv));
       }
     }
 #pragma unroll
@@ -1319,8 +1333,9 @@ static int sparse_gather_run(const bd_tensor* q, const bd_tensor* k, const bd_te
           : ((rc = check_tensor(em, "m", 2, BD_F32)) || (rc = check_tensor(el, "l", 2, BD_F32)) ||
              (rc = check_tensor(eo, "o", 3, BD_F32))))
     return rc;
-  if (k->dtype != v->dtype || (k->dtype != BD_BF16 && k->dtype != BD_F8E4M3))
-    return fail(BD_ERR_DTYPE, "k and v must both be bf16 or both fp8 e4m3");
+  if (k->dtype != v->dtype ||
+      (k->dtype != BD_BF16 && k->dtype != BD_F8E4M3 && k->dtype != BD_F16 && k->dtype != BD_F32))
+    return fail(BD_ERR_DTYPE, "k and v must share one dtype: bf16, fp8 e4m3, f16 or f32");
   if (idx->dtype != BD_I32 && idx->dtype != BD_I64) return fail(BD_ERR_DTYPE, "idx must be int32 or int64");
   if (q->dtype != BD_BF16 && q->dtype != BD_F16 && q->dtype != BD_F32) return fail(BD_ERR_DTYPE, "q must be bf16/f16/f32");
   const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
@@ -1369,17 +1384,16 @@ static int sparse_gather_run(const bd_tensor* q, const bd_tensor* k, const bd_te
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(nsplit, unsigned(Hq), unsigned(B));
-  const bool fp8 = k->dtype == BD_F8E4M3;
-  if (D == 128) {
-    rc = launch_programmatic(fp8 ? gather_attn_kernel<128, true> : gather_attn_kernel<128, false>, grid, dim3(128), 0,
-                             st, p, "gather_attn_kernel launch");
-  } else if (D == 64) {
-    rc = launch_programmatic(fp8 ? gather_attn_kernel<64, true> : gather_attn_kernel<64, false>, grid, dim3(128), 0,
-                             st, p, "gather_attn_kernel launch");
-  } else {
-    rc = launch_programmatic(fp8 ? gather_attn_kernel<32, true> : gather_attn_kernel<32, false>, grid, dim3(128), 0,
-                             st, p, "gather_attn_kernel launch");
-  }
+  const int kv = k->dtype == BD_F8E4M3 ? kGvFp8 : k->dtype == BD_F16 ? kGvF16 : k->dtype == BD_F32 ? kGvF32 : kGvBf16;
+  auto pick = [&](auto d) {
+    constexpr int DD = decltype(d)::value;
+    return kv == kGvFp8 ? gather_attn_kernel<DD, kGvFp8>
+         : kv == kGvF16 ? gather_attn_kernel<DD, kGvF16>
+         : kv == kGvF32 ? gather_attn_kernel<DD, kGvF32> : gather_attn_kernel<DD, kGvBf16>;
+  };
+  auto kern = D == 128 ? pick(std::integral_constant<int, 128>{})
+            : D == 64 ? pick(std::integral_constant<int, 64>{}) : pick(std::integral_constant<int, 32>{});
+  rc = launch_programmatic(kern, grid, dim3(128), 0, st, p, "gather_attn_kernel launch");
   if (rc) return rc;
   if (direct) return BD_OK;
   if (out) return launch_combine(part, int(B), int(Hq), int(D), out, st, true);
@@ -1443,9 +1457,12 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
                          int force_from_page, const bd_tensor* bounds, bd_stream_t stream) {
   using namespace bd;
   int rc;
-  if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(kmin, "kmin", 4, BD_BF16)) ||
-      (rc = check_tensor(kmax, "kmax", 4, BD_BF16)) || (rc = check_tensor(bounds, "bounds", 3, BD_F32)))
+  if ((rc = check_tensor(q, "q", 3)) || (rc = check_tensor(kmin, "kmin", 4)) ||
+      (rc = check_tensor(kmax, "kmax", 4, kmin->dtype)) || (rc = check_tensor(bounds, "bounds", 3, BD_F32)))
     return rc;
+  if (kmin->dtype != BD_BF16 && kmin->dtype != BD_F16 && kmin->dtype != BD_F32)
+    return fail(BD_ERR_DTYPE, "kmin/kmax must be bf16, f16 or f32");
+  if (q->dtype != BD_BF16 && q->dtype != BD_F16 && q->dtype != BD_F32) return fail(BD_ERR_DTYPE, "q must be bf16/f16/f32");
   const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
   const int64_t Hk = kmin->shape[1], np = kmin->shape[2];
   if (Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "H_q must be a multiple of H_k");
@@ -1463,9 +1480,10 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   auto* mn = static_cast<const __nv_bfloat16*>(kmin->data);
   auto* mx = static_cast<const __nv_bfloat16*>(kmax->data);
-  // bf16 query with 4-byte aligned channel pairs: tensor-core bounds
-  if (q->dtype == BD_BF16 && (reinterpret_cast<uintptr_t>(q->data) & 3) == 0 && (q->stride[0] % 2) == 0 &&
-      (q->stride[1] % 2) == 0) {
+  // bf16 query and metadata with 4-byte aligned channel pairs: tensor-core bounds (bf16
+  // products are exact in fp32)
+  if (kmin->dtype == BD_BF16 && q->dtype == BD_BF16 && (reinterpret_cast<uintptr_t>(q->data) & 3) == 0 &&
+      (q->stride[0] % 2) == 0 && (q->stride[1] % 2) == 0) {
     QuestMmaParams p{};
     p.q = static_cast<const __nv_bfloat16*>(q->data); p.q_sb = q->stride[0]; p.q_sh = q->stride[1];
     p.kmin = mn; p.kmax = mx; p.m_sb = kmin->stride[0]; p.m_sh = kmin->stride[1]; p.m_sp = kmin->stride[2];
@@ -1494,11 +1512,19 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
     if (D == 64) return launch(quest_bounds_mma_kernel<64>);
     return launch(quest_bounds_mma_kernel<32>);
   }
-  dim3 grid(unsigned((np + kQPages - 1) / kQPages), unsigned(Hk), unsigned(B));
-  auto kern = D == 128 ? quest_bounds_kernel<128> : D == 64 ? quest_bounds_kernel<64> : quest_bounds_kernel<32>;
-  return launch_pdl(kern, grid, dim3(kQPages), 0, st, "quest_bounds_kernel launch", q->data, q->dtype, q->stride[0],
-                    q->stride[1], mn, mx, kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np),
-                    scaling, force_from_page, static_cast<float*>(bounds->data));
+  auto run = [&](auto tag) {
+    using MT = decltype(tag);
+    constexpr int NP = sizeof(MT) == 4 ? kQPages / 2 : kQPages;
+    dim3 grid(unsigned((np + NP - 1) / NP), unsigned(Hk), unsigned(B));
+    auto kern = D == 128 ? quest_bounds_kernel<128, MT> : D == 64 ? quest_bounds_kernel<64, MT> : quest_bounds_kernel<32, MT>;
+    return launch_pdl(kern, grid, dim3(NP), 0, st, "quest_bounds_kernel launch", q->data, q->dtype, q->stride[0],
+                      q->stride[1], static_cast<const MT*>(kmin->data), static_cast<const MT*>(kmax->data),
+                      kmin->stride[0], kmin->stride[1], kmin->stride[2], int(Hq), int(Hk), int(np), scaling,
+                      force_from_page, static_cast<float*>(bounds->data));
+  };
+  if (kmin->dtype == BD_F32) return run(float{});
+  if (kmin->dtype == BD_F16) return run(__half{});
+  return run(__nv_bfloat16{});
 }
 
 size_t bd_quest_select_workspace(const bd_tensor* q, const bd_tensor* kmin, int kb, int page) {

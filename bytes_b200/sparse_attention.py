@@ -42,10 +42,12 @@ def select_topk(selector, q_blk, sel_keys, q_pos, S, kb, k_chunk, scaling, page=
     B, Hq, _, D = q_blk.shape
     keys = sel_keys[:, :, :S]
     q3 = q_blk[:, :, 0, :]
-    if keys.dtype != torch.bfloat16:
-        keys = keys.to(torch.bfloat16)
-    if q3.dtype != torch.bfloat16:
-        q3 = q3.to(torch.bfloat16)
+    # scores in fp32 from the unrounded inputs, like the reference's fp32 score tiles
+    # (bf16 query and keys on the tensor cores, where every product is exact)
+    if keys.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        keys = keys.float()
+    if q3.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        q3 = q3.float()
     scores = _ops.sparse_score(q3, keys, None, None, scaling, 16, 32)
     kk = min(kb, S)
     _, idx = _ops.topk(scores, kk, sorted=True, want_values=False)
@@ -105,10 +107,12 @@ def attend_topk(q_blk, k_r, v, idx, q_pos, scaling):
     S = k_r.shape[2]
     _decode_row(q_blk, q_pos, S)
     q3 = q_blk[:, :, 0, :]
-    out = torch.empty(q3.shape, dtype=v.dtype, device=q3.device)
+    odt = v.dtype if v.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32
+    out = torch.empty(q3.shape, dtype=odt, device=q3.device)
     kk, vv = k_r, v
-    if kk.dtype not in (torch.bfloat16, torch.float8_e4m3fn):
-        kk = kk.to(torch.bfloat16)
-        vv = vv.to(torch.bfloat16)
+    if kk.dtype not in (torch.bfloat16, torch.float16, torch.float32, torch.float8_e4m3fn) or kk.dtype != vv.dtype:
+        kk, vv = kk.float(), vv.float()
+    if q3.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        q3 = q3.float()
     _ops.gather_attn(q3, kk, vv, idx[:, :, 0, :], scaling, out)
-    return out.unsqueeze(2)
+    return out.to(v.dtype).unsqueeze(2)

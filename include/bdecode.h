@@ -206,10 +206,13 @@ int bd_kivi_gemv_outer(int group_size, const bd_tensor* fA, const bd_tensor* qB,
 
 /* ---------------------------------------------------------------------------
  * Pass-1 scores [B,Hq,S] f32 = scaling * q.k over all keys.
- * score_bits 16: k bf16 [B,Hk,S,D];  8: k fp8 e4m3 [B,Hk,S,D];
+ * score_bits 16: k bf16, f16 or f32 [B,Hk,S,D];  8: k fp8 e4m3 [B,Hk,S,D];
  * 4 / 2: k uint8 [B,Hk,S,D*bits/8] (channel c at byte c/(8/bits), shift
  * (c%(8/bits))*bits), key = code*scale + zero with scale/zero bf16 or f16
- * [B,Hk,S,D/group_size] (token-major, contiguous per (b,h)).
+ * [B,Hk,S,D/group_size] (token-major, contiguous per (b,h)). q bf16/f16/f32.
+ * A bf16 query over bf16 keys, or a bf16/f16 query over fp8 or packed keys, runs on
+ * the tensor cores (products exact in fp32); an fp32 query, an f16 query over bf16
+ * keys and f16/f32 keys run in fp32 on the CUDA cores, unrounded.
  * ref: sparse_score_scalar  src/attention_kernels.py:1113
  *      sparse_score_packed  src/attention_kernels.py:1199 */
 int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* scale, const bd_tensor* zero,
@@ -235,8 +238,9 @@ int bd_topk(const bd_tensor* scores, int k, int sorted, const bd_tensor* values,
 
 /* Exact softmax(scaling * q.k_sel) . v_sel over per-query-head key positions
  * idx [B,Hq,kb] (int32/int64; duplicates count once per occurrence, positions
- * outside [0,S) are skipped). q [B,Hq,D]; k,v [B,Hk,S,D] bf16 or fp8 e4m3;
- * out [B,Hq,D] (bf16 for fp8 values in the reference).
+ * outside [0,S) are skipped). q [B,Hq,D] bf16/f16/f32; k,v [B,Hk,S,D] of one
+ * dtype: bf16, fp8 e4m3, f16 or f32 (widened to fp32); out [B,Hq,D] bf16/f16/f32
+ * (bf16 for fp8 values in the reference).
  * ref: sparse_gather_attn  src/attention_kernels.py:1037; attend_topk
  *      benchmarks/sparse_attention.py:367 */
 size_t bd_sparse_gather_attn_workspace(const bd_tensor* q, const bd_tensor* idx);
@@ -266,7 +270,8 @@ int bd_quest_page_minmax(const bd_tensor* k, int page, const bd_tensor* kmin, co
                          bd_stream_t stream);
 /* bound[b,hq,p] = scaling * sum_d max(q_d*kmin_pd, q_d*kmax_pd) (fp32), with
  * pages p >= force_from_page set to +inf (the reference's forced recent window;
- * pass a value >= np for none). kmin/kmax bf16 [B,Hk,np,D]; bounds f32 [B,Hq,np].
+ * pass a value >= np for none). kmin/kmax [B,Hk,np,D] bf16, f16 or f32 (both one
+ * dtype, read unrounded); q bf16/f16/f32; bounds f32 [B,Hq,np].
  * ref: benchmarks/sparse_attention.py:342-355 */
 int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_tensor* kmax, float scaling,
                          int force_from_page, const bd_tensor* bounds, bd_stream_t stream);

@@ -19,6 +19,7 @@ positions). Skipped when the install is absent.
 import importlib.util
 import math
 import os
+import sys
 
 import pytest
 import torch
@@ -30,7 +31,8 @@ from bytes_b200 import quantization as qz
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_SRC = os.path.join(ROOT, "baseline", "_ref", "src")
+REF_ROOT = os.path.join(ROOT, "baseline", "_ref")
+REF_SRC = os.path.join(REF_ROOT, "src")
 
 
 def _load(name, fname):
@@ -51,6 +53,30 @@ def ref(cuda):
 @pytest.fixture(scope="module")
 def ref_q(cuda):
     return _load("_reference_quantization", "quantization.py")
+
+
+@pytest.fixture(scope="module")
+def ref_sa(cuda):
+    """benchmarks/sparse_attention.py of the reference (it imports src.quantization; the
+    reference's own ``src`` package is importable only while the module loads)."""
+    path = os.path.join(REF_ROOT, "benchmarks", "sparse_attention.py")
+    if not os.path.isfile(path):
+        pytest.skip("reference install (baseline/_ref) not present")
+    owned = lambda k: k == "src" or k.startswith("src.")
+    saved = {k: v for k, v in sys.modules.items() if owned(k)}
+    for k in saved:
+        del sys.modules[k]
+    sys.path.insert(0, REF_ROOT)
+    try:
+        spec = importlib.util.spec_from_file_location("_reference_sparse_attention", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        sys.path.remove(REF_ROOT)
+        for k in [k for k in sys.modules if owned(k)]:
+            del sys.modules[k]
+        sys.modules.update(saved)
+    return mod
 
 
 def gen(seed):
@@ -351,3 +377,88 @@ def test_sparse_decode_chain(ref, cuda, bits):
     ours = ak.sparse_decode_scalar(q, ks, s_, z_, k, v, frac, scaling, score_bits=bits, group_size=32)
     theirs = ref.sparse_decode_scalar(q, ks, s_, z_, k, v, frac, scaling, score_bits=bits, group_size=32)
     same(ours, theirs, max_abs=2e-2, mean_abs=1e-3)
+
+
+def _clear_rows(scores, k, margin=1e-4):
+    v = scores.sort(-1, descending=True).values
+    return (v[..., k - 1] - v[..., k]) > margin
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_select_topk_exact_vs_reference(ref_sa, cuda, dt):
+    """select_topk('exact') of benchmarks/sparse_attention.py:226-325 on the GPU: the same
+    key set on every row whose cut-off is not a near-tie."""
+    from bytes_b200 import sparse_attention as sa
+    g = gen(120)
+    B, Hq, S, D, kb = 2, 8, 3000, 128, 150
+    q = torch.randn(B, Hq, 1, D, generator=g).to(dt)
+    keys = torch.randn(B, Hq, S, D, generator=g).to(dt)
+    pos = torch.tensor([S - 1])
+    theirs = ref_sa.select_topk("exact", q.to(cuda), keys.to(cuda), pos.to(cuda), S, kb, 512, 0.088)
+    ours = sa.select_topk("exact", q.to(cuda), keys.to(cuda), pos, S, kb, 512, 0.088)
+    assert ours.shape == theirs.shape
+    sc = torch.einsum("bhqd,bhsd->bhqs", q.float(), keys.float()) * 0.088
+    ok = _clear_rows(sc, kb)
+    assert ok.float().mean() > 0.5
+    a, b = ours.cpu().sort(-1).values, theirs.cpu().sort(-1).values
+    assert torch.equal(a[ok], b[ok])
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_quest_select_vs_reference(ref_sa, cuda, dt):
+    """_quest_select (benchmarks/sparse_attention.py:328-364) on the GPU: the same pages on
+    every row whose page cut-off is not a near-tie."""
+    from bytes_b200 import sparse_attention as sa
+    g = gen(121)
+    B, Hq, S, D, page, kb = 2, 8, 1000, 128, 16, 160
+    q = torch.randn(B, Hq, 1, D, generator=g).to(dt)
+    kr = (torch.randn(B, Hq, S, D, generator=g) * 2).to(dt)
+    pos = torch.tensor([S - 1])
+    theirs = ref_sa._quest_select(q.to(cuda), kr.to(cuda), pos.to(cuda), S, kb, page, 0.088)
+    ours = sa._quest_select(q.to(cuda), kr.to(cuda), pos, S, kb, page, 0.088)
+    assert ours.shape == theirs.shape
+    kmin, kmax = oracle.quest_page_minmax(kr, page)
+    rb = oracle.quest_page_bounds(q, kmin, kmax, 0.088)
+    ok = _clear_rows(rb, kb // page)
+    assert ok.float().mean() > 0.5
+    a, b = ours.cpu()[:, :, 0].sort(-1).values, theirs.cpu()[:, :, 0].sort(-1).values
+    assert torch.equal(a[ok], b[ok])
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_attend_topk_vs_reference(ref_sa, cuda, dt):
+    """attend_topk (benchmarks/sparse_attention.py:367-387) over the same selection, sentinel
+    slots included. The reference rounds a bf16 call's softmax weights to bf16 before the
+    weighted sum, hence the wider bf16 tolerance."""
+    from bytes_b200 import sparse_attention as sa
+    g = gen(122)
+    B, Hq, S, D, ks = 2, 4, 600, 128, 48
+    q = torch.randn(B, Hq, 1, D, generator=g).to(dt)
+    k = torch.randn(B, Hq, S, D, generator=g).to(dt)
+    v = torch.randn(B, Hq, S, D, generator=g).to(dt)
+    idx = torch.randint(0, S, (B, Hq, 1, ks), generator=g)
+    idx[0, 1, 0, :5] = S
+    pos = torch.tensor([S - 1])
+    args = [t.to(cuda) for t in (q, k, v, idx)]
+    theirs = ref_sa.attend_topk(*args, pos.to(cuda), 0.088)
+    ours = sa.attend_topk(*args, pos, 0.088)
+    if dt == torch.float32:
+        same(ours, theirs, max_abs=1e-4, mean_abs=1e-5)
+    else:
+        same(ours, theirs, max_abs=2e-2, mean_abs=2e-3)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16])
+def test_full_precision_scores_and_gather_vs_reference(ref, cuda, dt):
+    """The reference's Triton score and gather kernels on fp32 / f16 inputs (they widen
+    every load to fp32) against this engine's unrounded paths."""
+    g = gen(123)
+    B, Hq, Hk, S, D, kb = 2, 8, 2, 2000, 128, 100
+    q = torch.randn(B, Hq, 1, D, generator=g).to(dt).to(cuda)
+    k = torch.randn(B, Hk, S, D, generator=g).to(dt).to(cuda)
+    v = torch.randn(B, Hk, S, D, generator=g).to(dt).to(cuda)
+    same_scores(ak.sparse_score_scalar(q, k, 0.088), ref.sparse_score_scalar(q, k, 0.088))
+    idx = torch.randint(0, S, (B, Hq, kb), generator=g).to(cuda)
+    tol = 1e-4 if dt == torch.float32 else 2e-3
+    same(ak.sparse_gather_attn(q, k, v, idx, 0.088), ref.sparse_gather_attn(q, k, v, idx, 0.088),
+         max_abs=tol, mean_abs=tol / 10)
