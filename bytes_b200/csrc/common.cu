@@ -18,6 +18,9 @@ int fail(int status, const std::string& msg) {
 
 int cuda_check(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return BD_OK;
+  // a launch that the runtime refused also left its code as the thread's last error; clear
+  // it so the next call's launch check does not report this one's failure again
+  (void)cudaGetLastError();
   return fail(BD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 

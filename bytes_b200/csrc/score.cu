@@ -537,7 +537,7 @@ int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* sca
   const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
   const int64_t Hk = k->shape[1], S = k->shape[2];
   if (k->shape[0] != B || Hk <= 0 || Hq % Hk) return fail(BD_ERR_SHAPE, "k must be [B,Hk,S,*] with Hq % Hk == 0");
-  if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (D != 32 && D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 32, 64 or 128");
   int kt;
   if (score_bits == 16) {
     if ((k->dtype != BD_BF16 && k->dtype != BD_F16 && k->dtype != BD_F32) || k->shape[3] != D)
@@ -592,12 +592,15 @@ int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* sca
   p.scaling = scaling;
   // inputs the tensor-core operands would round (fp32 query; f16 query against bf16 keys;
   // f16 / fp32 keys) take the fp32 CUDA-core kernel
-  const bool generic = q->dtype == BD_F32 || (kt == 16 && (k->dtype != BD_BF16 || q->dtype != BD_BF16));
+  // (and head_dim 32, which the tensor-core tiles do not cover)
+  const bool generic =
+      D == 32 || q->dtype == BD_F32 || (kt == 16 && (k->dtype != BD_BF16 || q->dtype != BD_BF16));
   if (generic) {
     const int kind = kt == 16 ? (k->dtype == BD_BF16 ? kGkBf16 : k->dtype == BD_F16 ? kGkF16 : kGkF32)
                               : kt == 8 ? kGkFp8 : kt == 4 ? kGkPack4 : kGkPack2;
     cudaStream_t gst = reinterpret_cast<cudaStream_t>(stream);
-    return D == 128 ? launch_score_generic<128>(p, kind, gst) : launch_score_generic<64>(p, kind, gst);
+    return D == 128 ? launch_score_generic<128>(p, kind, gst)
+                    : D == 64 ? launch_score_generic<64>(p, kind, gst) : launch_score_generic<32>(p, kind, gst);
   }
   const int64_t tt = tile_tokens(kt);
   const int64_t ntiles = (S + tt - 1) / tt;

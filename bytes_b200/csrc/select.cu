@@ -1497,14 +1497,16 @@ int bd_quest_page_bounds(const bd_tensor* q, const bd_tensor* kmin, const bd_ten
     dim3 gm(unsigned((nblk + p.blocks_per_cta - 1) / p.blocks_per_cta), unsigned(Hk * p.head_chunks), unsigned(B));
     const size_t smem = size_t(2) * kQmPages * (4 * D + 16);
     auto launch = [&](auto kern) {
-      static bool attr[64] = {false};
+      // one flag per head_dim instance and device: the instances need different sizes
+      static bool attr[3][64] = {};
+      const int di = D == 128 ? 2 : D == 64 ? 1 : 0;
       int dev = 0;
       cudaGetDevice(&dev);
-      if (!attr[dev & 63]) {
+      if (!attr[di][dev & 63]) {
         const int r = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
                                  "cudaFuncSetAttribute(quest_bounds)");
         if (r) return r;
-        attr[dev & 63] = true;
+        attr[di][dev & 63] = true;
       }
       return launch_programmatic(kern, gm, dim3(128), smem, st, p, "quest_bounds_mma_kernel launch");
     };

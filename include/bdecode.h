@@ -212,7 +212,8 @@ int bd_kivi_gemv_outer(int group_size, const bd_tensor* fA, const bd_tensor* qB,
  * [B,Hk,S,D/group_size] (token-major, contiguous per (b,h)). q bf16/f16/f32.
  * A bf16 query over bf16 keys, or a bf16/f16 query over fp8 or packed keys, runs on
  * the tensor cores (products exact in fp32); an fp32 query, an f16 query over bf16
- * keys and f16/f32 keys run in fp32 on the CUDA cores, unrounded.
+ * keys, f16/f32 keys and head_dim 32 run in fp32 on the CUDA cores, unrounded.
+ * head_dim 32, 64 or 128.
  * ref: sparse_score_scalar  src/attention_kernels.py:1113
  *      sparse_score_packed  src/attention_kernels.py:1199 */
 int bd_sparse_score(const bd_tensor* q, const bd_tensor* k, const bd_tensor* scale, const bd_tensor* zero,

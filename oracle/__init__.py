@@ -65,4 +65,8 @@ from .select import (  # noqa: F401
     quest_select,
     quest_select_from_meta,
     attend_topk,
+    select_topk_exact_window,
+    quest_bounds_window,
+    quest_select_window,
+    sparse_attention_chunked,
 )

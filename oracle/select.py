@@ -1,9 +1,11 @@
 """fp32 CPU restatement of the reference's selection primitives (test oracle only).
 
 References: ``benchmarks/sparse_attention.py`` (select_topk, _quest_select,
-attend_topk) and the ``scores.topk`` calls of ``src/attention_kernels.py``.
-Decode-shaped: one query row per (batch, head) at position S-1, so every cached key
-is causally valid.
+attend_topk, sparse_attention_chunked) and the ``scores.topk`` calls of
+``src/attention_kernels.py``. The decode-shaped functions take one query row per
+(batch, head) at position S-1 (every cached key causally valid); the ``*_window`` forms take
+a block of query rows at positions q_pos with per-row causal limits, as the reference's
+prefill loop does.
 """
 import torch
 
@@ -112,3 +114,78 @@ def attend_topk(q, k_r, v, idx, q_pos, scaling):
     sc = torch.where(valid, sc, torch.full_like(sc, NEG_INF))
     w = torch.softmax(sc, dim=-1)
     return (w.unsqueeze(-1) * vs).sum(3).to(v.dtype)
+
+
+def select_topk_exact_window(q, sel_keys, q_pos, S, kb, scaling, local_w=0):
+    """``select_topk('exact', ...)`` over a block of query rows.
+
+    benchmarks/sparse_attention.py:287-309: fp32 scores q.k*scaling of the causal keys
+    (position <= the row's q_pos), the most recent local_w causal keys forced in (:253-262),
+    top-kb with the lower index first on equal scores (the streaming merge keeps earlier
+    candidates first); slots no causal key fills hold the sentinel S (:292-293).
+    q [B,Hq,Qc,D], sel_keys [B,Hq,S,D], q_pos [Qc] -> [B,Hq,Qc,kb] int64.
+    """
+    sc = torch.einsum("bhqd,bhsd->bhqs", q.float(), sel_keys[:, :, :S].float()) * scaling
+    kpos = torch.arange(S)
+    pos = q_pos.reshape(-1)
+    sc = sc.masked_fill(kpos[None, None, None, :] > pos[None, None, :, None], NEG_INF)
+    if local_w > 0:
+        rec = (kpos[None, :] > (pos[:, None] - local_w)) & (kpos[None, :] <= pos[:, None])
+        sc = sc.masked_fill(rec[None, None], float("inf"))
+    kk = min(kb, S)
+    vals, idx = topk_lower_index(sc, kk)
+    idx = torch.where(vals == NEG_INF, torch.full_like(idx, S), idx)
+    if kb > kk:
+        idx = torch.cat([idx, torch.full(idx.shape[:-1] + (kb - kk,), S, dtype=torch.long)], dim=-1)
+    return idx
+
+
+def quest_bounds_window(q, k_r, q_pos, S, page, scaling, local_w=0):
+    """Page bounds of _quest_select over a block of query rows (benchmarks/sparse_attention.py:
+    334-355): pages starting after a row's position -inf, pages overlapping the row's recent
+    window (p-local_w, p] +inf. q [B,Hq,Qc,D], k_r [B,Hq,S,D] -> [B,Hq,Qc,np] fp32."""
+    kmin, kmax = quest_page_minmax(k_r[:, :, :S], page)
+    qf = q.float()[:, :, :, None, :]
+    bound = torch.maximum(qf * kmin.float()[:, :, None], qf * kmax.float()[:, :, None]).sum(-1) * scaling
+    np_ = bound.shape[-1]
+    pos = q_pos.reshape(-1)
+    pstart = torch.arange(np_) * page
+    bound = bound.masked_fill(pstart[None, None, None, :] > pos[None, None, :, None], NEG_INF)
+    if local_w > 0:
+        pg = torch.arange(np_)
+        lo = (pos - local_w + 1).clamp(min=0) // page
+        hi = pos // page
+        rec = (pg[None, :] >= lo[:, None]) & (pg[None, :] <= hi[:, None])
+        bound = bound.masked_fill(rec[None, None], float("inf"))
+    return bound
+
+
+def quest_select_window(q, k_r, q_pos, S, kb, page, scaling, local_w=0):
+    """_quest_select over a block of query rows (benchmarks/sparse_attention.py:328-364):
+    top npick = min(max(1, ceil(kb/page)), np) pages by bound (lower page first on ties),
+    expanded to token indices clamped to S-1. -> [B,Hq,Qc,npick*page] int64."""
+    bound = quest_bounds_window(q, k_r, q_pos, S, page, scaling, local_w)
+    np_ = bound.shape[-1]
+    npick = min(max(1, (kb + page - 1) // page), np_)
+    _, pidx = topk_lower_index(bound, npick)
+    return _expand_pages(pidx, page, S)
+
+
+def sparse_attention_chunked(q_r, k_r, v, selector, frac, n_kv_groups, scaling, page=16, q_chunk=256, local_w=0):
+    """The reference's chunked prefill loop (benchmarks/sparse_attention.py:463-497) for the
+    'exact' and 'quest' selectors, in fp32."""
+    B, Hq, S, D = q_r.shape
+    kb = max(1, int(round(frac * S)))
+    kfull = k_r.repeat_interleave(n_kv_groups, dim=1)
+    vfull = v.repeat_interleave(n_kv_groups, dim=1)
+    out = torch.empty(q_r.shape, dtype=v.dtype)
+    for q0 in range(0, S, q_chunk):
+        q1 = min(q0 + q_chunk, S)
+        q_blk = q_r[:, :, q0:q1]
+        pos = torch.arange(q0, q1)
+        if selector == "exact":
+            idx = select_topk_exact_window(q_blk, kfull, pos, S, kb, scaling, local_w)
+        else:
+            idx = quest_select_window(q_blk, kfull, pos, S, kb, page, scaling, local_w)
+        out[:, :, q0:q1] = attend_topk(q_blk, kfull, vfull, idx, pos, scaling)
+    return out

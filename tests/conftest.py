@@ -26,6 +26,25 @@ def golden_cuda():
 
 
 @pytest.fixture(scope="session")
+def golden_window():
+    """The reference's selection code over prefill windows (tests/golden/make_golden_window.py)."""
+    return torch.load(os.path.join(ROOT, "tests", "golden", "golden_window.pt"))
+
+
+def valid_sets(idx, q_pos, S):
+    """Per query row, the sorted set of causal in-range positions of an index tensor
+    [..., Qc, k] (slots the reference fills with a sentinel or with -inf-tied future keys
+    carry no weight and are dropped)."""
+    out = []
+    flat = idx.reshape(-1, idx.shape[-2], idx.shape[-1])
+    for m in range(flat.shape[0]):
+        for r in range(flat.shape[1]):
+            row = flat[m, r]
+            out.append(sorted(set(int(x) for x in row[(row <= int(q_pos[r])) & (row < S) & (row >= 0)])))
+    return out
+
+
+@pytest.fixture(scope="session")
 def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")

@@ -462,3 +462,20 @@ def test_full_precision_scores_and_gather_vs_reference(ref, cuda, dt):
     tol = 1e-4 if dt == torch.float32 else 2e-3
     same(ak.sparse_gather_attn(q, k, v, idx, 0.088), ref.sparse_gather_attn(q, k, v, idx, 0.088),
          max_abs=tol, mean_abs=tol / 10)
+
+
+@pytest.mark.parametrize("selector", ["exact", "quest"])
+def test_sparse_attention_chunked_vs_reference(ref_sa, cuda, selector):
+    """The reference's own chunked prefill loop (benchmarks/sparse_attention.py:463-497) on the
+    GPU against this engine's, fp32 inputs (bf16 values)."""
+    from bytes_b200 import sparse_attention as sa
+    g = gen(124)
+    B, Hq, Hk, S, D = 1, 8, 2, 768, 64
+    q = torch.randn(B, Hq, S, D, generator=g).bfloat16().float().to(cuda)
+    k = torch.randn(B, Hk, S, D, generator=g).bfloat16().float().to(cuda)
+    v = torch.randn(B, Hk, S, D, generator=g).bfloat16().float().to(cuda)
+    theirs = ref_sa.sparse_attention_chunked(q, k, v, None, selector, 0.1, Hq // Hk, 0.125, page=16, q_chunk=256)
+    ours = sa.sparse_attention_chunked(q, k, v, None, selector, 0.1, Hq // Hk, 0.125, page=16, q_chunk=256)
+    d = (ours - theirs).abs()
+    assert d.mean().item() <= 1e-4, d.mean().item()
+    assert (d.amax(-1) > 1e-3).float().mean().item() <= 2e-3

@@ -7,6 +7,7 @@ import pytest
 import torch
 
 import oracle
+from bytes_b200 import _ops
 from bytes_b200 import attention_kernels as ak
 from bytes_b200 import sparse_attention as sa
 
@@ -318,3 +319,17 @@ def test_sharded_sparse_decode_matches_single_device(cuda):
         ms.append(m); ls.append(l); os_.append(o)
     out = _ops.lse_combine(torch.stack(ms), torch.stack(ls), torch.stack(os_), torch.bfloat16)
     close(out.unsqueeze(2), ref, max_abs=1e-2, mean_abs=1e-4)
+
+
+def test_quest_bounds_every_head_dim_in_one_process(cuda):
+    """The tensor-core bound kernel has one instance per head_dim, each with its own shared
+    memory size: calls at 32, 128 and 64 in a row must each launch (and match the oracle)."""
+    g = gen(31)
+    for D in (32, 128, 64):
+        B, Hq, Hk, S, page = 2, 8, 2, 640, 16
+        q = torch.randn(B, Hq, 1, D, generator=g).bfloat16()
+        k = torch.randn(B, Hk, S, D, generator=g).bfloat16()
+        kmin, kmax = oracle.quest_page_minmax(k, page)
+        bounds = _ops.quest_page_bounds(q[:, :, 0].to(cuda), kmin.to(cuda), kmax.to(cuda), 0.125)
+        ref = oracle.quest_page_bounds(q, kmin, kmax, 0.125)
+        assert torch.allclose(bounds.cpu(), ref, rtol=1e-5, atol=1e-4), (D, (bounds.cpu() - ref).abs().max())

@@ -13,6 +13,7 @@ import math
 import torch
 
 import oracle
+from conftest import valid_sets
 
 
 def test_pack_score_keys_bit_exact(golden):
@@ -183,3 +184,42 @@ def test_lse_combine_equals_dense():
     comb = oracle.lse_combine(m, l, o)
     ref = oracle.decode_attn_dense(q, k, v, 0.125, out_dtype=torch.float32)[:, :, 0]
     assert torch.allclose(comb, ref, atol=1e-5, rtol=1e-5)
+
+
+def _near_tie_rows(scores, kb, tol=1e-5):
+    """Rows whose kb-th and (kb+1)-th largest finite scores agree within tol."""
+    v = scores.sort(-1, descending=True).values
+    if v.shape[-1] <= kb:
+        return torch.zeros(v.shape[:-1], dtype=torch.bool)
+    a, b = v[..., kb - 1], v[..., kb]
+    return torch.isfinite(a) & torch.isfinite(b) & ((a - b).abs() <= tol)
+
+
+def test_select_exact_window_matches_reference(golden_window):
+    for c in golden_window["select_exact_window"]:
+        q, keys = c["q"].float(), c["keys"].float()
+        idx = oracle.select_topk_exact_window(q, keys, c["q_pos"], c["S"], c["kb"], c["scaling"], c["local_w"])
+        assert idx.shape == c["idx"].shape
+        sc = torch.einsum("bhqd,bhsd->bhqs", q, keys) * c["scaling"]
+        tie = _near_tie_rows(sc, c["kb"]).reshape(-1)
+        a, b = valid_sets(idx, c["q_pos"], c["S"]), valid_sets(c["idx"], c["q_pos"], c["S"])
+        assert all(x == y or t for x, y, t in zip(a, b, tie.tolist()))
+        assert tie.float().mean() < 0.05
+
+
+def test_quest_window_matches_reference(golden_window):
+    for c in golden_window["quest_window"]:
+        q, k_r = c["q"].float(), c["k_r"].float()
+        idx = oracle.quest_select_window(q, k_r, c["q_pos"], c["S"], c["kb"], c["page"], c["scaling"], c["local_w"])
+        assert idx.shape == c["idx"].shape
+        assert valid_sets(idx, c["q_pos"], c["S"]) == valid_sets(c["idx"], c["q_pos"], c["S"])
+
+
+def test_attend_and_chunked_window_match_reference(golden_window):
+    for c in golden_window["attend_window"]:
+        o = oracle.attend_topk(c["q"].float(), c["k_r"].float(), c["v"].float(), c["idx"], c["q_pos"], c["scaling"])
+        assert torch.allclose(o, c["out"], rtol=1e-5, atol=1e-5, equal_nan=True)
+    for c in golden_window["chunked"]:
+        o = oracle.sparse_attention_chunked(c["q_r"].float(), c["k_r"].float(), c["v"].float(), c["selector"],
+                                            c["frac"], c["n_kv_groups"], c["scaling"], c["page"], c["q_chunk"])
+        assert torch.allclose(o, c["out"], rtol=1e-4, atol=1e-4), (o - c["out"]).abs().max()
