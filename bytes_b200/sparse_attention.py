@@ -16,6 +16,13 @@ from . import _ops
 
 NEG_INF = float("-inf")
 
+# Selectors that rank keys by an approximate key tensor the caller supplies (as
+# ``sel_keys``, or as ``sel_override`` of ``sparse_attention_chunked``); the ranking itself
+# is the exact top-k over those keys (benchmarks/sparse_attention.py:32-35, 287-309).
+SOFT_SELECTORS = ("approx", "int4", "int2", "fp8", "signvq")
+# SparQ: query channels kept for scoring, the top-r by magnitude (reference default 16)
+SPARQ_R = 16
+
 
 def repeat_kv(x, n_rep):
     """[B,H_k,S,D] -> [B,H_k*n_rep,S,D]. ref: benchmarks/sparse_attention.py:85-90."""
@@ -55,7 +62,11 @@ def _full_precision(t):
 
 
 def select_topk(selector, q_blk, sel_keys, q_pos, S, kb, k_chunk, scaling, page=16, generator=None, local_w=0):
-    """Top-kb causal key indices per query row: 'exact' (q.k scores) or 'quest' (page bounds).
+    """Top-kb causal key indices per query row.
+
+    Selectors: 'exact' (q.k scores), the soft selectors (the same exact top-k over the
+    approximate keys passed as ``sel_keys``), 'sparq' (the query cut to its SPARQ_R
+    largest-magnitude channels), 'quest' (page bounds), 'recent' and 'random'.
 
     ref: benchmarks/sparse_attention.py:226-325. q_blk [B,Hq,Qc,D]; sel_keys [B,Hq,S,D];
     q_pos [Qc] -> [B,Hq,Qc,kb] int64. Exact selection breaks ties by lower index (the
@@ -66,9 +77,26 @@ def select_topk(selector, q_blk, sel_keys, q_pos, S, kb, k_chunk, scaling, page=
     """
     if selector == "quest":
         return _quest_select(q_blk, sel_keys, q_pos, S, kb, page, scaling, local_w)
-    if selector != "exact":
-        raise ValueError(f"selector {selector!r} is not on the decode hot path")
     B, Hq, Qc, D = q_blk.shape
+    if selector == "recent":
+        # the kb most recent causal positions [p-kb+1 .. p] (clamped at 0), :265-269
+        pos = _positions(q_pos, Qc, q_blk.device)
+        idx = (pos[:, None] - torch.arange(kb, device=q_blk.device)[None, :]).clamp(min=0)
+        return idx[None, None].expand(B, Hq, Qc, kb).contiguous()
+    if selector == "random":
+        # kb uniform draws over [0, p] per row from the caller's generator, :271-276
+        pos = _positions(q_pos, Qc, q_blk.device)
+        rnd = torch.rand(B, Hq, Qc, kb, device=q_blk.device, generator=generator)
+        return (rnd * (pos[None, None, :, None].float() + 1)).long().clamp(min=0)
+    if selector == "sparq":
+        # score with the query cut to its SPARQ_R largest-magnitude channels, :281-285
+        r = min(SPARQ_R, D)
+        mag = _fold(q_blk).abs().float()
+        _, topr = _ops.topk(mag, r, sorted=False, want_values=False)
+        m = torch.zeros(mag.shape, dtype=q_blk.dtype, device=q_blk.device).scatter_(-1, topr, 1.0)
+        q_blk = q_blk * m.view(B, Hq, Qc, D)
+    elif selector != "exact" and selector not in SOFT_SELECTORS:
+        raise ValueError(f"selector {selector!r} is not on the decode hot path")
     keys = _full_precision(sel_keys[:, :, :S])
     q3 = _fold(q_blk)
     # scores in fp32 from the unrounded inputs, like the reference's fp32 score tiles
@@ -183,26 +211,29 @@ def attend_topk(q_blk, k_r, v, idx, q_pos, scaling):
 
 def sparse_attention_chunked(q_r, k_r, v, sel_override, selector, frac, n_kv_groups, scaling, page=16, q_chunk=256,
                              k_chunk=2048, generator=None, local_w=0):
-    """Chunked sparse attention over a prefill window (every position is a query), for the
-    'exact' and 'quest' selectors: per chunk of q_chunk query rows, select the top-kb causal
-    keys (kb = max(1, round(frac*S))) and attend over them exactly.
+    """Chunked sparse attention over a prefill window (every position is a query): per chunk
+    of q_chunk query rows, select the top-kb causal keys (kb = max(1, round(frac*S))) and
+    attend over them exactly.
 
     ref: benchmarks/sparse_attention.py:463-497. q_r [B,Hq,S,D]; k_r, v [B,Hk,S,D] ->
-    [B,Hq,S,D]. ``sel_override`` (approximate selection keys) belongs to the soft selectors
-    and is ignored here, as the reference ignores it for 'exact' and 'quest'.
+    [B,Hq,S,D]. Selectors as ``select_topk``; the soft selectors rank by ``sel_override``
+    [B,Hk,S,D] (approximate keys) when it is given, otherwise by the exact keys. The
+    global keep-set selectors ('h2o', 'snapkv') and the SDPA 'dense' route are not built.
     """
-    if selector not in ("exact", "quest"):
+    if selector not in ("exact", "quest", "sparq", "recent", "random") + SOFT_SELECTORS:
         raise ValueError(f"selector {selector!r} is not on the decode hot path")
     B, Hq, S, D = q_r.shape
     kb = max(1, int(round(frac * S)))
     kfull = repeat_kv(k_r, n_kv_groups)
     vfull = repeat_kv(v, n_kv_groups)
+    sel_keys = repeat_kv(sel_override, n_kv_groups) if selector in SOFT_SELECTORS and sel_override is not None \
+        else kfull
     out = torch.empty_like(q_r)
     for q0 in range(0, S, q_chunk):
         q1 = min(q0 + q_chunk, S)
         q_blk = q_r[:, :, q0:q1, :]
         q_pos = torch.arange(q0, q1, device=q_r.device)
-        idx = select_topk(selector, q_blk, kfull, q_pos, S, kb, k_chunk, scaling, page=page, generator=generator,
+        idx = select_topk(selector, q_blk, sel_keys, q_pos, S, kb, k_chunk, scaling, page=page, generator=generator,
                           local_w=local_w)
         out[:, :, q0:q1, :] = attend_topk(q_blk, kfull, vfull, idx, q_pos, scaling)
     return out

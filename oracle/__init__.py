@@ -68,5 +68,6 @@ from .select import (  # noqa: F401
     select_topk_exact_window,
     quest_bounds_window,
     quest_select_window,
+    select_topk_window,
     sparse_attention_chunked,
 )

@@ -171,21 +171,46 @@ def quest_select_window(q, k_r, q_pos, S, kb, page, scaling, local_w=0):
     return _expand_pages(pidx, page, S)
 
 
-def sparse_attention_chunked(q_r, k_r, v, selector, frac, n_kv_groups, scaling, page=16, q_chunk=256, local_w=0):
+SOFT_SELECTORS = ("approx", "int4", "int2", "fp8", "signvq")
+
+
+def select_topk_window(selector, q, sel_keys, q_pos, S, kb, scaling, page=16, local_w=0, sparq_r=16):
+    """``select_topk`` over a block of query rows for the deterministic selectors
+    (benchmarks/sparse_attention.py:226-309): 'exact' and the soft selectors (exact top-k over
+    the keys given), 'sparq' (the query cut to its sparq_r largest-magnitude channels, lower
+    channel first on equal magnitudes, then exact), 'recent' ([p-kb+1 .. p] clamped at 0)
+    and 'quest'."""
+    B, Hq, Qc, D = q.shape
+    if selector == "recent":
+        idx = (q_pos.reshape(-1)[:, None] - torch.arange(kb)[None, :]).clamp(min=0)
+        return idx[None, None].expand(B, Hq, Qc, kb).contiguous()
+    if selector == "quest":
+        return quest_select_window(q, sel_keys, q_pos, S, kb, page, scaling, local_w)
+    if selector == "sparq":
+        r = min(sparq_r, D)
+        _, topr = topk_lower_index(q.float().abs(), r)
+        q = q * torch.zeros_like(q).scatter_(-1, topr, 1.0)
+    elif selector != "exact" and selector not in SOFT_SELECTORS:
+        raise ValueError(selector)
+    return select_topk_exact_window(q, sel_keys, q_pos, S, kb, scaling, local_w)
+
+
+def sparse_attention_chunked(q_r, k_r, v, selector, frac, n_kv_groups, scaling, page=16, q_chunk=256, local_w=0,
+                             sel_override=None):
     """The reference's chunked prefill loop (benchmarks/sparse_attention.py:463-497) for the
-    'exact' and 'quest' selectors, in fp32."""
+    deterministic selectors of ``select_topk_window``, in fp32; the soft selectors rank by
+    ``sel_override`` [B,Hk,S,D] when it is given."""
     B, Hq, S, D = q_r.shape
     kb = max(1, int(round(frac * S)))
     kfull = k_r.repeat_interleave(n_kv_groups, dim=1)
     vfull = v.repeat_interleave(n_kv_groups, dim=1)
+    sel = sel_override.repeat_interleave(n_kv_groups, dim=1) \
+        if selector in SOFT_SELECTORS and sel_override is not None else kfull
     out = torch.empty(q_r.shape, dtype=v.dtype)
     for q0 in range(0, S, q_chunk):
         q1 = min(q0 + q_chunk, S)
         q_blk = q_r[:, :, q0:q1]
         pos = torch.arange(q0, q1)
-        if selector == "exact":
-            idx = select_topk_exact_window(q_blk, kfull, pos, S, kb, scaling, local_w)
-        else:
-            idx = quest_select_window(q_blk, kfull, pos, S, kb, page, scaling, local_w)
+        idx = select_topk_window(selector, q_blk, sel, pos, S, kb, scaling, page, local_w)
         out[:, :, q0:q1] = attend_topk(q_blk, kfull, vfull, idx, pos, scaling)
     return out

@@ -8,7 +8,8 @@ Runs ``benchmarks.sparse_attention`` of the reference on the CPU with fixed seed
 blocks of query rows at positions inside the context (per-row causal limits), with and
 without the forced recent window: ``select_topk('exact')``, ``_quest_select``,
 ``attend_topk`` (including sentinel and future positions) and ``sparse_attention_chunked``
-for the 'exact' and 'quest' selectors. Inputs are bf16 values (stored as bf16, passed to
+for the 'exact', 'quest', 'approx' (approximate keys as ``sel_override``), 'sparq' and
+'recent' selectors. Inputs are bf16 values (stored as bf16, passed to
 the reference as fp32), so every product is exact in fp32. Output:
 ``tests/golden/golden_window.pt``.
 """
@@ -75,6 +76,18 @@ def main():
                                      page=16, q_chunk=64, k_chunk=64)
         chunked.append(dict(selector=selector, q_r=q_r, k_r=k_r, v=v, frac=0.1, n_kv_groups=Hq // Hk,
                             scaling=0.15, page=16, q_chunk=64, out=o))
+    # the soft selectors (ranking by approximate keys passed as sel_override), SparQ and the
+    # recent window (the random selector's draws depend on the device's generator)
+    for selector in ("approx", "sparq", "recent"):
+        B, Hq, Hk, S, D = 1, 4, 2, 192, 32
+        q_r = randn(B, Hq, S, D)
+        k_r = randn(B, Hk, S, D)
+        v = randn(B, Hk, S, D)
+        approx = (k_r.float() + 0.3 * randn(B, Hk, S, D).float()).bfloat16()
+        o = sparse_attention_chunked(q_r.float(), k_r.float(), v.float(), approx.float(), selector, 0.1, Hq // Hk,
+                                     0.15, page=16, q_chunk=64, k_chunk=64)
+        chunked.append(dict(selector=selector, q_r=q_r, k_r=k_r, v=v, sel_override=approx, frac=0.1,
+                            n_kv_groups=Hq // Hk, scaling=0.15, page=16, q_chunk=64, out=o))
     out["chunked"] = chunked
 
     path = os.path.join(HERE, "golden_window.pt")

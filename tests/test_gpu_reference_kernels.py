@@ -479,3 +479,37 @@ def test_sparse_attention_chunked_vs_reference(ref_sa, cuda, selector):
     d = (ours - theirs).abs()
     assert d.mean().item() <= 1e-4, d.mean().item()
     assert (d.amax(-1) > 1e-3).float().mean().item() <= 2e-3
+
+
+@pytest.mark.parametrize("selector", ["random", "recent", "sparq", "approx"])
+def test_other_selectors_vs_reference(ref_sa, cuda, selector):
+    """The reference's select_topk for its other selectors on the GPU: 'random' from the same
+    CUDA generator state and 'recent' give the same indices; 'sparq' and a soft selector
+    ('approx', ranking approximate keys) the same key sets outside near-ties."""
+    from bytes_b200 import sparse_attention as sa
+    g = gen(125)
+    B, Hq, S, D, q0, Qc, kb = 2, 4, 500, 64, 300, 60, 40
+    q = torch.randn(B, Hq, Qc, D, generator=g).bfloat16().float().to(cuda)
+    keys = torch.randn(B, Hq, S, D, generator=g).bfloat16().float().to(cuda)
+    pos = torch.arange(q0, q0 + Qc)
+    gens = [torch.Generator(device=cuda).manual_seed(5) for _ in range(2)]
+    theirs = ref_sa.select_topk(selector, q, keys, pos.to(cuda), S, kb, 128, 0.125, generator=gens[0]).cpu()
+    ours = sa.select_topk(selector, q, keys, pos, S, kb, 128, 0.125, generator=gens[1]).cpu()
+    assert ours.shape == theirs.shape
+    if selector in ("random", "recent"):
+        assert torch.equal(ours, theirs)
+        return
+    qs = q.float().cpu()
+    if selector == "sparq":
+        _, topr = oracle.topk_lower_index(qs.abs(), ref_sa.SPARQ_R)
+        qs = qs * torch.zeros_like(qs).scatter_(-1, topr, 1.0)
+    sc = torch.einsum("bhqd,bhsd->bhqs", qs, keys.float().cpu()) * 0.125
+    sc = sc.masked_fill(torch.arange(S)[None, None, None, :] > pos[None, None, :, None], float("-inf"))
+    ok = _clear_rows(sc, kb)
+    from conftest import sparq_tie_rows, valid_sets
+    if selector == "sparq":
+        ok &= ~sparq_tie_rows(q.cpu(), ref_sa.SPARQ_R)
+    ok = ok.reshape(-1).tolist()
+    a, b = valid_sets(ours, pos, S), valid_sets(theirs, pos, S)
+    assert sum(ok) > 0.5 * len(ok)
+    assert all(x == y or not o for x, y, o in zip(a, b, ok))

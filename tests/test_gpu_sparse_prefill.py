@@ -3,7 +3,8 @@
 The reference runs select_topk / _quest_select / attend_topk over blocks of query rows at
 positions q_pos (keys causal per row, an optional forced recent window), and
 sparse_attention_chunked loops them over a whole prefill window
-(benchmarks/sparse_attention.py:226-387, 463-497). This engine folds a block's rows into the
+(benchmarks/sparse_attention.py:226-387, 463-497), for the 'exact', 'quest', soft
+(approximate-key), 'sparq', 'recent' and 'random' selectors. This engine folds a block's rows into the
 head axis and runs the decode kernels with per-row causal limits. Gates: the golden vectors
 made by running the reference's code (tests/golden/make_golden_window.py) and the fp32
 oracle; selections compared as sets of usable (causal, in-range) positions per row, exact
@@ -15,7 +16,7 @@ import torch
 
 import oracle
 from bytes_b200 import sparse_attention as sa
-from conftest import valid_sets
+from conftest import chunked_mismatch, valid_sets
 
 pytestmark = pytest.mark.gpu
 
@@ -60,9 +61,10 @@ def test_attend_window_golden(cuda, golden_window):
 def test_chunked_golden(cuda, golden_window):
     for c in golden_window["chunked"]:
         args = [c[n].float().to(cuda) for n in ("q_r", "k_r", "v")]
-        o = sa.sparse_attention_chunked(*args, None, c["selector"], c["frac"], c["n_kv_groups"], c["scaling"],
-                                        page=c["page"], q_chunk=c["q_chunk"]).cpu()
-        assert torch.allclose(o, c["out"], rtol=1e-4, atol=1e-4), (c["selector"], (o - c["out"]).abs().max())
+        so = c.get("sel_override")
+        o = sa.sparse_attention_chunked(*args, None if so is None else so.float().to(cuda), c["selector"], c["frac"],
+                                        c["n_kv_groups"], c["scaling"], page=c["page"], q_chunk=c["q_chunk"]).cpu()
+        assert chunked_mismatch(o, c["out"], c, 1e-4) <= 1e-4, c["selector"]
 
 
 @pytest.mark.parametrize("selector,local_w", [("exact", 0), ("exact", 32), ("quest", 0), ("quest", 48)])

@@ -13,7 +13,7 @@ import math
 import torch
 
 import oracle
-from conftest import valid_sets
+from conftest import chunked_mismatch, valid_sets
 
 
 def test_pack_score_keys_bit_exact(golden):
@@ -220,6 +220,8 @@ def test_attend_and_chunked_window_match_reference(golden_window):
         o = oracle.attend_topk(c["q"].float(), c["k_r"].float(), c["v"].float(), c["idx"], c["q_pos"], c["scaling"])
         assert torch.allclose(o, c["out"], rtol=1e-5, atol=1e-5, equal_nan=True)
     for c in golden_window["chunked"]:
+        so = c.get("sel_override")
         o = oracle.sparse_attention_chunked(c["q_r"].float(), c["k_r"].float(), c["v"].float(), c["selector"],
-                                            c["frac"], c["n_kv_groups"], c["scaling"], c["page"], c["q_chunk"])
-        assert torch.allclose(o, c["out"], rtol=1e-4, atol=1e-4), (o - c["out"]).abs().max()
+                                            c["frac"], c["n_kv_groups"], c["scaling"], c["page"], c["q_chunk"],
+                                            sel_override=None if so is None else so.float())
+        assert chunked_mismatch(o, c["out"], c, 1e-4) <= 1e-4, c["selector"]
