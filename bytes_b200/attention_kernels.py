@@ -17,32 +17,57 @@ def _squeeze_q(q):
     return q[:, :, 0, :]
 
 
+def _decode_all_positions(q3, k, v, out_dtype):
+    """Exact attention of each query head over every cached position through the gather
+    kernel (fp32 arithmetic on the unrounded query), for queries the tensor-core decode
+    tiles would have to round. The position list is one [S] ramp viewed with zero batch /
+    head strides."""
+    B, Hq, D = q3.shape
+    S = k.shape[2]
+    idx = torch.arange(S, dtype=torch.int32, device=q3.device).expand(B, Hq, S)
+    out = torch.empty(q3.shape, dtype=out_dtype, device=q3.device)
+    _ops.gather_attn(q3, k, v, idx, 1.0, out)
+    return out.unsqueeze(2)
+
+
 def decode_attn_bf16(q, k, v):
     """softmax(q.k) . v per query head, GQA by h_q // (H_q/H_k); NO scale is applied.
 
     ref: src/attention_kernels.py:65-92. q [B,H_q,1,D]; k,v [B,H_k,S,D] bf16
-    -> [B,H_q,1,D] in q.dtype. A non-bf16 query is rounded to bf16 for the
-    tensor-core contraction.
+    -> [B,H_q,1,D] in q.dtype. A bf16 query takes the tensor-core decode tiles (every
+    product exact in fp32); an f16 or fp32 query, which they would round, is computed in
+    fp32 over every position by the gather kernel, as the reference widens it.
     """
     if q.is_cuda and q.dtype == torch.bfloat16:
         rc, out = _ops.N.glue().decode_attn_nq(q, k, v)
         if rc == 0:
             return out
     q3 = _squeeze_q(q)
+    if q3.dtype in (torch.float16, torch.float32):
+        return _decode_all_positions(q3, k, v, q.dtype)
     if q3.dtype != torch.bfloat16:
-        q3 = q3.to(torch.bfloat16)
+        q3 = q3.float()
+        return _decode_all_positions(q3, k, v, torch.float32).to(q.dtype)
     out = torch.empty(q3.shape, dtype=q.dtype, device=q.device)
     _ops.decode_attn(q3, k, v, 1.0, out)
     return out.unsqueeze(2)
 
 
 def decode_attn_fp8(q, k, v):
-    """decode_attn_bf16 over an fp8 e4m3 KV cache. ref: src/attention_kernels.py:156-182."""
-    if q.is_cuda:
+    """decode_attn_bf16 over an fp8 e4m3 KV cache. ref: src/attention_kernels.py:156-182.
+
+    bf16 and f16 queries meet the keys as exact f16 operands on the tensor cores; an fp32
+    query, which that would round, is computed in fp32 over every position by the gather
+    kernel.
+    """
+    if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16):
         rc, out = _ops.N.glue().decode_attn_nq(q, k, v)
         if rc == 0:
             return out
     q3 = _squeeze_q(q)
+    if q3.dtype not in (torch.bfloat16, torch.float16):
+        out = _decode_all_positions(q3.float(), k, v, torch.float32)
+        return out.to(q.dtype)
     out = torch.empty(q3.shape, dtype=q.dtype, device=q.device)
     _ops.decode_attn(q3, k, v, 1.0, out)
     return out.unsqueeze(2)

@@ -141,3 +141,24 @@ def test_attend_topk_fp32(cuda):
     ref = oracle.attend_topk(q, k, v, idx, pos, 0.125)
     assert out.dtype == torch.float32
     assert torch.allclose(out.cpu(), ref, rtol=1e-4, atol=1e-4), (out.cpu() - ref).abs().max()
+
+
+@pytest.mark.parametrize("qd", ["f32", "f16"])
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_dense_decode_unrounded_query(cuda, qd, kv):
+    """decode_attn_bf16 / decode_attn_fp8 with an f16 or fp32 query: the reference widens it
+    to fp32 (src/attention_kernels.py:8-63, 98-150); this engine computes those calls in
+    fp32 over every position (an f16 query over fp8 keys stays on the exact f16 tiles)."""
+    g = gen(140 + len(qd + kv))
+    B, Hq, Hk, S, D = 2, 8, 2, 3000, 128
+    q = (randn(g, B, Hq, 1, D) / math.sqrt(D) * 3.0).to(DT[qd])
+    k = randn(g, B, Hk, S, D, dtype=torch.bfloat16)
+    v = randn(g, B, Hk, S, D, dtype=torch.bfloat16)
+    if kv == "fp8":
+        k, v = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
+    fn = ak.decode_attn_bf16 if kv == "bf16" else ak.decode_attn_fp8
+    out = fn(q.to(cuda), k.to(cuda), v.to(cuda))
+    ref = oracle.decode_attn_dense(q.float(), k, v, 1.0)
+    assert out.dtype == q.dtype and out.shape == (B, Hq, 1, D)
+    tol = 1e-4 if qd == "f32" else 2e-3
+    assert torch.allclose(out.float().cpu(), ref.float(), rtol=tol, atol=tol), (out.float().cpu() - ref.float()).abs().max()

@@ -513,3 +513,19 @@ def test_other_selectors_vs_reference(ref_sa, cuda, selector):
     a, b = valid_sets(ours, pos, S), valid_sets(theirs, pos, S)
     assert sum(ok) > 0.5 * len(ok)
     assert all(x == y or not o for x, y, o in zip(a, b, ok))
+
+
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_dense_decode_fp32_query_vs_reference(ref, cuda, kv):
+    """The reference's dense Triton kernels widen an fp32 query; so does this engine."""
+    g = gen(126)
+    B, Hq, Hk, S, D = 2, 8, 2, 2000, 128
+    q = (torch.randn(B, Hq, 1, D, generator=g) / math.sqrt(D)).to(cuda)
+    k = torch.randn(B, Hk, S, D, generator=g).bfloat16().to(cuda)
+    v = torch.randn(B, Hk, S, D, generator=g).bfloat16().to(cuda)
+    if kv == "fp8":
+        k, v = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
+        ours, theirs = ak.decode_attn_fp8(q, k, v), ref.decode_attn_fp8(q, k, v)
+    else:
+        ours, theirs = ak.decode_attn_bf16(q, k, v), ref.decode_attn_bf16(q, k, v)
+    same(ours, theirs, max_abs=1e-4, mean_abs=1e-5)
