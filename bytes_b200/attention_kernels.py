@@ -163,7 +163,9 @@ def topk(scores, k, sorted=True):
 
 
 def _v_for_pq(v):
-    return v if v.dtype in (torch.bfloat16, torch.float8_e4m3fn, torch.int8) else v.to(torch.bfloat16)
+    """Values as the PQ kernels take them: bf16, f16, fp8 e4m3 or int8 as given; other
+    dtypes (fp32) as bf16, which keeps their range."""
+    return v if v.dtype in (torch.bfloat16, torch.float16, torch.float8_e4m3fn, torch.int8) else v.to(torch.bfloat16)
 
 
 def decode_attn_dequant(q, k_idx, centroids, v, d_sub=8):

@@ -41,7 +41,7 @@ constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kLn2P = 0.6931471805599453f;
 constexpr float kPHeadroom = 4.f;  // log2 headroom of the lazily moved softmax reference
 
-enum VKind { V_BF16 = 0, V_FP8 = 1, V_INT8 = 2, V_PQ = 3, V_NONE = 4 };
+enum VKind { V_BF16 = 0, V_FP8 = 1, V_INT8 = 2, V_PQ = 3, V_NONE = 4, V_F16 = 5 };
 
 struct PqParams {
   const float* lut; int64_t l_sb, l_sh, l_sm, l_sk;
@@ -82,7 +82,7 @@ __host__ __device__ inline PqSmem pq_smem(int vk, int M, int K, int C, int D, in
   s.kout_pitch = C > 0 ? 16 : 0;  // up to 8 x 2-byte outlier channels per token
   s.kout_bytes = kPRows * s.kout_pitch;
   int vrow = 0;
-  if (vk == V_BF16) vrow = D * 2;
+  if (vk == V_BF16 || vk == V_F16) vrow = D * 2;
   else if (vk == V_FP8 || vk == V_INT8) vrow = D;
   else if (vk == V_PQ) vrow = round16(Mv);
   s.v_pitch = vk == V_PQ ? vrow : (vrow ? vrow + 16 : 0);
@@ -260,8 +260,8 @@ __global__ void __launch_bounds__(kPW * 32, 2)
       }
     }
     uint8_t* vst = st + L.off_v;
-    if (VK == V_BF16 || VK == V_FP8 || VK == V_INT8) {
-      constexpr int ELT = VK == V_BF16 ? 2 : 1;
+    if (VK == V_BF16 || VK == V_F16 || VK == V_FP8 || VK == V_INT8) {
+      constexpr int ELT = (VK == V_BF16 || VK == V_F16) ? 2 : 1;
       constexpr int CH = D * ELT / 16;
       for (int c = threadIdx.x; c < kPRows * CH; c += kPW * 32) {
         const int r = c / CH, cc = c % CH;
@@ -495,16 +495,18 @@ __global__ void __launch_bounds__(kPW * 32, 2)
     }
 
     // ---- O^T += V^T . P^T
-    if (VK == V_BF16) {
-      const uint32_t pb0 = movmatrix_trans(pack_bf16x2(pv[0], pv[1]));
-      const uint32_t pb1 = movmatrix_trans(pack_bf16x2(pv[2], pv[3]));
+    if (VK == V_BF16 || VK == V_F16) {
+      // 16-bit values straight from the tile; f16 values meet f16 weights
+      const uint32_t pb0 = movmatrix_trans(VK == V_F16 ? pack_f16x2(pv[0], pv[1]) : pack_bf16x2(pv[0], pv[1]));
+      const uint32_t pb1 = movmatrix_trans(VK == V_F16 ? pack_f16x2(pv[2], pv[3]) : pack_bf16x2(pv[2], pv[3]));
       const uint32_t vs = smem_u32(vst);
       const int vrow = r0 + (lane & 7) + (lane >> 4) * 8;
 #pragma unroll
       for (int mt = 0; mt < KSTEPS; ++mt) {
         uint32_t a0, a1, a2, a3;
         ldmatrix_x4_trans(a0, a1, a2, a3, vs + vrow * L.v_pitch + (mt * 16 + ((lane >> 3) & 1) * 8) * 2);
-        mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
+        if (VK == V_F16) mma_f16(o[mt], a0, a1, a2, a3, pb0, pb1);
+        else mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
       }
     } else if (VK == V_PQ) {
       const uint32_t pb0 = movmatrix_trans(pack_f16x2(pv[0], pv[1]));
@@ -799,6 +801,7 @@ int dispatch_pq(const PqParams& p, int vk, bool paged, bool outl, cudaStream_t s
   if (p.D == 128) {
     switch (vk) {
       case V_BF16: return dispatch_pq2<V_BF16, 128>(p, paged, outl, st);
+      case V_F16: return dispatch_pq2<V_F16, 128>(p, paged, outl, st);
       case V_FP8: return dispatch_pq2<V_FP8, 128>(p, paged, outl, st);
       case V_INT8: return dispatch_pq2<V_INT8, 128>(p, paged, outl, st);
       case V_PQ: return dispatch_pq2<V_PQ, 128>(p, paged, outl, st);
@@ -807,6 +810,7 @@ int dispatch_pq(const PqParams& p, int vk, bool paged, bool outl, cudaStream_t s
   }
   switch (vk) {
     case V_BF16: return dispatch_pq2<V_BF16, 64>(p, paged, outl, st);
+    case V_F16: return dispatch_pq2<V_F16, 64>(p, paged, outl, st);
     case V_FP8: return dispatch_pq2<V_FP8, 64>(p, paged, outl, st);
     case V_INT8: return dispatch_pq2<V_INT8, 64>(p, paged, outl, st);
     case V_PQ: return dispatch_pq2<V_PQ, 64>(p, paged, outl, st);
@@ -857,11 +861,12 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
       if ((rc = check_tensor(v, "v", 4))) return rc;
       D = v->shape[3];
       if (v->dtype == BD_BF16) vk = V_BF16;
+      else if (v->dtype == BD_F16) vk = V_F16;
       else if (v->dtype == BD_F8E4M3) vk = V_FP8;
       else if (v->dtype == BD_I8) {
         vk = V_INT8;
         if (!ws_query && (rc = check_tensor(v_scale, "v_scale", 3, BD_F16))) return rc;
-      } else return fail(BD_ERR_DTYPE, "v must be bf16, fp8 e4m3 or int8 (+ v_scale)");
+      } else return fail(BD_ERR_DTYPE, "v must be bf16, f16, fp8 e4m3 or int8 (+ v_scale)");
       if ((rc = check_rows_aligned(v, "v"))) return rc;
     }
     if (D != 64 && D != 128) return fail(BD_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
@@ -923,7 +928,7 @@ static int pq_common(const bd_tensor* lut, const bd_tensor* codes, const bd_tens
     p.qo_dtype = q_out->dtype;
     p.C = int(k_out->shape[3]);
   }
-  if (vk == V_BF16 || vk == V_FP8 || vk == V_INT8) {
+  if (vk == V_BF16 || vk == V_F16 || vk == V_FP8 || vk == V_INT8) {
     p.v = static_cast<const uint8_t*>(v->data); p.v_sb = v->stride[0]; p.v_sh = v->stride[1]; p.v_ss = v->stride[2];
     if (vk == V_INT8) {
       p.vsc = static_cast<const __half*>(v_scale->data);

@@ -162,3 +162,30 @@ def test_dense_decode_unrounded_query(cuda, qd, kv):
     assert out.dtype == q.dtype and out.shape == (B, Hq, 1, D)
     tol = 1e-4 if qd == "f32" else 2e-3
     assert torch.allclose(out.float().cpu(), ref.float(), rtol=tol, atol=tol), (out.float().cpu() - ref.float()).abs().max()
+
+
+def test_pq_family_f16_values(cuda):
+    """f16 value caches go to the PQ kernels as they are (PV in f16 on the tensor cores),
+    not through a bf16 copy: decode_attn_pq_lut, decode_attn_dequant and the outlier-aware
+    form, against the fp32 oracle within the f16 output's rounding."""
+    g = gen(150)
+    B, Hq, Hk, S, D, K = 2, 8, 2, 900, 128, 256
+    M = D // 8
+    cent = torch.randn(M, K, 8, generator=g)
+    codes = torch.randint(0, K, (B, Hk, S, M), generator=g).to(torch.uint8)
+    lut = oracle.pq_lut(torch.randn(B, Hq, D, generator=g) / math.sqrt(D), cent)
+    v = torch.randn(B, Hk, S, D, generator=g).half()
+    out = ak.decode_attn_pq_lut(lut.to(cuda), codes.to(cuda), v.to(cuda))
+    assert out.dtype == torch.float16
+    ref = oracle.decode_attn_pq_lut(lut, codes, v)
+    assert torch.allclose(out.float().cpu(), ref.float(), rtol=2e-3, atol=2e-3), (out.float().cpu() - ref.float()).abs().max()
+    q = (torch.randn(B, Hq, 1, D, generator=g) / math.sqrt(D)).half()
+    out = ak.decode_attn_dequant(q.to(cuda), codes.to(cuda), cent.to(cuda), v.to(cuda), d_sub=8)
+    ref = oracle.decode_attn_dequant(q, codes, cent, v, 8)
+    assert torch.allclose(out.float().cpu(), ref.float(), rtol=2e-3, atol=2e-3), (out.float().cpu() - ref.float()).abs().max()
+    k_out = torch.randn(B, Hk, S, 2, generator=g).bfloat16() * 20
+    q_out = torch.randn(B, Hq, 2, generator=g).bfloat16()
+    out = ak.decode_attn_pq_lut_asym(lut.to(cuda), codes.to(cuda), k_out.to(cuda), q_out.to(cuda), v.to(cuda))
+    assert out.dtype == torch.float16
+    ref = oracle.decode_attn_pq_lut_asym(lut, codes, k_out, q_out, v)
+    assert torch.allclose(out.float().cpu(), ref.float(), rtol=2e-3, atol=2e-3), (out.float().cpu() - ref.float()).abs().max()

@@ -529,3 +529,13 @@ def test_dense_decode_fp32_query_vs_reference(ref, cuda, kv):
     else:
         ours, theirs = ak.decode_attn_bf16(q, k, v), ref.decode_attn_bf16(q, k, v)
     same(ours, theirs, max_abs=1e-4, mean_abs=1e-5)
+
+
+def test_pq_lut_f16_values_vs_reference(ref, cuda):
+    """decode_attn_pq_lut over an f16 value cache (the reference widens it to fp32)."""
+    g = gen(127)
+    B, Hq, Hk, S, D, K = 2, 8, 2, 1500, 128, 256
+    _, codes, lut = _pq(g, B, Hq, Hk, S, D, K)
+    v = torch.randn(B, Hk, S, D, generator=g).half()
+    lut, codes, v = to(cuda, lut, codes, v)
+    same(ak.decode_attn_pq_lut(lut, codes, v), ref.decode_attn_pq_lut(lut, codes, v), max_abs=2e-3, mean_abs=1e-4)
