@@ -35,14 +35,22 @@ def decode_attn_bf16(q, k, v):
 
     ref: src/attention_kernels.py:65-92. q [B,H_q,1,D]; k,v [B,H_k,S,D] bf16
     -> [B,H_q,1,D] in q.dtype. A bf16 query takes the tensor-core decode tiles (every
-    product exact in fp32); an f16 or fp32 query, which they would round, is computed in
-    fp32 over every position by the gather kernel, as the reference widens it.
+    product exact in fp32); an f16 or fp32 query, which they would round, and an f16 or
+    fp32 cache are computed in fp32 over every position by the gather kernel, as the
+    reference widens them.
     """
-    if q.is_cuda and q.dtype == torch.bfloat16:
+    if q.is_cuda and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16:
         rc, out = _ops.N.glue().decode_attn_nq(q, k, v)
         if rc == 0:
             return out
     q3 = _squeeze_q(q)
+    if k.dtype in (torch.float16, torch.float32) and v.dtype == k.dtype:
+        # an f16 / fp32 cache (off the function's name, as the reference allows): fp32
+        # attention over every position by the gather kernel
+        if q3.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            q3 = q3.float()
+        out_dt = q.dtype if q.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32
+        return _decode_all_positions(q3, k, v, out_dt).to(q.dtype)
     if q3.dtype in (torch.float16, torch.float32):
         return _decode_all_positions(q3, k, v, q.dtype)
     if q3.dtype != torch.bfloat16:

@@ -189,3 +189,17 @@ def test_pq_family_f16_values(cuda):
     assert out.dtype == torch.float16
     ref = oracle.decode_attn_pq_lut_asym(lut, codes, k_out, q_out, v)
     assert torch.allclose(out.float().cpu(), ref.float(), rtol=2e-3, atol=2e-3), (out.float().cpu() - ref.float()).abs().max()
+
+
+@pytest.mark.parametrize("kvd", ["f16", "f32"])
+def test_dense_decode_f16_f32_cache(cuda, kvd):
+    """decode_attn_bf16 over an f16 / fp32 cache (the reference's kernel widens any dtype)."""
+    g = gen(160)
+    B, Hq, Hk, S, D = 2, 8, 2, 1500, 64
+    q = (randn(g, B, Hq, 1, D) / math.sqrt(D)).bfloat16()
+    k = randn(g, B, Hk, S, D, dtype=DT[kvd])
+    v = randn(g, B, Hk, S, D, dtype=DT[kvd])
+    out = ak.decode_attn_bf16(q.to(cuda), k.to(cuda), v.to(cuda))
+    ref = oracle.decode_attn_dense(q, k, v, 1.0)
+    assert out.dtype == torch.bfloat16
+    assert torch.allclose(out.float().cpu(), ref.float(), rtol=8e-3, atol=8e-3), (out.float().cpu() - ref.float()).abs().max()
