@@ -539,3 +539,34 @@ def test_pq_lut_f16_values_vs_reference(ref, cuda):
     v = torch.randn(B, Hk, S, D, generator=g).half()
     lut, codes, v = to(cuda, lut, codes, v)
     same(ak.decode_attn_pq_lut(lut, codes, v), ref.decode_attn_pq_lut(lut, codes, v), max_abs=2e-3, mean_abs=1e-4)
+
+
+def _nan_same(ours, theirs):
+    """Equal NaN pattern, and the finite entries within the attention tolerance."""
+    assert ours.shape == theirs.shape and ours.dtype == theirs.dtype
+    a, b = ours.float().cpu(), theirs.float().cpu()
+    assert torch.equal(torch.isnan(a), torch.isnan(b))
+    fin = ~torch.isnan(a)
+    if fin.any():
+        assert (a[fin] - b[fin]).abs().max().item() <= 4e-3
+
+
+def test_empty_contexts_vs_reference(ref, cuda):
+    """Empty inputs the reference's kernels accept: a paged sequence of length 0 and a gather
+    with no positions give 0/0 = NaN rows there; the same rows here."""
+    g = gen(128)
+    B, Hq, Hk, D, bs = 2, 8, 2, 64, 16
+    lens = torch.tensor([0, 45], dtype=torch.int32)
+    _, codes, lut = _pq(g, B, Hq, Hk, 45, D, 16)
+    vcent = torch.randn(D // 8, 16, 8, generator=g)
+    vidx = torch.randint(0, 16, (B, Hk, 45, D // 8), generator=g).to(torch.uint8)
+    kp, table = _paged(codes, torch.tensor([16, 45]), bs, 3)  # sequence 0 keeps one page it never reads
+    vp, _ = _paged(vidx, torch.tensor([16, 45]), bs, 3)
+    lut, kp, vp, vcent, table, lens = to(cuda, lut, kp, vp, vcent, table, lens)
+    _nan_same(ak.paged_attn_pq_lut_kv(lut, kp, vp, vcent, table, lens, block_size=bs),
+              ref.paged_attn_pq_lut_kv(lut, kp, vp, vcent, table, lens, block_size=bs))
+    q = torch.randn(B, Hq, 1, D, generator=g).bfloat16().to(cuda)
+    k = torch.randn(B, Hk, 100, D, generator=g).bfloat16().to(cuda)
+    v = torch.randn(B, Hk, 100, D, generator=g).bfloat16().to(cuda)
+    idx = torch.zeros(B, Hq, 0, dtype=torch.int64, device=cuda)
+    _nan_same(ak.sparse_gather_attn(q, k, v, idx, 0.1), ref.sparse_gather_attn(q, k, v, idx, 0.1))
