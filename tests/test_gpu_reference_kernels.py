@@ -570,3 +570,41 @@ def test_empty_contexts_vs_reference(ref, cuda):
     v = torch.randn(B, Hk, 100, D, generator=g).bfloat16().to(cuda)
     idx = torch.zeros(B, Hq, 0, dtype=torch.int64, device=cuda)
     _nan_same(ak.sparse_gather_attn(q, k, v, idx, 0.1), ref.sparse_gather_attn(q, k, v, idx, 0.1))
+
+
+@pytest.mark.parametrize("gs", [16, 64, 128])
+@pytest.mark.parametrize("bits", [4, 2])
+def test_other_group_sizes_vs_reference(ref, cuda, gs, bits):
+    """Score-key groups of 16, 64 and 128 channels: the packer bit-exact, the packed scores
+    within 1e-4."""
+    g = gen(129 + gs + bits)
+    B, Hq, Hk, S, D = 2, 8, 2, 1200, 128
+    q = torch.randn(B, Hq, 1, D, generator=g).bfloat16().to(cuda)
+    k = (torch.randn(B, Hk, S, D, generator=g) * 2).bfloat16().to(cuda)
+    ours = ak.quantize_and_pack_score_keys(k, bits, gs)
+    theirs = ref.quantize_and_pack_score_keys(k, bits, gs)
+    for a, b in zip(ours, theirs):
+        assert a.dtype == b.dtype and a.shape == b.shape and torch.equal(a, b)
+    kp, s_, z_ = theirs
+    same_scores(ak.sparse_score_packed(q, kp, s_, z_, 0.1, score_bits=bits, group_size=gs),
+                ref.sparse_score_packed(q, kp, s_, z_, 0.1, score_bits=bits, group_size=gs))
+
+
+@pytest.mark.parametrize("d_sub", [4, 16])
+def test_other_subvector_lengths_vs_reference(ref, cuda, d_sub):
+    """PQ with sub-vectors of 4 and 16 channels: decode_attn_dequant and the PQ value path."""
+    g = gen(130 + d_sub)
+    B, Hq, Hk, S, D = 2, 8, 2, 600, 128
+    M = D // d_sub
+    cent = torch.randn(M, 16, d_sub, generator=g)
+    codes = torch.randint(0, 16, (B, Hk, S, M), generator=g).to(torch.uint8)
+    q = (torch.randn(B, Hq, 1, D, generator=g) / math.sqrt(D)).bfloat16()
+    v = torch.randn(B, Hk, S, D, generator=g).bfloat16()
+    qd, cd, ced, vd = to(cuda, q, codes, cent, v)
+    same(ak.decode_attn_dequant(qd, cd, ced, vd, d_sub=d_sub), ref.decode_attn_dequant(qd, cd, ced, vd, d_sub=d_sub))
+    q_rot = torch.randn(B, Hq, D, generator=g) / math.sqrt(D)
+    lut = torch.einsum("bhmd,mkd->bhmk", q_rot.view(B, Hq, M, d_sub), cent).contiguous().to(cuda)
+    vcent = torch.randn(M, 16, d_sub, generator=g).to(cuda)
+    vidx = torch.randint(0, 16, (B, Hk, S, M), generator=g).to(torch.uint8).to(cuda)
+    same(ak.decode_attn_pq_lut_kv(lut, cd, vidx, vcent, d_sub_v=d_sub),
+         ref.decode_attn_pq_lut_kv(lut, cd, vidx, vcent, d_sub_v=d_sub))
